@@ -1,0 +1,349 @@
+"""Recurrent tokens/sec of the fused leapfrog recurrence on B200.
+
+Default workload (N=1): the long-horizon configuration -- parity bit tokens,
+d=256, 6 layers, 8 heads, rank 32 (per-head 4), leapfrog dt=0.1, batch 64
+per GPU, the 100,000-token stream processed in chunks with the O(1) (x, v)
+state carried between chunks.  One step = one chunk of --chunk tokens for
+all 64 rows through all 6 layers (one kernel launch).  Weights are seeded
+random (U, W ~ N(0, 0.2^2) etc.); data is synthetic.
+
+Multi-GPU (torchrun): every rank runs its own 64 independent streams (weak
+scaling by batch sharding, no collective on the path); time is the max over
+ranks of the device time.
+
+--impl reference times the CPU baseline: the numpy restatement of the
+reference's algorithm (oracle/), all host threads, on the same config.
+"""
+import argparse
+import json
+import os
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+CONFIGS = {
+    # name: model shape, per-rank batch, default chunk (tokens per step)
+    "c2": dict(V=2, d=256, NL=6, H=8, rank=32, B=64, dt=0.1, chunk=2000, parity=True,
+               workload="C2 long-horizon recurrence fp32: d=256, 6 layers, 8 heads, rank 32, "
+                        "leapfrog, batch 64, 100k-token stream in chunks"),
+    "c4": dict(V=32000, d=1024, NL=24, H=16, rank=64, B=4096, dt=0.1, chunk=1, parity=False,
+               workload="C4 batched decode fp32: 4096 streams, d=1024, 24 layers, 16 heads, "
+                        "rank 64, one token per step"),
+    "c3": dict(V=50257, d=512, NL=12, H=8, rank=32, B=256, dt=0.1, chunk=64, functional=True,
+               workload="C3 LM prefill: bf16 functional-embedding forces, fp32 state, d=512, "
+                        "12 layers, 8 heads, batch 256"),
+    "c1": dict(V=2, d=128, NL=4, H=4, rank=16, B=32, dt=0.1, chunk=20, parity=True,
+               workload="C1 cumulative parity fp32: d=128, 4 layers, 4 heads, batch 32, L=20"),
+}
+
+
+def flops_per_token(c):
+    d, H = c["d"], c["H"]
+    hd = d // H
+    r = max(4, c["rank"] // H)
+    # mixing 2 GEMVs (2*d*d MAC) + 2 friction GEMVs per head (2*hd*hd MAC per head)
+    # + 2 Gamma evaluations (2 * 2*hd*r MAC per head) + ~30 elementwise flops per element
+    mac = 2 * d * d + H * (2 * hd * hd + 4 * hd * r)
+    return c["NL"] * (2 * mac + 30 * d)
+
+
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms."""
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={q}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        rows = []
+        for line in open(self.path):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rows.append(dict(sm=float(parts[1]), max=float(parts[2]), hw=parts[5], hwt=parts[6],
+                                 swt=parts[7], pcap=parts[8]))
+            except ValueError:
+                continue
+        os.unlink(self.path)
+        if not rows:
+            return None
+        reasons = set()
+        for r in rows:
+            for k, name in (("hw", "hw_slowdown"), ("hwt", "hw_thermal_slowdown"),
+                            ("swt", "sw_thermal_slowdown"), ("pcap", "sw_power_cap")):
+                if r[k].lower().startswith("active"):
+                    reasons.add(name)
+        return dict(sm_mhz=float(np.median([r["sm"] for r in rows])), sm_max_mhz=rows[0]["max"],
+                    samples=len(rows), reasons=sorted(reasons))
+
+
+def measured_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return d["hbm_gbs"], d["bf16_tflops"], "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+def make_model(c, device):
+    import torch
+    import manifold_b200 as gfn
+    from tests.golden import cases as C
+    cfg = dict(c, seed=1234)
+    P = C.make_params(cfg)
+    torch.manual_seed(0)
+    m = gfn.Manifold(**C.model_kwargs(cfg)).to(device).eval()
+    C.load_into_model(m, cfg, P)
+    for p in m.parameters():
+        p.requires_grad_(False)
+    return m, P
+
+
+def make_ids(c, B, T, seed):
+    from tests.golden import cases as C
+    rng = np.random.default_rng(seed)
+    if c.get("parity"):
+        return rng.integers(0, 2, (B, T)).astype(np.int64)
+    if c.get("functional"):
+        return C.zipf_ids(rng, c["V"], (B, T))
+    return rng.integers(0, c["V"], (B, T)).astype(np.int64)
+
+
+def run_ours(args, c):
+    import torch
+    import torch.distributed as dist
+    world, rank, local = dist_env()
+    if world > 1:
+        dist.init_process_group("nccl")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    from manifold_b200.cuda import ops
+    m, P = make_model(c, dev)
+    B, T = c["B"], args.chunk or c["chunk"]
+    steps, warm = args.steps, args.warmup
+    ids_host = [torch.from_numpy(make_ids(c, B, T, 100 * rank + i)).pin_memory()
+                for i in range(steps + warm)]
+    ids_dev = [t.to(dev) for t in ids_host]
+    flush = torch.empty(256 * 1024 * 1024 // 4, device=dev, dtype=torch.float32)
+    stream = torch.cuda.current_stream(dev)
+    packed, meta = m._pack.get(list(m.layers))
+    if c.get("functional"):
+        m.force_dtype = torch.bfloat16
+
+    x = m.x0.detach().expand(B, -1).contiguous()
+    v = m.v0.detach().expand(B, -1).contiguous()
+    want_v = True
+
+    def step(i, state):
+        with torch.no_grad():
+            if c.get("functional"):
+                forces = m.embedding(ids_dev[i], out_dtype=torch.bfloat16)
+                xs, vs, xf, vf = ops.leapfrog_sequence(state[0], state[1], packed, meta, c["dt"],
+                                                       forces=forces, want_v_seq=want_v)
+            else:
+                xs, vs, xf, vf = ops.leapfrog_sequence(state[0], state[1], packed, meta, c["dt"],
+                                                       ids=ids_dev[i], table=m.embedding.weight,
+                                                       want_v_seq=want_v)
+        return (xf, vf)
+
+    state = (x, v)
+    for i in range(warm):
+        state = step(i, state)
+    torch.cuda.synchronize(dev)
+    # kernel-level event timing of the sequence kernel: per step, L2 flushed between
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    sampler = ClockSampler(local) if rank == 0 else None
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    if sampler:
+        sampler.start()
+        time.sleep(0.3)
+    wall0 = time.perf_counter()
+    for i in range(steps):
+        flush.zero_()
+        ev[i][0].record(stream)
+        state = step(warm + i, state)
+        ev[i][1].record(stream)
+    torch.cuda.synchronize(dev)
+    wall = time.perf_counter() - wall0
+    ms = sum(a.elapsed_time(b) for a, b in ev)
+    # end to end through the public API: pinned host ids -> device, recurrence,
+    # final state read back to the host, every step
+    hx = torch.empty(B, c["d"], dtype=torch.float32).pin_memory()
+    hv = torch.empty_like(hx)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    st = (x, v)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    e0.record(stream)
+    for i in range(steps):
+        with torch.no_grad():
+            idd = ids_host[warm + i].to(dev, non_blocking=True)
+            _, _, st, _ = m.recurrence(idd, state=st)
+        hx.copy_(st[0], non_blocking=True)
+        hv.copy_(st[1], non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    e2e_ms = e0.elapsed_time(e1)
+    clocks = sampler.stop() if sampler else None
+    if world > 1:
+        t = torch.tensor([ms, e2e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, e2e_ms = t.tolist()
+    tokens = world * B * T * steps
+    value = tokens / (ms / 1e3)
+    e2e_value = tokens / (e2e_ms / 1e3)
+    result = None
+    if rank == 0:
+        hbm, bf16, peak_kind = measured_peaks()
+        step_ms = ms / steps
+        # algorithmic HBM bytes per launch: ids (8 B) + x_seq, v_seq writes (8 d B) per
+        # token-row, the packed weights once, the state in/out
+        per_tok = (2 if c.get("functional") else 8) * (c["d"] if c.get("functional") else 1) \
+            + 4 * c["d"] * (2 if want_v else 1)
+        alg = B * T * per_tok + packed.numel() * 4 + 4 * 4 * B * c["d"]
+        achieved = alg / (step_ms / 1e3) / 1e9
+        fl = flops_per_token(c) * B * T / (step_ms / 1e3) / 1e12
+        plan = ops.leapfrog_plan(B, c["d"], c["H"], max(4, c["rank"] // c["H"]), c["NL"])
+        result = {
+            "metric": "recurrent tokens/sec (prefill+decode)",
+            "value": round(value, 1),
+            "unit": "tokens/s",
+            "n_gpus": world,
+            "steps": steps,
+            "warmup": warm,
+            "ms_per_step": round(ms / steps, 4),
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "f32",
+            "data": "synthetic (seeded parity bits / ids; seeded random weights)",
+            "config": {"workload": c["workload"], "batch_per_gpu": B, "tokens_per_step": T,
+                       "dim": c["d"], "layers": c["NL"], "heads": c["H"],
+                       "rank": c["rank"], "l2": "flushed (256 MB write) between timed steps",
+                       "plan": plan},
+            "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s",
+                    "h2d_bytes_per_step": int(B * T * 8), "d2h_bytes_per_step": int(2 * B * c["d"] * 4)},
+            "gpu_launches": steps * (2 if c.get("functional") else 1),
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": hbm, "unit": "GB/s",
+                         "frac": round(achieved / hbm, 5), "traffic": None,
+                         "peak_source": peak_kind,
+                         "note": "latency-bound dependent chain; fp32 SIMT FLOP rate in fp32_tflops",
+                         "fp32_tflops": round(fl, 3)},
+            "clocks": clocks,
+            "wall_s_timed": round(wall, 3),
+        }
+        if not args.no_cpu_baseline and world == 1:
+            result["cpu_baseline"] = cpu_baseline(c, args.cpu_tokens)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return result
+
+
+def cpu_baseline(c, tokens):
+    """The numpy port of the reference algorithm (oracle/) on the host cores,
+    on a bounded sample of the same workload."""
+    from oracle import gfn_oracle as O
+    from tests.golden import cases as C
+    cfg = dict(c, seed=1234)
+    P = C.make_params(cfg)
+    B = c["B"]
+    T = tokens or max(1, min(c.get("chunk", 1), 200))
+    Bs = B if B <= 256 else 256
+    ids = make_ids(c, Bs, T, 7)
+    F = O.functional_embedding(ids, P["func"]) if c.get("functional") else P["emb"][ids]
+    x0 = np.broadcast_to(P["x0"], (Bs, c["d"])).copy()
+    v0 = np.broadcast_to(P["v0"], (Bs, c["d"])).copy()
+    t0 = time.perf_counter()
+    O.manifold_forward(x0, v0, F, P["layers"], c["H"], c["dt"])
+    dt = time.perf_counter() - t0
+    return {"value": round(Bs * T / dt, 1), "unit": "tokens/s", "cores": os.cpu_count(),
+            "kind": "port", "sample": f"{Bs} rows x {T} tokens through all {c['NL']} layers "
+                                      f"(numpy float32, BLAS threads = host cores)"}
+
+
+def run_reference(args, c):
+    world, rank, _ = dist_env()
+    if rank != 0:
+        return None
+    T = args.cpu_tokens or max(1, min(c.get("chunk", 1), 100))
+    vals = []
+    for _ in range(args.warmup):
+        cpu_baseline(c, T)
+    for _ in range(args.steps):
+        vals.append(cpu_baseline(c, T)["value"])
+    v = float(np.mean(vals))
+    B = c["B"] if c["B"] <= 256 else 256
+    cb = {"value": round(v, 1), "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
+          "sample": f"{B} rows x {T} tokens per step, all {c['NL']} layers, numpy float32"}
+    return {"metric": "recurrent tokens/sec (prefill+decode)", "value": round(v, 1),
+            "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(B * T / v * 1e3, 3), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic", "impl": "reference",
+            "config": {"workload": c["workload"], "batch_per_gpu": c["B"]},
+            "cpu_baseline": cb,
+            "e2e": {"value": round(v, 1), "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--config", default="c2", choices=sorted(CONFIGS))
+    ap.add_argument("--chunk", type=int, default=0, help="tokens per step (default per config)")
+    ap.add_argument("--cpu-tokens", type=int, default=0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    c = CONFIGS[args.config]
+    if args.impl == "reference":
+        out = run_reference(args, c)
+    else:
+        out = run_ours(args, c)
+    if out is not None:
+        print(json.dumps(out), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,166 @@
+/*
+ * gfn_b200 -- C ABI of the B200 (sm_100a) kernels for the recurrent
+ * geodesic-flow hot path of Manifold-Laboratory/manifold (package `gfn`).
+ *
+ * Conventions
+ *  - Plain device pointers, contiguous row-major float32 unless stated.
+ *    The caller owns and allocates every buffer; no entry point allocates
+ *    device memory.  Optional inputs are NULL.
+ *  - Every entry point is asynchronous on `stream` and returns a status
+ *    (GFN_OK == 0).  Arguments are validated before anything is launched;
+ *    gfn_last_error_message() describes the last failure of this thread.
+ *  - Device-side faults are never raised with a trap: kernels record them in
+ *    a device error word (gfn_get_device_error) and finish their launch.
+ *  - `rank` is the per-head Christoffel rank (U.size(-1)), as in the
+ *    reference's launchers; `heads * head_dim == dim`.
+ *
+ * Each function names the reference entry point it replaces
+ * (gfn/cuda/cuda_kernels.cpp is the reference's pybind/C boundary).
+ */
+#ifndef GFN_B200_H
+#define GFN_B200_H
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* gfn_stream_t; /* == cudaStream_t */
+
+enum {
+  GFN_OK = 0,
+  GFN_ERR_INVALID = 1,     /* bad size / null pointer */
+  GFN_ERR_UNSUPPORTED = 2, /* a configuration this build does not implement */
+  GFN_ERR_ALIGN = 3,       /* pointer not 16-byte aligned where required */
+  GFN_ERR_CUDA = 4,        /* a CUDA runtime call or launch failed */
+  GFN_ERR_RESOURCES = 5,   /* no launch plan fits the device (shared memory) */
+};
+
+/* Device error bits recorded by kernels. */
+enum {
+  GFN_DEVERR_MBAR_TIMEOUT = 1, /* a bounded wait for a bulk copy gave up */
+  GFN_DEVERR_BAD_TOKEN = 2,    /* a token id outside [0, vocab) (force 0 used) */
+};
+
+const char* gfn_status_string(int status);
+const char* gfn_last_error_message(void);
+const char* gfn_build_info(void);
+
+/* Synchronises `stream`, stores the device error bits in *bits and, when
+ * reset != 0, clears them. */
+int gfn_get_device_error(int* bits, int reset, gfn_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Christoffel contraction Gamma(v) = 20 tanh(((vU)^2 s) W^T / 20),
+ * s = 1/(1 + |vU| + 1e-6), for one head.
+ * Replaces launch_christoffel_fused (gfn/cuda/cuda_kernels.cpp:14-19) for the
+ * configuration the leapfrog path uses: x/V_w NULL, plasticity 0,
+ * topology 0 (anything else returns GFN_ERR_UNSUPPORTED).
+ * Semantics: gfn/geometry/lowrank.py:93-98,125-127.
+ * v [batch, dim], U, W [dim, rank], gamma [batch, dim].
+ */
+int gfn_christoffel_fused(const float* v, const float* U, const float* W, float* gamma,
+                          const float* x, const float* V_w, int batch, int dim, int rank,
+                          float plasticity, float sing_thresh, float sing_strength, int topology,
+                          float R_val, float r_val, gfn_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * One head's leapfrog (kick-drift-kick with implicit friction), `steps`
+ * times.  Replaces launch_leapfrog_fused (gfn/cuda/cuda_kernels.cpp:74-83).
+ * Semantics: gfn/integrators/symplectic/leapfrog.py:50-114.
+ * x, v, f [batch, dim] (f may be NULL: zero force); U, W [dim, rank];
+ * W_forget [dim, dim] + b_forget [dim] (NULL: no friction);
+ * dt_scales: NULL (1.0), 1 value, or `batch` values (dt_scales_count).
+ */
+int gfn_leapfrog_fused(const float* x, const float* v, const float* f, const float* U,
+                       const float* W, const float* W_forget, const float* b_forget, float* x_new,
+                       float* v_new, float dt, const float* dt_scales, int dt_scales_count,
+                       int batch, int dim, int rank, int steps, int topology, float plasticity,
+                       float R_val, float r_val, gfn_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Whole-sequence fused leapfrog recurrence (all tokens x layers x heads in
+ * one persistent launch).  The reference has no leapfrog entry here: its
+ * launch_recurrent_manifold_fused (gfn/cuda/cuda_kernels.cpp:41-52) is
+ * excluded for leapfrog at gfn/model.py:207 and the per-token Python loop
+ * (gfn/model.py:377-402 over gfn/layers/base.py:198-338) runs instead; this
+ * entry computes exactly that loop.
+ *
+ * Weights go through gfn_leapfrog_pack first (once per weight update).
+ *
+ * x_init, v_init: initial state, row r at x_init + r*state_row_stride
+ *   (stride 0 broadcasts one [dim] row, as the model's x0/v0 parameters).
+ * Forces, exactly one of:
+ *   forces_f32 [batch, seq_len, dim] float32,
+ *   forces_bf16 [batch, seq_len, dim] bfloat16 (raw uint16 storage),
+ *   token_ids [batch, seq_len] int64 + embed_table [vocab, dim] (fused
+ *   nn.Embedding gather, gfn/model.py:55,163).
+ * mask [batch, seq_len] or NULL (force_t *= mask_t, gfn/model.py:381).
+ * Outputs (any may be NULL): x_seq, v_seq [batch, seq_len, dim] = state
+ * after the last layer at every token; x_final, v_final [batch, dim].
+ * base_dt: the layers' base_dt; heads == 1 means no head mixing.
+ */
+int gfn_leapfrog_sequence_forward(const float* x_init, const float* v_init,
+                                  long long state_row_stride, const float* forces_f32,
+                                  const void* forces_bf16, const long long* token_ids,
+                                  const float* embed_table, long long vocab, const float* mask,
+                                  const float* packed, long long packed_floats, int batch,
+                                  int seq_len, int dim, int heads, int rank, int num_layers,
+                                  float base_dt, float* x_seq, float* v_seq, float* x_final,
+                                  float* v_final, gfn_stream_t stream);
+
+/* Number of floats of the packed weight buffer for these shapes. */
+long long gfn_leapfrog_pack_floats(int dim, int heads, int rank, int num_layers);
+
+/* Pack the stacked layer parameters (the stacks the reference builds for
+ * launch_recurrent_manifold_fused, gfn/model.py:222-293, plus the mixing
+ * parameters of every layer) into `packed`:
+ *   U_stack, W_stack [num_layers*heads, head_dim, rank]
+ *   W_forget_stack [num_layers*heads, head_dim, head_dim], b_forget_stack [num_layers*heads, head_dim]
+ *   dt_params [num_layers*heads]           (raw; softplus is applied in-kernel)
+ *   mix_x_w/mix_v_w [num_layers, dim, dim] out_proj weights ([out, in]),
+ *   mix_x_b/mix_v_b [num_layers, dim] biases, norm_x_w/norm_v_w [num_layers, dim]
+ *   RMSNorm weights (all six NULL when heads == 1). */
+int gfn_leapfrog_pack(const float* U_stack, const float* W_stack, const float* W_forget_stack,
+                      const float* b_forget_stack, const float* dt_params, const float* mix_x_w,
+                      const float* mix_x_b, const float* norm_x_w, const float* mix_v_w,
+                      const float* mix_v_b, const float* norm_v_w, int dim, int heads, int rank,
+                      int num_layers, float* packed, long long packed_floats, gfn_stream_t stream);
+
+/* Launch plan the sequence kernel would use for `batch` rows:
+ * out[0..5] = cluster size K, rows per cluster, clusters, shared bytes,
+ * k-chunk, ring slots. */
+int gfn_leapfrog_plan(int batch, int dim, int heads, int rank, int num_layers, int* out6);
+
+/* ------------------------------------------------------------------------
+ * y_t = a_t y_{t-1} + x_t along t of [batch, seq_len, dim] (a NULL: a == 1).
+ * Replaces parallel_scan_fused (gfn/cuda/src/layers/parallel_scan_fused.cu:81,
+ * called from gfn/scan.py:20); semantics gfn/scan.py:11-104.
+ * dim % 4 == 0, 16-byte aligned pointers.  `workspace` (may be NULL) of
+ * gfn_parallel_scan_workspace_floats() floats lets short-batch, long
+ * sequences split the time axis; without it one pass is used.
+ */
+long long gfn_parallel_scan_workspace_floats(int batch, int seq_len, int dim);
+int gfn_parallel_scan(const float* a, const float* x, float* y, float* workspace,
+                      long long workspace_floats, int batch, int seq_len, int dim,
+                      gfn_stream_t stream);
+
+/* ParallelMLayer recurrence (gfn/layers/parallel.py:101-121) from the
+ * pre-activations z = [to_A(f) | to_dt(f) | to_B(f)] of shape
+ * [batch, seq_len, 3*dim]: v_seq, x_seq [batch, seq_len, dim]. */
+int gfn_parallel_layer_scan(const float* z, float* x_seq, float* v_seq, int batch, int seq_len,
+                            int dim, int heads, float base_dt, gfn_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * FunctionalEmbedding, mode 'binary', coord_dim 16, hidden 64, 2 hidden
+ * SIREN layers (gfn/embeddings.py:121-206): ids [n] -> forces [n, dim],
+ * float32 (out_f32) or bfloat16 (out_bf16, raw uint16 storage).
+ * impulse: device pointer to the scalar impulse_scale. */
+int gfn_functional_embedding(const long long* ids, long long n, const float* W0, const float* b0,
+                             const float* W1, const float* b1, const float* W2, const float* b2,
+                             const float* Wo, const float* bo, const float* impulse, float omega0,
+                             int dim, float* out_f32, void* out_bf16, gfn_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* GFN_B200_H */

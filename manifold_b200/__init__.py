@@ -1,0 +1,25 @@
+"""manifold_b200: the recurrent geodesic-flow (leapfrog) hot path of the
+reference package ``gfn`` (Manifold-Laboratory/manifold), re-built for
+NVIDIA B200 (sm_100a).  ``import manifold_b200 as gfn`` exposes the
+reference's model / layer / integrator / geometry / scan API for that path.
+"""
+__version__ = "0.1.0"
+
+from . import _lib
+from ._lib import GfnError
+from .model import Manifold, ImplicitReadout
+from .model import Manifold as GFN
+from .layers import MLayer, ParallelMLayer, RiemannianGating
+from .layers import MLayer as GLayer
+from .geometry import LowRankChristoffel, ReactiveChristoffel
+from .integrators import LeapfrogIntegrator
+from .embeddings import FunctionalEmbedding, ImplicitEmbedding, SineLayer
+from .scan import parallel_scan
+from . import cuda
+
+INTEGRATORS = {"leapfrog": LeapfrogIntegrator}
+
+__all__ = ["GFN", "Manifold", "GLayer", "MLayer", "ParallelMLayer", "RiemannianGating",
+           "LowRankChristoffel", "ReactiveChristoffel", "LeapfrogIntegrator",
+           "FunctionalEmbedding", "ImplicitEmbedding", "SineLayer", "ImplicitReadout",
+           "parallel_scan", "GfnError", "INTEGRATORS"]

@@ -1,0 +1,453 @@
+// gfn_b200: the C ABI (include/gfn_b200.h) over the sm_100a kernels.
+// One translation unit: every kernel header is included here.
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+
+#include "../../include/gfn_b200.h"
+#include "embed.cuh"
+#include "leapfrog_seq.cuh"
+#include "ops_small.cuh"
+#include "pack.cuh"
+#include "scan.cuh"
+
+using namespace gfn;
+
+namespace {
+
+thread_local char g_msg[512] = "";
+
+int fail(int status, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_msg, sizeof(g_msg), fmt, ap);
+  va_end(ap);
+  return status;
+}
+
+int cuda_status(cudaError_t e, const char* what) {
+  if (e == cudaSuccess) return GFN_OK;
+  return fail(GFN_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+int launch_status(const char* what) { return cuda_status(cudaGetLastError(), what); }
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+struct DevInfo {
+  int sms = 0;
+  int max_smem = 0;
+};
+
+int dev_info(DevInfo* out) {
+  int dev;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_status(e, "cudaGetDevice");
+  static thread_local int cached_dev = -1;
+  static thread_local DevInfo cached;
+  if (dev != cached_dev) {
+    e = cudaDeviceGetAttribute(&cached.sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return cuda_status(e, "cudaDeviceGetAttribute");
+    e = cudaDeviceGetAttribute(&cached.max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    if (e != cudaSuccess) return cuda_status(e, "cudaDeviceGetAttribute");
+    cached_dev = dev;
+  }
+  *out = cached;
+  return GFN_OK;
+}
+
+// ------------------------------------------------------------------ plans
+// The weight layout (K, KC) depends only on (d, H, r); the row blocking R
+// also on the batch and the device.
+struct Layout {
+  int d, H, hd, r, NL, K, C, hpc, KC, nchunk, HS, CF, mix;
+  long long LF;
+};
+
+int make_layout(int d, int H, int r, int NL, Layout* L) {
+  if (d <= 0 || H <= 0 || r <= 0 || NL <= 0 || d % H != 0)
+    return fail(GFN_ERR_INVALID, "bad shape dim=%d heads=%d rank=%d layers=%d", d, H, r, NL);
+  const int hd = d / H;
+  if (hd % 4 != 0) return fail(GFN_ERR_UNSUPPORTED, "head_dim %d must be a multiple of 4", hd);
+  if (r != 4 && r != 8 && r != 16)
+    return fail(GFN_ERR_UNSUPPORTED, "per-head rank %d not in {4, 8, 16}", r);
+  int K = 1;
+  while (K * 2 <= 8 && H % (K * 2) == 0) K *= 2;
+  if (d >= 1024 && H % 16 == 0) K = 16;
+  L->d = d; L->H = H; L->hd = hd; L->r = r; L->NL = NL;
+  L->K = K; L->C = d / K; L->hpc = H / K;
+  L->mix = H > 1;
+  int KC = 2048 / L->C;
+  if (KC < 4) KC = 4;
+  if (KC > d) KC = d;
+  while (d % KC) --KC;
+  L->KC = KC;
+  L->nchunk = L->mix ? d / KC : 0;
+  L->CF = KC * 2 * L->C;
+  L->HS = head_offsets(L->hpc, hd, r, L->C).total;
+  L->LF = (long long)L->HS + (long long)L->nchunk * L->CF;
+  return GFN_OK;
+}
+
+struct SeqPlan {
+  Layout L;
+  int R, TR, NG, tiles, S, NST, nclusters;
+  size_t smem;
+  int o_head, o_chunk, o_xs, o_vs, o_ox, o_ov, o_catx, o_catv, o_part, o_p, o_red;
+};
+
+size_t plan_smem(const Layout& L, int R, int NST, SeqPlan* p) {
+  int off = 0;
+  auto take = [&](int n) { int o = off; off += ((n + 31) / 32) * 32; return o; };
+  p->o_head = take(2 * L.HS);
+  p->o_chunk = take(L.mix ? NST * L.CF : 0);
+  p->o_xs = take(R * L.C);
+  p->o_vs = take(R * L.C);
+  p->o_ox = take(L.mix ? R * L.C : 0);
+  p->o_ov = take(L.mix ? R * L.C : 0);
+  p->o_catx = take(L.mix ? R * L.d : 0);
+  p->o_catv = take(L.mix ? R * L.d : 0);
+  p->o_part = take(L.mix ? L.K * R * 2 : 0);
+  p->o_p = take(R * L.hpc * L.r);
+  p->o_red = take(L.mix ? SEQ_RED_FLOATS : 0);
+  return 128 + (size_t)off * 4;
+}
+
+int make_plan(int B, const Layout& L, const DevInfo& di, SeqPlan* p) {
+  p->L = L;
+  const int per_wave = di.sms / L.K > 0 ? di.sms / L.K : 1;
+  int want = (B + per_wave - 1) / per_wave;
+  int R = 1;
+  while (R < want) R *= 2;
+  int rb = 1;  // smallest pow2 >= B
+  while (rb < B) rb *= 2;
+  if (R > rb) R = rb;
+  for (; R >= 1; R /= 2) {
+    if (R * L.C > SEQ_THREADS * SEQ_OPT) continue;
+    const int TR = R < 4 ? R : 4;
+    const int NG = 2 * L.C / 4;
+    const int tiles = NG * (R / TR);
+    if (L.mix && tiles > SEQ_THREADS) continue;
+    for (int NST = 4; NST >= 2; --NST) {
+      const size_t smem = plan_smem(L, R, NST, p);
+      if (smem <= (size_t)di.max_smem) {
+        p->R = R; p->TR = TR; p->NG = NG; p->tiles = L.mix ? tiles : 1;
+        int S = 1;
+        while (L.mix && S * 2 * tiles <= SEQ_THREADS) S *= 2;
+        p->S = S;
+        p->NST = NST;
+        p->smem = smem;
+        p->nclusters = (B + R - 1) / R;
+        return GFN_OK;
+      }
+    }
+  }
+  return fail(GFN_ERR_RESOURCES, "no sequence plan fits %d bytes of shared memory", di.max_smem);
+}
+
+template <int RK>
+int launch_seq(const SeqArgs& a, const SeqPlan& p, cudaStream_t stream) {
+  auto kern = leapfrog_seq_kernel<RK>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.smem);
+  if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(smem)");
+  if (p.L.K > 8) {
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(cluster)");
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(p.nclusters * p.L.K));
+  cfg.blockDim = dim3(SEQ_THREADS);
+  cfg.dynamicSmemBytes = p.smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = p.L.K;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cfg, kern, a);
+  return cuda_status(e, "leapfrog_seq_kernel launch");
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* gfn_status_string(int s) {
+  switch (s) {
+    case GFN_OK: return "ok";
+    case GFN_ERR_INVALID: return "invalid argument";
+    case GFN_ERR_UNSUPPORTED: return "unsupported configuration";
+    case GFN_ERR_ALIGN: return "misaligned pointer";
+    case GFN_ERR_CUDA: return "CUDA error";
+    case GFN_ERR_RESOURCES: return "insufficient device resources";
+    default: return "unknown status";
+  }
+}
+
+const char* gfn_last_error_message(void) { return g_msg; }
+
+const char* gfn_build_info(void) {
+  return "gfn_b200 sm_100a; kernels: leapfrog_seq (cluster/DSMEM/bulk-copy), leapfrog_head, "
+         "christoffel, scan, parallel_layer_scan, siren_embed, pack";
+}
+
+int gfn_get_device_error(int* bits, int reset, gfn_stream_t stream) {
+  if (!bits) return fail(GFN_ERR_INVALID, "bits is NULL");
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  int v = 0;
+  cudaError_t e = cudaMemcpyFromSymbolAsync(&v, gfn_device_err, sizeof(int), 0, cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) return cuda_status(e, "read device error word");
+  *bits = v;
+  if (reset && v) {
+    const int zero = 0;
+    e = cudaMemcpyToSymbolAsync(gfn_device_err, &zero, sizeof(int), 0, cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) return cuda_status(e, "reset device error word");
+  }
+  return GFN_OK;
+}
+
+int gfn_christoffel_fused(const float* v, const float* U, const float* W, float* gamma,
+                          const float* x, const float* V_w, int batch, int dim, int rank,
+                          float plasticity, float sing_thresh, float sing_strength, int topology,
+                          float R_val, float r_val, gfn_stream_t stream) {
+  (void)x; (void)sing_thresh; (void)sing_strength; (void)R_val; (void)r_val;
+  if (!v || !U || !W || !gamma) return fail(GFN_ERR_INVALID, "christoffel: NULL operand");
+  if (batch < 0 || dim <= 0) return fail(GFN_ERR_INVALID, "christoffel: batch=%d dim=%d", batch, dim);
+  if (topology != 0 || plasticity != 0.f || V_w)
+    return fail(GFN_ERR_UNSUPPORTED, "christoffel: only the Euclidean, plasticity-free form");
+  if (rank != 4 && rank != 8 && rank != 16)
+    return fail(GFN_ERR_UNSUPPORTED, "christoffel: rank %d not in {4, 8, 16}", rank);
+  if (rank % 4 == 0 && !aligned16(U)) return fail(GFN_ERR_ALIGN, "christoffel: U not 16-byte aligned");
+  if (batch == 0) return GFN_OK;
+  HeadArgs a = {};
+  a.v = v; a.U = U; a.W = W; a.gamma_out = gamma; a.B = batch; a.hd = dim;
+  const size_t smem = (size_t)small_smem(dim, rank).total * 4;
+  if (smem > 200 * 1024) return fail(GFN_ERR_RESOURCES, "christoffel: dim %d too large", dim);
+  dim3 grid((batch + SMALL_ROWS - 1) / SMALL_ROWS);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+#define GFN_CH(RK)                                                                                   \
+  case RK:                                                                                           \
+    cudaFuncSetAttribute(christoffel_kernel<RK>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); \
+    christoffel_kernel<RK><<<grid, SMALL_THREADS, smem, s>>>(a);                                     \
+    break;
+  switch (rank) { GFN_CH(4) GFN_CH(8) GFN_CH(16) }
+#undef GFN_CH
+  return launch_status("christoffel_kernel");
+}
+
+int gfn_leapfrog_fused(const float* x, const float* v, const float* f, const float* U,
+                       const float* W, const float* W_forget, const float* b_forget, float* x_new,
+                       float* v_new, float dt, const float* dt_scales, int dt_scales_count,
+                       int batch, int dim, int rank, int steps, int topology, float plasticity,
+                       float R_val, float r_val, gfn_stream_t stream) {
+  (void)R_val; (void)r_val;
+  if (!x || !v || !U || !W || !x_new || !v_new) return fail(GFN_ERR_INVALID, "leapfrog: NULL operand");
+  if (batch < 0 || dim <= 0 || steps < 0) return fail(GFN_ERR_INVALID, "leapfrog: bad sizes");
+  if (topology != 0 || plasticity != 0.f)
+    return fail(GFN_ERR_UNSUPPORTED, "leapfrog: only topology 0 without plasticity");
+  if (rank != 4 && rank != 8 && rank != 16)
+    return fail(GFN_ERR_UNSUPPORTED, "leapfrog: rank %d not in {4, 8, 16}", rank);
+  if (!aligned16(U)) return fail(GFN_ERR_ALIGN, "leapfrog: U not 16-byte aligned");
+  if (dt_scales && dt_scales_count != 1 && dt_scales_count != batch)
+    return fail(GFN_ERR_INVALID, "leapfrog: dt_scales_count %d (need 1 or batch)", dt_scales_count);
+  if ((W_forget == nullptr) != (b_forget == nullptr) && W_forget == nullptr)
+    return fail(GFN_ERR_INVALID, "leapfrog: b_forget without W_forget");
+  if (batch == 0) return GFN_OK;
+  HeadArgs a = {};
+  a.x = x; a.v = v; a.f = f; a.U = U; a.W = W; a.Wf = W_forget; a.bf = b_forget;
+  a.dt_scale = dt_scales; a.dt_scale_n = dt_scales_count; a.dt = dt; a.steps = steps;
+  a.x_out = x_new; a.v_out = v_new; a.B = batch; a.hd = dim;
+  const size_t smem = (size_t)small_smem(dim, rank).total * 4;
+  if (smem > 200 * 1024) return fail(GFN_ERR_RESOURCES, "leapfrog: dim %d too large", dim);
+  dim3 grid((batch + SMALL_ROWS - 1) / SMALL_ROWS);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+#define GFN_LF(RK)                                                                                     \
+  case RK:                                                                                             \
+    cudaFuncSetAttribute(leapfrog_head_kernel<RK>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); \
+    leapfrog_head_kernel<RK><<<grid, SMALL_THREADS, smem, s>>>(a);                                     \
+    break;
+  switch (rank) { GFN_LF(4) GFN_LF(8) GFN_LF(16) }
+#undef GFN_LF
+  return launch_status("leapfrog_head_kernel");
+}
+
+long long gfn_leapfrog_pack_floats(int dim, int heads, int rank, int num_layers) {
+  Layout L;
+  if (make_layout(dim, heads, rank, num_layers, &L) != GFN_OK) return -1;
+  return (long long)num_layers * L.K * L.LF;
+}
+
+int gfn_leapfrog_plan(int batch, int dim, int heads, int rank, int num_layers, int* out6) {
+  if (!out6) return fail(GFN_ERR_INVALID, "plan: out6 NULL");
+  Layout L;
+  int st = make_layout(dim, heads, rank, num_layers, &L);
+  if (st) return st;
+  DevInfo di;
+  st = dev_info(&di);
+  if (st) return st;
+  SeqPlan p;
+  st = make_plan(batch > 0 ? batch : 1, L, di, &p);
+  if (st) return st;
+  out6[0] = L.K; out6[1] = p.R; out6[2] = p.nclusters; out6[3] = (int)p.smem;
+  out6[4] = L.KC; out6[5] = p.NST;
+  return GFN_OK;
+}
+
+int gfn_leapfrog_pack(const float* U_stack, const float* W_stack, const float* W_forget_stack,
+                      const float* b_forget_stack, const float* dt_params, const float* mix_x_w,
+                      const float* mix_x_b, const float* norm_x_w, const float* mix_v_w,
+                      const float* mix_v_b, const float* norm_v_w, int dim, int heads, int rank,
+                      int num_layers, float* packed, long long packed_floats, gfn_stream_t stream) {
+  Layout L;
+  int st = make_layout(dim, heads, rank, num_layers, &L);
+  if (st) return st;
+  if (!U_stack || !W_stack || !W_forget_stack || !b_forget_stack || !dt_params || !packed)
+    return fail(GFN_ERR_INVALID, "pack: NULL head parameter");
+  if (L.mix && (!mix_x_w || !mix_v_w))
+    return fail(GFN_ERR_INVALID, "pack: heads > 1 needs the mixing weights");
+  const long long need = (long long)num_layers * L.K * L.LF;
+  if (packed_floats < need) return fail(GFN_ERR_INVALID, "pack: buffer %lld < %lld floats", packed_floats, need);
+  if (!aligned16(packed)) return fail(GFN_ERR_ALIGN, "pack: output not 16-byte aligned");
+  PackArgs a;
+  a.U = U_stack; a.W = W_stack; a.Wf = W_forget_stack; a.bf = b_forget_stack; a.dtp = dt_params;
+  a.Wx = mix_x_w; a.bx = mix_x_b; a.gx = norm_x_w; a.Wv = mix_v_w; a.bv = mix_v_b; a.gv = norm_v_w;
+  a.out = packed; a.NL = num_layers; a.d = dim; a.H = heads; a.hd = L.hd; a.r = rank; a.K = L.K;
+  a.C = L.C; a.hpc = L.hpc; a.KC = L.KC; a.nchunk = L.nchunk; a.HS = L.HS; a.CF = L.CF; a.LF = L.LF;
+  long long blocks = (need + 255) / 256;
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  pack_kernel<<<(unsigned)blocks, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(a);
+  return launch_status("pack_kernel");
+}
+
+int gfn_leapfrog_sequence_forward(const float* x_init, const float* v_init,
+                                  long long state_row_stride, const float* forces_f32,
+                                  const void* forces_bf16, const long long* token_ids,
+                                  const float* embed_table, long long vocab, const float* mask,
+                                  const float* packed, long long packed_floats, int batch,
+                                  int seq_len, int dim, int heads, int rank, int num_layers,
+                                  float base_dt, float* x_seq, float* v_seq, float* x_final,
+                                  float* v_final, gfn_stream_t stream) {
+  Layout L;
+  int st = make_layout(dim, heads, rank, num_layers, &L);
+  if (st) return st;
+  if (batch < 0 || seq_len < 0) return fail(GFN_ERR_INVALID, "sequence: batch=%d seq_len=%d", batch, seq_len);
+  if (!x_init || !v_init || !packed) return fail(GFN_ERR_INVALID, "sequence: NULL state or weights");
+  if (state_row_stride < 0) return fail(GFN_ERR_INVALID, "sequence: negative state stride");
+  const int nsrc = (forces_f32 != nullptr) + (forces_bf16 != nullptr) + (token_ids != nullptr);
+  if (seq_len > 0 && nsrc != 1)
+    return fail(GFN_ERR_INVALID, "sequence: give exactly one of forces_f32, forces_bf16, token_ids");
+  if (token_ids && (!embed_table || vocab <= 0))
+    return fail(GFN_ERR_INVALID, "sequence: token_ids need embed_table and vocab > 0");
+  const long long need = (long long)num_layers * L.K * L.LF;
+  if (packed_floats < need) return fail(GFN_ERR_INVALID, "sequence: packed %lld < %lld floats", packed_floats, need);
+  if (!aligned16(packed)) return fail(GFN_ERR_ALIGN, "sequence: packed weights not 16-byte aligned");
+  if (batch == 0) return GFN_OK;
+  DevInfo di;
+  st = dev_info(&di);
+  if (st) return st;
+  SeqPlan p;
+  st = make_plan(batch, L, di, &p);
+  if (st) return st;
+  SeqArgs a = {};
+  a.x0 = x_init; a.v0 = v_init; a.state_stride = state_row_stride;
+  a.f32 = forces_f32; a.fbf16 = reinterpret_cast<const __nv_bfloat16*>(forces_bf16);
+  a.ids = token_ids; a.table = embed_table; a.vocab = vocab; a.mask = mask; a.pack = packed;
+  a.x_seq = x_seq; a.v_seq = v_seq; a.x_out = x_final; a.v_out = v_final;
+  a.B = batch; a.L = seq_len; a.d = dim; a.H = heads; a.hd = L.hd; a.NL = num_layers;
+  a.K = L.K; a.R = p.R; a.C = L.C; a.hpc = L.hpc; a.KC = L.KC; a.nchunk = L.nchunk; a.NST = p.NST;
+  a.HS = L.HS; a.CF = L.CF; a.LF = L.LF; a.mix = L.mix;
+  a.TR = p.TR; a.NG = p.NG; a.tiles = p.tiles; a.S = p.S; a.base_dt = base_dt;
+  a.o_head = p.o_head; a.o_chunk = p.o_chunk; a.o_xs = p.o_xs; a.o_vs = p.o_vs; a.o_ox = p.o_ox;
+  a.o_ov = p.o_ov; a.o_catx = p.o_catx; a.o_catv = p.o_catv; a.o_part = p.o_part; a.o_p = p.o_p;
+  a.o_red = p.o_red;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  switch (rank) {
+    case 4: return launch_seq<4>(a, p, s);
+    case 8: return launch_seq<8>(a, p, s);
+    default: return launch_seq<16>(a, p, s);
+  }
+}
+
+long long gfn_parallel_scan_workspace_floats(int batch, int seq_len, int dim) {
+  (void)seq_len;
+  return 2LL * 64 * batch * dim;
+}
+
+int gfn_parallel_scan(const float* a, const float* x, float* y, float* workspace,
+                      long long workspace_floats, int batch, int seq_len, int dim,
+                      gfn_stream_t stream) {
+  if (!x || !y) return fail(GFN_ERR_INVALID, "scan: NULL x or y");
+  if (batch < 0 || seq_len < 0 || dim <= 0) return fail(GFN_ERR_INVALID, "scan: bad sizes");
+  if (dim % 4) return fail(GFN_ERR_UNSUPPORTED, "scan: dim %d must be a multiple of 4", dim);
+  if (!aligned16(x) || !aligned16(y) || (a && !aligned16(a)))
+    return fail(GFN_ERR_ALIGN, "scan: operands must be 16-byte aligned");
+  if (batch == 0 || seq_len == 0) return GFN_OK;
+  DevInfo di;
+  int st = dev_info(&di);
+  if (st) return st;
+  ScanArgs s;
+  s.a = a; s.x = x; s.y = y; s.ws = workspace; s.B = batch; s.L = seq_len; s.D = dim; s.P = 1;
+  const long long groups = (long long)batch * (dim / 4);
+  const long long want_threads = (long long)di.sms * 1024;
+  int P = 1;
+  if (workspace && groups < want_threads / 4) {
+    while (P < 64 && groups * P * 2 <= want_threads && seq_len / (P * 2) >= 64) P *= 2;
+  }
+  if (P > 1 && workspace_floats < 2LL * P * batch * dim) P = 1;
+  s.P = P;
+  cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);
+  const unsigned gx = (unsigned)((groups + SCAN_THREADS - 1) / SCAN_THREADS);
+  if (P == 1) {
+    scan_single_kernel<<<gx, SCAN_THREADS, 0, cs>>>(s);
+    return launch_status("scan_single_kernel");
+  }
+  scan_chunk_reduce_kernel<<<dim3(gx, P), SCAN_THREADS, 0, cs>>>(s);
+  const long long BD = (long long)batch * dim;
+  scan_chunk_carry_kernel<<<(unsigned)((BD + SCAN_THREADS - 1) / SCAN_THREADS), SCAN_THREADS, 0, cs>>>(s);
+  scan_chunk_apply_kernel<<<dim3(gx, P), SCAN_THREADS, 0, cs>>>(s);
+  return launch_status("scan_chunk kernels");
+}
+
+int gfn_parallel_layer_scan(const float* z, float* x_seq, float* v_seq, int batch, int seq_len,
+                            int dim, int heads, float base_dt, gfn_stream_t stream) {
+  if (!z || !x_seq || !v_seq) return fail(GFN_ERR_INVALID, "layer scan: NULL operand");
+  if (batch < 0 || seq_len < 0 || dim <= 0 || heads <= 0 || dim % heads)
+    return fail(GFN_ERR_INVALID, "layer scan: bad sizes");
+  if (dim % 4) return fail(GFN_ERR_UNSUPPORTED, "layer scan: dim %d must be a multiple of 4", dim);
+  if (!aligned16(z) || !aligned16(x_seq) || !aligned16(v_seq))
+    return fail(GFN_ERR_ALIGN, "layer scan: operands must be 16-byte aligned");
+  if (batch == 0 || seq_len == 0) return GFN_OK;
+  PScanArgs s;
+  s.z = z; s.x_seq = x_seq; s.v_seq = v_seq; s.B = batch; s.L = seq_len; s.D = dim; s.H = heads;
+  s.base_dt = base_dt;
+  const long long groups = (long long)batch * (dim / 4);
+  parallel_layer_scan_kernel<<<(unsigned)((groups + SCAN_THREADS - 1) / SCAN_THREADS), SCAN_THREADS, 0,
+                               reinterpret_cast<cudaStream_t>(stream)>>>(s);
+  return launch_status("parallel_layer_scan_kernel");
+}
+
+int gfn_functional_embedding(const long long* ids, long long n, const float* W0, const float* b0,
+                             const float* W1, const float* b1, const float* W2, const float* b2,
+                             const float* Wo, const float* bo, const float* impulse, float omega0,
+                             int dim, float* out_f32, void* out_bf16, gfn_stream_t stream) {
+  if (!ids || !W0 || !b0 || !W1 || !b1 || !W2 || !b2 || !Wo || !bo || !impulse)
+    return fail(GFN_ERR_INVALID, "embedding: NULL operand");
+  if ((out_f32 == nullptr) == (out_bf16 == nullptr))
+    return fail(GFN_ERR_INVALID, "embedding: give exactly one of out_f32, out_bf16");
+  if (n < 0 || dim <= 0) return fail(GFN_ERR_INVALID, "embedding: bad sizes");
+  if (!aligned16(Wo)) return fail(GFN_ERR_ALIGN, "embedding: Wo not 16-byte aligned");
+  if (n == 0) return GFN_OK;
+  EmbArgs a;
+  a.ids = ids; a.n = n; a.W0 = W0; a.b0 = b0; a.W1 = W1; a.b1 = b1; a.W2 = W2; a.b2 = b2;
+  a.Wo = Wo; a.bo = bo; a.impulse = impulse; a.omega0 = omega0; a.d = dim;
+  a.out_f32 = out_f32; a.out_bf16 = reinterpret_cast<__nv_bfloat16*>(out_bf16);
+  const long long blocks = (n + EMB_TOK - 1) / EMB_TOK;
+  siren_embed_kernel<<<(unsigned)blocks, EMB_THREADS, 0, reinterpret_cast<cudaStream_t>(stream)>>>(a);
+  return launch_status("siren_embed_kernel");
+}
+
+}  // extern "C"

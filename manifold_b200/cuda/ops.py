@@ -1,0 +1,210 @@
+"""Operator boundary: the reference's ``gfn.cuda.ops`` entry points on the
+B200 kernels (through the C ABI of include/gfn_b200.h).
+
+Names, arguments and return values follow gfn/cuda/ops.py.  There is no
+Python fallback: CPU tensors and unsupported options raise ``GfnError``.
+"""
+import torch
+
+from .. import _lib
+from .._lib import GfnError, call, ptr, require_cuda
+
+CUDA_AVAILABLE = True  # the library is required; import fails loudly otherwise
+
+
+def _f32c(t, name):
+    if t is None:
+        return None
+    if t.dtype != torch.float32:
+        raise GfnError(f"{name} must be float32, got {t.dtype}")
+    return t.contiguous()
+
+
+def _stream(t):
+    return _lib.stream_of(t.device)
+
+
+def christoffel_fused(v, U, W, x=None, V_w=None, plasticity=0.0, sing_thresh=1.0,
+                      sing_strength=1.0, topology=0, R=2.0, r=1.0):
+    """Gamma(v) for one head (gfn/cuda/ops.py:88-118; gfn/geometry/lowrank.py:93-98,125-127)."""
+    require_cuda(v, U, W)
+    v, U, W = _f32c(v, "v"), _f32c(U, "U"), _f32c(W, "W")
+    gamma = torch.empty_like(v)
+    call("gfn_christoffel_fused", ptr(v), ptr(U), ptr(W), ptr(gamma), None,
+         ptr(V_w) if V_w is not None else None, v.shape[0], v.shape[1], U.shape[1],
+         float(plasticity), float(sing_thresh), float(sing_strength), int(topology), float(R),
+         float(r), _stream(v))
+    return gamma
+
+
+def leapfrog_fused(x, v, f, U, W, dt, dt_scale, steps, topology=0, Wf=None, bf=None,
+                   plasticity=0.0, R=2.0, r=1.0):
+    """One head's leapfrog, `steps` times (gfn/cuda/ops.py:131-182;
+    gfn/integrators/symplectic/leapfrog.py:50-114).  Returns (x_new, v_new)."""
+    require_cuda(x, v, f, U, W, Wf, bf)
+    x, v, U, W = _f32c(x, "x"), _f32c(v, "v"), _f32c(U, "U"), _f32c(W, "W")
+    f = _f32c(f, "f")
+    Wf, bf = _f32c(Wf, "Wf"), _f32c(bf, "bf")
+    if not isinstance(dt_scale, torch.Tensor):
+        dt_scale = torch.tensor([float(dt_scale)], device=x.device, dtype=torch.float32)
+    dts = dt_scale.reshape(-1).to(torch.float32).contiguous()
+    x_new = torch.empty_like(x)
+    v_new = torch.empty_like(v)
+    call("gfn_leapfrog_fused", ptr(x), ptr(v), ptr(f), ptr(U), ptr(W), ptr(Wf), ptr(bf),
+         ptr(x_new), ptr(v_new), float(dt), ptr(dts), dts.numel(), x.shape[0], x.shape[1],
+         U.shape[1], int(steps), int(topology), float(plasticity), float(R), float(r), _stream(x))
+    return x_new, v_new
+
+
+def leapfrog_pack(U_stack, W_stack, Wf_stack, bf_stack, dt_params, mix=None):
+    """Pack stacked layer parameters for leapfrog_sequence.
+
+    U_stack/W_stack [NL*H, hd, r], Wf_stack [NL*H, hd, hd], bf_stack
+    [NL*H, hd], dt_params [NL*H]; mix = (Wx, bx, gx, Wv, bv, gv) with
+    Wx/Wv [NL, d, d] and the rest [NL, d], or None when heads == 1.
+    """
+    NLH, hd, r = U_stack.shape
+    dev = U_stack.device
+    args = [_f32c(t, "stack") for t in (U_stack, W_stack, Wf_stack, bf_stack, dt_params)]
+    if mix is not None:
+        Wx = _f32c(mix[0], "Wx")
+        num_layers, d, _ = Wx.shape
+        heads = d // hd
+        mix = [_f32c(t, "mix") for t in mix]
+    else:
+        heads = 1
+        num_layers = NLH
+        d = hd
+        mix = [None] * 6
+    n = _lib.load().gfn_leapfrog_pack_floats(d, heads, r, num_layers)
+    if n < 0:
+        call("gfn_leapfrog_pack_floats", d, heads, r, num_layers)  # raises with the message
+    packed = torch.empty(int(n), device=dev, dtype=torch.float32)
+    call("gfn_leapfrog_pack", *[ptr(t) for t in args], ptr(mix[0]), ptr(mix[1]), ptr(mix[2]),
+         ptr(mix[3]), ptr(mix[4]), ptr(mix[5]), d, heads, r, num_layers, ptr(packed), packed.numel(),
+         _lib.stream_of(dev))
+    return packed, dict(dim=d, heads=heads, rank=r, num_layers=num_layers)
+
+
+def leapfrog_sequence(x0, v0, packed, meta, base_dt, forces=None, ids=None, table=None,
+                      mask=None, want_x_seq=True, want_v_seq=True):
+    """Whole-sequence fused leapfrog recurrence over all layers.
+
+    x0/v0: [B, d] or [1, d] / [d] (broadcast).  Exactly one of forces
+    ([B, L, d] float32 or bfloat16) or ids ([B, L] int64) + table ([V, d]).
+    Returns (x_seq, v_seq, x_final, v_final); x_seq/v_seq None if not wanted.
+    """
+    require_cuda(x0, v0, packed, forces, ids, table, mask)
+    d = meta["dim"]
+    x0 = _f32c(x0, "x0")
+    v0 = _f32c(v0, "v0")
+    if forces is not None:
+        B, L, _ = forces.shape
+        forces = forces.contiguous()
+    elif ids is not None:
+        B, L = ids.shape
+        ids = ids.to(torch.int64).contiguous()
+        table = _f32c(table, "table")
+    else:
+        raise GfnError("leapfrog_sequence needs forces or ids")
+    if x0.dim() == 1 or x0.shape[0] == 1:
+        stride = 0
+        if B > 1 and (v0.dim() != 1 and v0.shape[0] != 1):
+            raise GfnError("x0 and v0 must both broadcast or both be [B, d]")
+    else:
+        if x0.shape != (B, d) or v0.shape != (B, d):
+            raise GfnError(f"state must be [B={B}, d={d}]")
+        stride = d
+    dev = x0.device
+    x_seq = torch.empty(B, L, d, device=dev, dtype=torch.float32) if want_x_seq else None
+    v_seq = torch.empty(B, L, d, device=dev, dtype=torch.float32) if want_v_seq else None
+    x_f = torch.empty(B, d, device=dev, dtype=torch.float32)
+    v_f = torch.empty(B, d, device=dev, dtype=torch.float32)
+    f32 = forces if (forces is not None and forces.dtype == torch.float32) else None
+    fbf = forces if (forces is not None and forces.dtype == torch.bfloat16) else None
+    if forces is not None and f32 is None and fbf is None:
+        raise GfnError(f"forces must be float32 or bfloat16, got {forces.dtype}")
+    if mask is not None:
+        mask = mask.to(torch.float32).contiguous()
+    call("gfn_leapfrog_sequence_forward", ptr(x0), ptr(v0), stride, ptr(f32), ptr(fbf), ptr(ids),
+         ptr(table), table.shape[0] if table is not None else 0, ptr(mask), ptr(packed),
+         packed.numel(), B, L, d, meta["heads"], meta["rank"], meta["num_layers"],
+         float(base_dt), ptr(x_seq), ptr(v_seq), ptr(x_f), ptr(v_f), _lib.stream_of(dev))
+    return x_seq, v_seq, x_f, v_f
+
+
+def leapfrog_plan(batch, dim, heads, rank, num_layers):
+    import ctypes
+    out = (ctypes.c_int * 6)()
+    call("gfn_leapfrog_plan", batch, dim, heads, rank, num_layers, out)
+    return dict(cluster=out[0], rows_per_cluster=out[1], clusters=out[2], smem=out[3],
+                k_chunk=out[4], ring=out[5])
+
+
+def parallel_scan_fused(a, x, workspace=True):
+    """y_t = a_t y_{t-1} + x_t over dim 1 of [B, L, D] (gfn/scan.py:11-104).
+    a None means a == 1."""
+    require_cuda(a, x)
+    x = _f32c(x, "x")
+    a = _f32c(a, "a")
+    B, L, D = x.shape
+    y = torch.empty_like(x)
+    ws = None
+    if workspace:
+        n = _lib.load().gfn_parallel_scan_workspace_floats(B, L, D)
+        ws = torch.empty(int(n), device=x.device, dtype=torch.float32)
+    call("gfn_parallel_scan", ptr(a), ptr(x), ptr(y), ptr(ws), ws.numel() if ws is not None else 0,
+         B, L, D, _stream(x))
+    return y
+
+
+def parallel_layer_scan(z, heads, base_dt=0.1):
+    """ParallelMLayer recurrence from z = [zA | zdt | zB] ([B, L, 3D]).
+    Returns (x_seq, v_seq)."""
+    require_cuda(z)
+    z = _f32c(z, "z")
+    B, L, D3 = z.shape
+    D = D3 // 3
+    x_seq = torch.empty(B, L, D, device=z.device, dtype=torch.float32)
+    v_seq = torch.empty_like(x_seq)
+    call("gfn_parallel_layer_scan", ptr(z), ptr(x_seq), ptr(v_seq), B, L, D, int(heads),
+         float(base_dt), _stream(z))
+    return x_seq, v_seq
+
+
+def functional_embedding(ids, W0, b0, W1, b1, W2, b2, Wo, bo, impulse, omega0=30.0,
+                         out_dtype=torch.float32):
+    """FunctionalEmbedding(mode='binary') forward (gfn/embeddings.py:171-206)."""
+    require_cuda(ids, Wo)
+    ids = ids.to(torch.int64).contiguous()
+    ws = [_f32c(t, "siren weight") for t in (W0, b0, W1, b1, W2, b2, Wo, bo)]
+    imp = _f32c(impulse.reshape(1), "impulse")
+    d = Wo.shape[0]
+    out = torch.empty(*ids.shape, d, device=ids.device, dtype=out_dtype)
+    f32 = out if out_dtype == torch.float32 else None
+    bf = out if out_dtype == torch.bfloat16 else None
+    if f32 is None and bf is None:
+        raise GfnError("functional_embedding: out_dtype must be float32 or bfloat16")
+    call("gfn_functional_embedding", ptr(ids), ids.numel(), *[ptr(t) for t in ws], ptr(imp),
+         float(omega0), d, ptr(f32), ptr(bf), _stream(ids))
+    return out
+
+
+def device_error(reset=True):
+    return _lib.device_error(reset)
+
+
+def _unsupported(name):
+    def fn(*args, **kwargs):
+        raise GfnError(f"{name}: only the leapfrog integrator is implemented on this build")
+    fn.__name__ = name
+    return fn
+
+
+euler_fused = _unsupported("euler_fused")
+heun_fused = _unsupported("heun_fused")
+rk4_fused = _unsupported("rk4_fused")
+verlet_fused = _unsupported("verlet_fused")
+yoshida_fused = _unsupported("yoshida_fused")
+forest_ruth_fused = _unsupported("forest_ruth_fused")
+dormand_prince_fused = _unsupported("dormand_prince_fused")

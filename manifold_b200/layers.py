@@ -1,0 +1,163 @@
+"""M-Layer and the parallel (scan) layer, mirrors of gfn/layers/base.py,
+gfn/layers/parallel.py and gfn/layers/gating.py on the B200 kernels.
+
+MLayer keeps the reference's submodule tree (christoffels, gatings,
+friction_gates, integrators, out_proj_*, mixed_norm_*, norm_*) and its
+construction order, so the same seed gives the same initial weights and a
+reference state_dict loads as is.  Its forward runs one layer step of the
+fused recurrence kernel.
+"""
+import torch
+import torch.nn as nn
+
+from ._lib import GfnError, require_cuda
+from .cuda import ops
+from .geometry import ReactiveChristoffel
+from .integrators import LeapfrogIntegrator
+from .packing import PackCache
+
+
+class RiemannianGating(nn.Module):
+    """Curvature-based dt gate (gfn/layers/gating.py:4-51).  Parameters only:
+    the dynamic-time option that uses it is off on the leapfrog path."""
+
+    def __init__(self, dim, topology=0):
+        super().__init__()
+        self.topology = topology
+        input_dim = 2 * dim if topology == 1 else dim
+        self.curvature_net = nn.Sequential(nn.Linear(input_dim, dim // 4), nn.Tanh(),
+                                           nn.Linear(dim // 4, 1), nn.Sigmoid())
+        with torch.no_grad():
+            nn.init.constant_(self.curvature_net[2].bias, 2.0)
+            nn.init.xavier_uniform_(self.curvature_net[0].weight, gain=0.1)
+            nn.init.xavier_uniform_(self.curvature_net[2].weight, gain=0.1)
+
+    def forward(self, x):
+        if self.topology == 1:
+            x = torch.cat([torch.sin(x), torch.cos(x)], dim=-1)
+        return self.curvature_net(x)
+
+
+def _check_config(physics_config, integrator_type):
+    pc = physics_config or {}
+    if integrator_type != "leapfrog":
+        raise GfnError(f"integrator_type={integrator_type!r}: only 'leapfrog' is implemented on "
+                       "this build")
+    if pc.get("topology", {}).get("type", "euclidean").lower() == "torus":
+        raise GfnError("toroidal topology is not implemented on this build")
+    for key in ("mixture", "hyper_curvature"):
+        if pc.get(key, {}).get("enabled", False):
+            raise GfnError(f"physics_config[{key!r}] is not implemented on this build")
+    ai = pc.get("active_inference", {})
+    if ai.get("enabled", False) or ai.get("dynamic_time", {}).get("enabled", False) \
+            or ai.get("recursive_geodesics", {}).get("enabled", False):
+        raise GfnError("active-inference options are not implemented on this build")
+    if pc.get("symmetries", {}).get("isomeric_groups"):
+        raise GfnError("isomeric head groups are not implemented on this build")
+
+
+class MLayer(nn.Module):
+    """One M-Layer: per-head leapfrog, head mixing, RMSNorm, saturation.
+
+    Parameters/init: gfn/layers/base.py:34-196.  forward: base.py:198-338.
+    """
+
+    def __init__(self, dim, heads=4, rank=16, base_dt=0.1, integrator_type="heun",
+                 physics_config=None, layer_idx=0, total_depth=6):
+        super().__init__()
+        assert dim % heads == 0, f"Dim {dim} must be divisible by heads {heads}"
+        _check_config(physics_config, integrator_type)
+        self.dim = dim
+        self.heads = heads
+        self.head_dim = dim // heads
+        self.physics_config = physics_config or {}
+        self.base_dt = self.physics_config.get("stability", {}).get("base_dt", base_dt)
+        self.layer_idx = layer_idx
+        self.total_depth = total_depth
+        self.depth_scale = 1.0 / (total_depth ** 0.5)
+        self.norm_x = nn.LayerNorm(dim)
+        self.norm_v = nn.LayerNorm(dim)
+        head_rank = max(4, rank // heads)
+        self.christoffels = nn.ModuleList(
+            [ReactiveChristoffel(self.head_dim, head_rank, physics_config=self.physics_config)
+             for _ in range(heads)])
+        self.register_buffer("headless_mode", torch.tensor(False))
+        self.use_dynamic_time = False
+        self.topology_id = 0
+        self.gatings = nn.ModuleList([RiemannianGating(self.head_dim, topology=0) for _ in range(heads)])
+        scale_vals = []
+        for i in range(heads):
+            target_dt = self.base_dt / 0.9
+            val_init = torch.tensor(target_dt).exp().sub(1.0).log()
+            scale_vals.append(val_init + i * 0.1)
+        self.dt_params = nn.Parameter(torch.tensor(scale_vals))
+        self.time_heads = None
+        self.friction_gates = nn.ModuleList([self.christoffels[i].forget_gate for i in range(heads)])
+        self.integrators = nn.ModuleList(
+            [LeapfrogIntegrator(self.christoffels[i], dt=self.base_dt) for i in range(heads)])
+        if heads > 1:
+            self.out_proj_x = nn.Linear(dim, dim)
+            self.out_proj_v = nn.Linear(dim, dim)
+            self.mixed_norm_x = nn.RMSNorm(dim)
+            self.mixed_norm_v = nn.RMSNorm(dim)
+            nn.init.xavier_uniform_(self.out_proj_x.weight)
+            nn.init.zeros_(self.out_proj_x.bias)
+            nn.init.xavier_uniform_(self.out_proj_v.weight)
+            nn.init.zeros_(self.out_proj_v.bias)
+        self.use_recursive = False
+        self._pack = PackCache()
+
+    def forward(self, x, v, force=None, context=None, collect_christ=False):
+        """One layer step for every row: returns (x_next, v_next, context, [])."""
+        require_cuda(x, v, force)
+        if collect_christ:
+            raise GfnError("collect_christ is not supported by the fused kernels")
+        B = x.shape[0]
+        packed, meta = self._pack.get([self])
+        if force is None:
+            force = torch.zeros_like(x)
+        _, _, xn, vn = ops.leapfrog_sequence(x, v, packed, meta, self.base_dt,
+                                             forces=force.reshape(B, 1, self.dim),
+                                             want_x_seq=False, want_v_seq=False)
+        context_next = torch.ones(B, self.heads, device=x.device, dtype=x.dtype)
+        return xn, vn, context_next, []
+
+
+class ParallelMLayer(nn.Module):
+    """Linearised layer for the scan path (gfn/layers/parallel.py:5-125):
+    force -> LayerNorm -> A = sigmoid(to_A), dt = softplus(to_dt) * 0.1 * 1.5^head,
+    B = to_B * dt -> v = scan(A, B), x = scan(1, v dt).
+
+    The three projections run as one cuBLAS GEMM against the concatenated
+    weight; the two scans and all elementwise work run in one fused kernel.
+    """
+
+    def __init__(self, dim, heads=4, physics_config=None, **kwargs):
+        super().__init__()
+        assert dim % heads == 0
+        self.dim = dim
+        self.heads = heads
+        self.head_dim = dim // heads
+        self.norm_x = nn.LayerNorm(dim)
+        self.norm_v = nn.LayerNorm(dim)
+        self.to_A = nn.Sequential(nn.Linear(dim, dim), nn.Sigmoid())
+        self.to_B = nn.Linear(dim, dim)
+        self.to_dt = nn.Sequential(nn.Linear(dim, dim), nn.Softplus())
+        scale_vec = []
+        for i in range(heads):
+            scale_vec.extend([1.5 ** i] * (dim // heads))
+        self.register_buffer("base_dt_scales", torch.tensor(scale_vec, dtype=torch.float32))
+        self.base_dt = 0.1
+        if heads > 1:
+            self.out_proj = nn.Linear(dim * 2, dim * 2)
+
+    def forward(self, x, v, force, collect_christ=False):
+        require_cuda(force)
+        if x is not None:
+            raise GfnError("ParallelMLayer with an explicit x is not used by the reference model")
+        f = self.norm_x(force)
+        Wcat = torch.cat([self.to_A[0].weight, self.to_dt[0].weight, self.to_B.weight], 0)
+        bcat = torch.cat([self.to_A[0].bias, self.to_dt[0].bias, self.to_B.bias], 0)
+        z = torch.nn.functional.linear(f, Wcat, bcat)
+        x_seq, v_seq = ops.parallel_layer_scan(z, self.heads, self.base_dt)
+        return x_seq, v_seq, None, []

@@ -1,0 +1,239 @@
+"""CPU restatement (numpy) of the reference's recurrent geodesic-flow hot path.
+
+TEST INFRASTRUCTURE ONLY.  This module is the parity checker for the CUDA
+path: only ``tests/``, ``__graft_entry__.smoke()`` and ``bench.py``'s CPU
+baseline leg may import it.  The product (``manifold_b200``) never calls it;
+there is no CPU fallback.
+
+Every function restates the reference's PyTorch CPU code path (Manifold-
+Laboratory/manifold, package ``gfn``) in numpy, in the dtype of its inputs
+(float32 for parity, float64 for drift references), keeping the reference's
+order of operations so that float32 results round the same way wherever the
+reference does elementwise work.  Citations are ``gfn/<file>:<line>``.
+
+Parity pin: the reference's own tests hold no golden vectors for this path,
+so this restatement is pinned against fixtures produced by running the
+reference itself (``tests/golden/make_golden.py`` imports ``gfn`` and records
+its outputs on seeded inputs); ``tests/test_oracle_golden.py`` checks it.
+
+Canonical parameter layout (numpy arrays), one dict per layer::
+
+    U, W      [H, hd, r]    low-rank Christoffel factors   (gfn/geometry/lowrank.py:31-32)
+    Wf        [H, hd, hd]   forget_gate.weight, [out, in]  (gfn/geometry/lowrank.py:47)
+    bf        [H, hd]       forget_gate.bias
+    dt_params [H]           raw per-head dt parameters     (gfn/layers/base.py:132-139)
+    Wx, Wv    [d, d]        out_proj_{x,v}.weight, [out,in] (gfn/layers/base.py:181-182)
+    bx, bv    [d]           out_proj_{x,v}.bias
+    gx, gv    [d]           mixed_norm_{x,v}.weight        (gfn/layers/base.py:185-186)
+"""
+import numpy as np
+
+# torch.finfo(torch.float32).eps -- nn.RMSNorm(eps=None) uses the input
+# dtype's machine epsilon (gfn/layers/base.py:185-186).
+def _rms_eps(dtype):
+    return np.finfo(dtype).eps
+
+
+def softplus(x):
+    """torch.nn.functional.softplus with beta=1, threshold=20."""
+    x = np.asarray(x)
+    return np.where(x > 20, x, np.log1p(np.exp(np.minimum(x, 20)))).astype(x.dtype)
+
+
+def sigmoid(x):
+    return (1.0 / (1.0 + np.exp(-x))).astype(x.dtype)
+
+
+def christoffel(v, U, W):
+    """Low-rank Christoffel contraction Gamma(v, v).
+
+    gfn/geometry/lowrank.py:93-98 (proj, norm, scale, sq, gamma) and the soft
+    clamp 20*tanh(gamma/20) applied when friction is returned separately
+    (gfn/geometry/lowrank.py:125-127).  v: [B, hd]; U, W: [hd, r].
+    """
+    dt = v.dtype
+    one = dt.type(1.0)
+    proj = v @ U                                              # [B, r]
+    norm = np.sqrt(np.sum(proj * proj, axis=-1, keepdims=True))
+    scale = one / ((one + norm) + dt.type(1e-6))
+    sq = (proj * proj) * scale
+    gamma = sq @ W.T                                          # [B, hd]
+    return dt.type(20.0) * np.tanh(gamma / dt.type(20.0))
+
+
+def friction(x, Wf, bf):
+    """mu = 5 * sigmoid(x Wf^T + bf)  (gfn/integrators/symplectic/leapfrog.py:72-81)."""
+    gate = (x @ Wf.T) + bf
+    return sigmoid(gate) * x.dtype.type(5.0)
+
+
+def leapfrog_head_step(x, v, F, U, W, Wf, bf, dt, dt_scale, steps=1):
+    """One head's kick-drift-kick with implicit friction.
+
+    gfn/integrators/symplectic/leapfrog.py:50-114 (steps loop, h = dt*scale/2,
+    v_half = (v + h(F - G(v)))/(1 + h mu(x)), x += dt_eff v_half,
+    v = (v_half + h(F - G(v_half)))/(1 + h mu(x'))).  Euclidean boundary is
+    the identity (gfn/geometry/boundaries.py:4-17).
+    """
+    dtp = x.dtype.type
+    eff = dtp(dt) * dtp(dt_scale)
+    h = dtp(0.5) * eff
+    one = dtp(1.0)
+    for _ in range(steps):
+        g0 = christoffel(v, U, W)
+        mu0 = friction(x, Wf, bf)
+        v_half = (v + h * (F - g0)) / (one + h * mu0)
+        x = x + eff * v_half
+        g1 = christoffel(v_half, U, W)
+        mu1 = friction(x, Wf, bf)
+        v = (v_half + h * (F - g1)) / (one + h * mu1)
+    return x, v
+
+
+def rmsnorm(y, g):
+    """torch.nn.RMSNorm(d, eps=None): y * rsqrt(mean(y^2) + eps) * g."""
+    dt = y.dtype
+    ms = np.mean(y * y, axis=-1, keepdims=True)
+    return (y * (dt.type(1.0) / np.sqrt(ms + dt.type(_rms_eps(dt))))) * g
+
+
+def mlayer_step(x, v, F, lp, heads, base_dt):
+    """MLayer.forward for the Euclidean leapfrog configuration.
+
+    gfn/layers/base.py:198-338: split heads (:209-217), dt scale =
+    softplus(dt_params) (:220,231), per-head integrator (:276-290), concat,
+    x' = RMSNorm(out_proj_x(x)), v' = RMSNorm(out_proj_v(v)) (:305-330) when
+    heads > 1, then v' = 100 tanh(v'/100) (:335).
+    """
+    B, d = x.shape
+    hd = d // heads
+    dtp = x.dtype.type
+    scale = softplus(lp["dt_params"].astype(x.dtype))
+    xo = np.empty_like(x)
+    vo = np.empty_like(v)
+    for h in range(heads):
+        sl = slice(h * hd, (h + 1) * hd)
+        xh, vh = leapfrog_head_step(x[:, sl], v[:, sl], F[:, sl], lp["U"][h], lp["W"][h],
+                                    lp["Wf"][h], lp["bf"][h], base_dt, scale[h])
+        xo[:, sl] = xh
+        vo[:, sl] = vh
+    if heads > 1:
+        xn = rmsnorm(xo @ lp["Wx"].T + lp["bx"], lp["gx"])
+        vn = rmsnorm(vo @ lp["Wv"].T + lp["bv"], lp["gv"])
+    else:
+        xn, vn = xo, vo
+    vn = dtp(100.0) * np.tanh(vn / dtp(100.0))
+    return xn, vn
+
+
+def manifold_forward(x0, v0, forces, layers, heads, base_dt, mask=None):
+    """Manifold.forward loop path without readout.
+
+    gfn/model.py:377-402: for each token t, force = F[:, t] * mask[:, t], then
+    every layer in order; x_seq/v_seq collect the state after the last layer.
+    x0, v0: [B, d]; forces: [B, L, d].  Returns (x_seq, v_seq, x, v).
+    """
+    B, L, d = forces.shape
+    x, v = x0.copy(), v0.copy()
+    xs = np.empty((B, L, d), x0.dtype)
+    vs = np.empty((B, L, d), x0.dtype)
+    for t in range(L):
+        F = forces[:, t]
+        if mask is not None:
+            F = F * mask[:, t, None].astype(F.dtype)
+        for lp in layers:
+            x, v = mlayer_step(x, v, F, lp, heads, base_dt)
+        xs[:, t] = x
+        vs[:, t] = v
+    return xs, vs, x, v
+
+
+def embedding_lookup(ids, table):
+    """nn.Embedding forward (gfn/model.py:55, 163)."""
+    return table[ids]
+
+
+def functional_embedding(ids, fp, coord_dim=16, omega_0=30.0):
+    """FunctionalEmbedding(mode='binary') forward (gfn/embeddings.py:171-206).
+
+    bits of the id -> {-1, 1} coords -> SIREN (sin(omega_0 * Linear)) x 3 ->
+    out_proj -> * impulse_scale -> zero for id 0.  fp holds W0,b0,W1,b1,W2,b2
+    (SineLayer linears, gfn/embeddings.py:24-49), Wo, bo, impulse.
+    """
+    dt = fp["Wo"].dtype
+    mask = (1 << np.arange(coord_dim)).astype(np.int64)
+    bits = (ids[..., None].astype(np.int64) & mask) > 0
+    coords = bits.astype(dt) * dt.type(2) - dt.type(1)
+    h = coords
+    for i in range(3):
+        h = np.sin(dt.type(omega_0) * (h @ fp[f"W{i}"].T + fp[f"b{i}"]))
+    out = (h @ fp["Wo"].T + fp["bo"]) * fp["impulse"]
+    active = (bits.astype(dt).sum(-1, keepdims=True) > 0).astype(dt)
+    return out * active
+
+
+# ----------------------------------------------------------------------------
+# Parallel-scan path
+# ----------------------------------------------------------------------------
+
+def scan_sequential(a, x):
+    """y_t = a_t y_{t-1} + x_t, y_{-1} = 0 (gfn/scan.py:56-63)."""
+    B, L, D = x.shape
+    y = np.empty_like(x)
+    hcur = np.zeros((B, D), x.dtype)
+    for t in range(L):
+        hcur = a[:, t] * hcur + x[:, t]
+        y[:, t] = hcur
+    return y
+
+
+def parallel_scan(a, x):
+    """gfn.scan.parallel_scan: sequential for L < 32, else Hillis-Steele
+    doubling with (a2,x2)o(a1,x1) = (a2 a1, a2 x1 + x2) (gfn/scan.py:52-104)."""
+    B, L, D = x.shape
+    if L < 32:
+        return scan_sequential(a, x)
+    ca, cx = a.copy(), x.copy()
+    steps = int(np.ceil(np.log2(L)))
+    for i in range(steps):
+        s = 2 ** i
+        na = ca.copy()
+        nx = cx.copy()
+        na[:, s:] = ca[:, s:] * ca[:, :-s]
+        nx[:, s:] = ca[:, s:] * cx[:, :-s] + cx[:, s:]
+        ca, cx = na, nx
+    return cx
+
+
+def layernorm(x, w, b, eps=1e-5):
+    mu = np.mean(x, axis=-1, keepdims=True)
+    var = np.mean((x - mu) ** 2, axis=-1, keepdims=True)
+    return (x - mu) / np.sqrt(var + x.dtype.type(eps)) * w + b
+
+
+def parallel_mlayer(force, pp, heads, scan=parallel_scan):
+    """ParallelMLayer.forward(None, None, force) (gfn/layers/parallel.py:75-125).
+
+    force = LayerNorm(force); A = sigmoid(to_A(force)); dt = softplus(to_dt(force))
+    * 0.1 * 1.5^head; B = to_B(force) * dt; v = scan(A, B); x = scan(1, v * dt).
+    pp: ln_w, ln_b, WA, bA, Wdt, bdt, WB, bB.  Returns (x_seq, v_seq).
+    """
+    dtp = force.dtype.type
+    B_, L, D = force.shape
+    f = layernorm(force, pp["ln_w"], pp["ln_b"])
+    A = sigmoid(f @ pp["WA"].T + pp["bA"])
+    scales = np.repeat(np.array([1.5 ** i for i in range(heads)], force.dtype), D // heads)
+    dt = softplus(f @ pp["Wdt"].T + pp["bdt"]) * dtp(0.1) * scales
+    Bv = (f @ pp["WB"].T + pp["bB"]) * dt
+    v_seq = scan(A, Bv)
+    x_seq = scan(np.ones_like(v_seq), v_seq * dt)
+    return x_seq, v_seq
+
+
+def manifold_scan_forward(forces, players, heads, scan=parallel_scan):
+    """Manifold(use_scan=True) recurrence part (gfn/model.py:171-182): each
+    layer's x_seq is the next layer's force.  Returns the last layer's x_seq."""
+    cur = forces
+    for pp in players:
+        cur, _ = parallel_mlayer(cur, pp, heads, scan)
+    return cur

@@ -1,0 +1,95 @@
+"""Pin the numpy oracle against fixtures recorded from the reference itself.
+
+CPU only.  Tolerances are the per-step fp32 parity bar (1e-5 relative,
+1e-6 absolute) scaled for sequence length where states compound.
+"""
+import os
+
+import numpy as np
+import pytest
+
+from oracle import gfn_oracle as O
+from tests.golden import cases as C
+from tests.parity import rowwise_close
+
+GOLD = os.path.join(os.path.dirname(__file__), "golden")
+
+
+def load(name):
+    return dict(np.load(os.path.join(GOLD, f"{name}.npz")))
+
+
+def close(a, b, rtol, atol):
+    np.testing.assert_allclose(a, b, rtol=rtol, atol=atol)
+
+
+SMALL = ["tiny", "h1", "mask", "c1", "c2s", "c3s", "c4s", "c5s"]
+
+
+@pytest.mark.parametrize("name", SMALL)
+def test_oracle_sequence_matches_reference(name):
+    cfg = C.CASES[name]
+    P = C.make_params(cfg)
+    g = load(name)
+    F = C.oracle_forces(P, g["ids"])
+    B = cfg["B"]
+    x0 = np.broadcast_to(P["x0"], (B, cfg["d"])).copy()
+    v0 = np.broadcast_to(P["v0"], (B, cfg["d"])).copy()
+    xs, vs, x, v = O.manifold_forward(x0, v0, F, P["layers"], cfg["H"], cfg["dt"], g.get("mask"))
+    close(xs, g["x_seq"], 1e-4, 1e-5)
+    close(vs, g["v_seq"], 1e-4, 1e-5)
+    close(x, g["x_final"], 1e-4, 1e-5)
+    close(v, g["v_final"], 1e-4, 1e-5)
+
+
+def test_oracle_fp64_tracks_reference_fp64():
+    cfg = C.CASES["tiny"]
+    P = C.make_params(cfg)
+    g = load("tiny")
+    P64 = dict(x0=P["x0"].astype(np.float64), v0=P["v0"].astype(np.float64),
+               layers=[{k: a.astype(np.float64) for k, a in lp.items()} for lp in P["layers"]])
+    F = P["emb"].astype(np.float64)[g["ids"]]
+    B, d = cfg["B"], cfg["d"]
+    xs, vs, _, _ = O.manifold_forward(np.broadcast_to(P64["x0"], (B, d)).copy(),
+                                      np.broadcast_to(P64["v0"], (B, d)).copy(),
+                                      F, P64["layers"], cfg["H"], cfg["dt"])
+    close(xs, g["x_seq64"], 1e-10, 1e-12)
+    close(vs, g["v_seq64"], 1e-10, 1e-12)
+
+
+@pytest.mark.parametrize("name", ["c2s", "c3s", "c4s"])
+def test_oracle_layer_step_matches_reference(name):
+    cfg = C.CASES[name]
+    g = load(name)
+    P = C.make_params(cfg)
+    lp = P["layers"][int(g["step_layer"])]
+    xo, vo = O.mlayer_step(g["step_x"], g["step_v"], g["step_F"], lp, cfg["H"], cfg["dt"])
+    rowwise_close(xo, g["step_xo"], what="x")
+    rowwise_close(vo, g["step_vo"], what="v")
+
+
+def test_oracle_functional_embedding_matches_reference():
+    cfg = C.CASES["c3s"]
+    P = C.make_params(cfg)
+    g = load("c3s")
+    F = O.functional_embedding(g["ids"], P["func"])
+    close(F, g["forces"], 1e-5, 1e-6)
+
+
+def test_oracle_units_match_reference():
+    g = load("units")
+    gam = O.christoffel(g["ch_v"], g["ch_U"], g["ch_W"])
+    close(gam, g["ch_gamma"], 1e-5, 1e-6)
+    xn, vn = O.leapfrog_head_step(g["lf_x"], g["ch_v"], g["lf_F"], g["ch_U"], g["ch_W"],
+                                  g["lf_Wf"], g["lf_bf"], 0.1, g["lf_scale"], steps=3)
+    close(xn, g["lf_xn"], 1e-5, 1e-6)
+    close(vn, g["lf_vn"], 1e-5, 1e-6)
+    for L in (20, 100):
+        y = O.parallel_scan(g[f"scan{L}_a"], g[f"scan{L}_x"])
+        close(y, g[f"scan{L}_y"], 1e-5, 1e-6)
+        ys = O.scan_sequential(g[f"scan{L}_a"].astype(np.float64), g[f"scan{L}_x"].astype(np.float64))
+        close(ys, g[f"scan{L}_y"], 1e-5, 1e-5)
+    pp = {k[3:]: g[k] for k in g if k.startswith("pl_") and k not in ("pl_f", "pl_x", "pl_v")}
+    xs, vs = O.parallel_mlayer(g["pl_f"], pp, heads=4)
+    close(xs, g["pl_x"], 1e-5, 1e-5)
+    close(vs, g["pl_v"], 1e-5, 1e-5)
