@@ -73,7 +73,6 @@ int make_layout(int d, int H, int r, int NL, Layout* L) {
     return fail(GFN_ERR_UNSUPPORTED, "per-head rank %d not in {4, 8, 16}", r);
   int K = 1;
   while (K * 2 <= 8 && H % (K * 2) == 0) K *= 2;
-  if (d >= 1024 && H % 16 == 0) K = 16;
   L->d = d; L->H = H; L->hd = hd; L->r = r; L->NL = NL;
   L->K = K; L->C = d / K; L->hpc = H / K;
   L->mix = H > 1;
