@@ -185,6 +185,8 @@ def run_ours(args, c):
     for i in range(warm):
         state = step(i, state)
     torch.cuda.synchronize(dev)
+    if args.phase_profile:
+        return phase_profile(step, warm, state, dev)
     # kernel-level event timing of the sequence kernel: per step, L2 flushed between
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
     sampler = ClockSampler(local) if rank == 0 else None
@@ -278,6 +280,25 @@ def run_ours(args, c):
     return result
 
 
+def phase_profile(step, i, state, dev):
+    """Cycles per layer step spent in each phase by CTA 0 (clock64 counters)."""
+    import ctypes
+    import torch
+    from manifold_b200 import _lib
+    buf = torch.zeros(12, dtype=torch.int64, device=dev)
+    _lib.call("gfn_debug_set_phase_profile", ctypes.c_void_p(buf.data_ptr()))
+    step(i, state)
+    torch.cuda.synchronize(dev)
+    _lib.call("gfn_debug_set_phase_profile", None)
+    v = buf.tolist()
+    n = max(1, v[11])
+    names = ["head_wait", "head_step_and_send", "exchange_wait", "mixing", "reduce_and_sync",
+             "norm_exchange", "norm", "token_io"]
+    out = {nm: round(v[k] / n, 1) for k, nm in enumerate(names)}
+    out["total"] = round(sum(v[:8]) / n, 1)
+    return {"phase_cycles_per_layer_step": out, "layer_steps": n}
+
+
 def cpu_baseline(c, tokens):
     """The numpy port of the reference algorithm (oracle/) on the host cores,
     on a bounded sample of the same workload."""
@@ -335,6 +356,8 @@ def main():
     ap.add_argument("--chunk", type=int, default=0, help="tokens per step (default per config)")
     ap.add_argument("--cpu-tokens", type=int, default=0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--phase-profile", action="store_true",
+                    help="print per-phase cycle counts of CTA 0 for one step instead")
     args = ap.parse_args()
     c = CONFIGS[args.config]
     if args.impl == "reference":

@@ -126,10 +126,17 @@ int gfn_leapfrog_pack(const float* U_stack, const float* W_stack, const float* W
                       const float* mix_v_b, const float* norm_v_w, int dim, int heads, int rank,
                       int num_layers, float* packed, long long packed_floats, gfn_stream_t stream);
 
+/* Testing/profiling aid: when device_counters (12 int64 on the device) is
+ * non-NULL, later sequence launches record per-phase clock64 cycle totals
+ * of CTA 0 there (head wait, head step + sends, exchange wait, mixing,
+ * reduction, norm exchange, norm, token I/O, unused x3, layer steps).
+ * NULL turns it off.  Not thread-safe; no reference counterpart. */
+int gfn_debug_set_phase_profile(long long* device_counters);
+
 /* Launch plan the sequence kernel would use for `batch` rows:
- * out[0..5] = cluster size K, rows per cluster, clusters, shared bytes,
- * k-chunk, ring slots. */
-int gfn_leapfrog_plan(int batch, int dim, int heads, int rank, int num_layers, int* out6);
+ * out[0..7] = cluster size K, rows per cluster, clusters, shared bytes,
+ * k-chunk, ring slots, max co-resident clusters, k-split lanes. */
+int gfn_leapfrog_plan(int batch, int dim, int heads, int rank, int num_layers, int* out8);
 
 /* ------------------------------------------------------------------------
  * y_t = a_t y_{t-1} + x_t along t of [batch, seq_len, dim] (a NULL: a == 1).

@@ -32,6 +32,7 @@ _SIGS = {
     "gfn_leapfrog_pack_floats": [_i, _i, _i, _i],
     "gfn_leapfrog_pack": [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i, _i, _i, _i, _p, _ll, _p],
     "gfn_leapfrog_plan": [_i, _i, _i, _i, _i, _p],
+    "gfn_debug_set_phase_profile": [_p],
     "gfn_parallel_scan_workspace_floats": [_i, _i, _i],
     "gfn_parallel_scan": [_p, _p, _p, _p, _ll, _i, _i, _i, _p],
     "gfn_parallel_layer_scan": [_p, _p, _p, _i, _i, _i, _i, _f, _p],

@@ -62,7 +62,7 @@ GFN_DEV bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 GFN_DEV bool mbar_wait(uint64_t* bar, uint32_t parity) {
   for (uint32_t i = 0; i < (1u << 22); ++i) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (i > 64) __nanosleep(256);
+    if (i > 1024) __nanosleep(64);
   }
   gfn_flag_error(kDevErrMbarTimeout);
   return false;

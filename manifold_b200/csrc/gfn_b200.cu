@@ -16,6 +16,7 @@ using namespace gfn;
 namespace {
 
 thread_local char g_msg[512] = "";
+long long* g_phase_prof = nullptr;  // gfn_debug_set_phase_profile
 
 int fail(int status, const char* fmt, ...) {
   va_list ap;
@@ -68,7 +69,8 @@ int make_layout(int d, int H, int r, int NL, Layout* L) {
   if (d <= 0 || H <= 0 || r <= 0 || NL <= 0 || d % H != 0)
     return fail(GFN_ERR_INVALID, "bad shape dim=%d heads=%d rank=%d layers=%d", d, H, r, NL);
   const int hd = d / H;
-  if (hd % 4 != 0) return fail(GFN_ERR_UNSUPPORTED, "head_dim %d must be a multiple of 4", hd);
+  if (hd % 4 != 0 || hd > 128)
+    return fail(GFN_ERR_UNSUPPORTED, "head_dim %d must be a multiple of 4 and <= 128", hd);
   if (r != 4 && r != 8 && r != 16)
     return fail(GFN_ERR_UNSUPPORTED, "per-head rank %d not in {4, 8, 16}", r);
   int K = 1;
@@ -82,7 +84,7 @@ int make_layout(int d, int H, int r, int NL, Layout* L) {
   while (d % KC) --KC;
   L->KC = KC;
   L->nchunk = L->mix ? d / KC : 0;
-  L->CF = KC * 2 * L->C;
+  L->CF = KC * chunk_row_stride(L->C);
   L->HS = head_offsets(L->hpc, hd, r, L->C).total;
   L->LF = (long long)L->HS + (long long)L->nchunk * L->CF;
   return GFN_OK;
@@ -90,9 +92,9 @@ int make_layout(int d, int H, int r, int NL, Layout* L) {
 
 struct SeqPlan {
   Layout L;
-  int R, TR, NG, tiles, S, NST, nclusters;
+  int R, TR, NG, tiles, S, NST, nclusters, max_active;
   size_t smem;
-  int o_head, o_chunk, o_xs, o_vs, o_ox, o_ov, o_catx, o_catv, o_part, o_p, o_red;
+  int o_head, o_chunk, o_ox, o_ov, o_catx, o_catv, o_part;
 };
 
 size_t plan_smem(const Layout& L, int R, int NST, SeqPlan* p) {
@@ -100,71 +102,115 @@ size_t plan_smem(const Layout& L, int R, int NST, SeqPlan* p) {
   auto take = [&](int n) { int o = off; off += ((n + 31) / 32) * 32; return o; };
   p->o_head = take(2 * L.HS);
   p->o_chunk = take(L.mix ? NST * L.CF : 0);
-  p->o_xs = take(R * L.C);
-  p->o_vs = take(R * L.C);
   p->o_ox = take(L.mix ? R * L.C : 0);
   p->o_ov = take(L.mix ? R * L.C : 0);
   p->o_catx = take(L.mix ? R * L.d : 0);
   p->o_catv = take(L.mix ? R * L.d : 0);
   p->o_part = take(L.mix ? L.K * R * 2 : 0);
-  p->o_p = take(R * L.hpc * L.r);
-  p->o_red = take(L.mix ? SEQ_RED_FLOATS : 0);
-  return 128 + (size_t)off * 4;
+  return SEQ_BAR_BYTES + (size_t)off * 4;
 }
 
-int make_plan(int B, const Layout& L, const DevInfo& di, SeqPlan* p) {
-  p->L = L;
-  const int per_wave = di.sms / L.K > 0 ? di.sms / L.K : 1;
-  int want = (B + per_wave - 1) / per_wave;
-  int R = 1;
-  while (R < want) R *= 2;
-  int rb = 1;  // smallest pow2 >= B
-  while (rb < B) rb *= 2;
-  if (R > rb) R = rb;
-  for (; R >= 1; R /= 2) {
-    if (R * L.C > SEQ_THREADS * SEQ_OPT) continue;
-    const int TR = R < 4 ? R : 4;
-    const int NG = 2 * L.C / 4;
-    const int tiles = NG * (R / TR);
-    if (L.mix && tiles > SEQ_THREADS) continue;
-    for (int NST = 4; NST >= 2; --NST) {
-      const size_t smem = plan_smem(L, R, NST, p);
-      if (smem <= (size_t)di.max_smem) {
-        p->R = R; p->TR = TR; p->NG = NG; p->tiles = L.mix ? tiles : 1;
-        int S = 1;
-        while (L.mix && S * 2 * tiles <= SEQ_THREADS) S *= 2;
-        p->S = S;
-        p->NST = NST;
-        p->smem = smem;
-        p->nclusters = (B + R - 1) / R;
-        return GFN_OK;
-      }
-    }
-  }
-  return fail(GFN_ERR_RESOURCES, "no sequence plan fits %d bytes of shared memory", di.max_smem);
+// The kernel instance for (rank, elements per lane).
+using SeqKernel = void (*)(SeqArgs);
+
+SeqKernel seq_kernel_for(int r, int epl) {
+#define GFN_K(RK, E) if (r == RK && epl == E) return leapfrog_seq_kernel<RK, E>;
+  GFN_K(4, 1) GFN_K(4, 2) GFN_K(4, 4) GFN_K(8, 1) GFN_K(8, 2) GFN_K(8, 4)
+  GFN_K(16, 1) GFN_K(16, 2) GFN_K(16, 4)
+#undef GFN_K
+  return nullptr;
 }
 
-template <int RK>
-int launch_seq(const SeqArgs& a, const SeqPlan& p, cudaStream_t stream) {
-  auto kern = leapfrog_seq_kernel<RK>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.smem);
-  if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(smem)");
-  if (p.L.K > 8) {
-    e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
-    if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(cluster)");
-  }
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)(p.nclusters * p.L.K));
-  cfg.blockDim = dim3(SEQ_THREADS);
-  cfg.dynamicSmemBytes = p.smem;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+int seq_epl(const Layout& L) { return L.hd <= 32 ? 1 : L.hd <= 64 ? 2 : 4; }
+
+// Row-block geometry for R rows: mixing tiles and the split-K factor.
+bool plan_rows(const Layout& L, int R, SeqPlan* p) {
+  if (R < 1 || R * L.hpc > SEQ_CWARPS * SEQ_MAXU) return false;
+  const int TR = R < 4 ? R : 4;
+  const int NG = 2 * L.C / 4;
+  const int tiles = NG * ((R + TR - 1) / TR);
+  if (L.mix && tiles > SEQ_CTHREADS) return false;
+  p->R = R; p->TR = TR; p->NG = NG; p->tiles = L.mix ? tiles : 1;
+  int S = 1;
+  while (L.mix && S < 16 && S * 2 * tiles <= SEQ_CTHREADS) S *= 2;
+  p->S = S;
+  return true;
+}
+
+int set_cluster_cfg(cudaLaunchConfig_t* cfg, cudaLaunchAttribute* attr, const SeqPlan& p) {
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = p.L.K;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg->blockDim = dim3(SEQ_THREADS);
+  cfg->dynamicSmemBytes = p.smem;
+  cfg->attrs = attr;
+  cfg->numAttrs = 1;
+  return GFN_OK;
+}
+
+int query_active_clusters(SeqKernel kern, const SeqPlan& p, int* out) {
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.smem);
+  if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(smem)");
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  set_cluster_cfg(&cfg, attr, p);
+  cfg.gridDim = dim3((unsigned)p.L.K);
+  e = cudaOccupancyMaxActiveClusters(out, kern, &cfg);
+  if (e != cudaSuccess) return cuda_status(e, "cudaOccupancyMaxActiveClusters");
+  return GFN_OK;
+}
+
+// Chooses rows per cluster R so that all ceil(B / R) clusters are resident
+// at once: a persistent cluster left for a second wave doubles the time.
+int make_plan(int B, const Layout& L, const DevInfo& di, SeqPlan* p) {
+  p->L = L;
+  SeqKernel kern = seq_kernel_for(L.r, seq_epl(L));
+  if (!kern) return fail(GFN_ERR_UNSUPPORTED, "no kernel for rank %d head_dim %d", L.r, L.hd);
+  auto fit = [&](int R) -> bool {
+    if (!plan_rows(L, R, p)) return false;
+    for (int NST = SEQ_MAX_NST < 6 ? SEQ_MAX_NST : 6; NST >= 2; --NST) {
+      const size_t smem = plan_smem(L, R, NST, p);
+      if (smem <= (size_t)di.max_smem) {
+        p->NST = NST;
+        p->smem = smem;
+        return true;
+      }
+    }
+    return false;
+  };
+  int Rmax = 0;
+  for (int R = 1; R <= B && R <= SEQ_CWARPS * SEQ_MAXU; ++R)
+    if (fit(R)) Rmax = R;
+  if (Rmax == 0)
+    return fail(GFN_ERR_RESOURCES, "no sequence plan fits %d bytes of shared memory", di.max_smem);
+  const int per_wave = di.sms / L.K > 0 ? di.sms / L.K : 1;
+  int R = (B + per_wave - 1) / per_wave;
+  if (R < 1) R = 1;
+  if (R > Rmax) R = Rmax;
+  for (int it = 0; it < 8; ++it) {
+    if (!fit(R)) return fail(GFN_ERR_RESOURCES, "sequence plan for %d rows does not fit", R);
+    int active = 0;
+    const int st = query_active_clusters(kern, *p, &active);
+    if (st) return st;
+    p->max_active = active;
+    if (active <= 0) return fail(GFN_ERR_RESOURCES, "a %d-CTA cluster cannot be scheduled", L.K);
+    const int need = (B + active - 1) / active;
+    if (need <= R || R == Rmax) break;
+    R = need < Rmax ? need : Rmax;
+  }
+  p->nclusters = (B + p->R - 1) / p->R;
+  return GFN_OK;
+}
+
+int launch_seq(SeqKernel kern, const SeqArgs& a, const SeqPlan& p, cudaStream_t stream) {
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.smem);
+  if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(smem)");
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  set_cluster_cfg(&cfg, attr, p);
+  cfg.gridDim = dim3((unsigned)(p.nclusters * p.L.K));
+  cfg.stream = stream;
   e = cudaLaunchKernelEx(&cfg, kern, a);
   return cuda_status(e, "leapfrog_seq_kernel launch");
 }
@@ -274,13 +320,19 @@ int gfn_leapfrog_fused(const float* x, const float* v, const float* f, const flo
   return launch_status("leapfrog_head_kernel");
 }
 
+int gfn_debug_set_phase_profile(long long* device_counters) {
+  g_phase_prof = device_counters;
+  return GFN_OK;
+}
+
 long long gfn_leapfrog_pack_floats(int dim, int heads, int rank, int num_layers) {
   Layout L;
   if (make_layout(dim, heads, rank, num_layers, &L) != GFN_OK) return -1;
   return (long long)num_layers * L.K * L.LF;
 }
 
-int gfn_leapfrog_plan(int batch, int dim, int heads, int rank, int num_layers, int* out6) {
+int gfn_leapfrog_plan(int batch, int dim, int heads, int rank, int num_layers, int* out8) {
+  int* out6 = out8;
   if (!out6) return fail(GFN_ERR_INVALID, "plan: out6 NULL");
   Layout L;
   int st = make_layout(dim, heads, rank, num_layers, &L);
@@ -292,7 +344,7 @@ int gfn_leapfrog_plan(int batch, int dim, int heads, int rank, int num_layers, i
   st = make_plan(batch > 0 ? batch : 1, L, di, &p);
   if (st) return st;
   out6[0] = L.K; out6[1] = p.R; out6[2] = p.nclusters; out6[3] = (int)p.smem;
-  out6[4] = L.KC; out6[5] = p.NST;
+  out6[4] = L.KC; out6[5] = p.NST; out6[6] = p.max_active; out6[7] = p.S;
   return GFN_OK;
 }
 
@@ -359,16 +411,11 @@ int gfn_leapfrog_sequence_forward(const float* x_init, const float* v_init,
   a.B = batch; a.L = seq_len; a.d = dim; a.H = heads; a.hd = L.hd; a.NL = num_layers;
   a.K = L.K; a.R = p.R; a.C = L.C; a.hpc = L.hpc; a.KC = L.KC; a.nchunk = L.nchunk; a.NST = p.NST;
   a.HS = L.HS; a.CF = L.CF; a.LF = L.LF; a.mix = L.mix;
-  a.TR = p.TR; a.NG = p.NG; a.tiles = p.tiles; a.S = p.S; a.base_dt = base_dt;
-  a.o_head = p.o_head; a.o_chunk = p.o_chunk; a.o_xs = p.o_xs; a.o_vs = p.o_vs; a.o_ox = p.o_ox;
-  a.o_ov = p.o_ov; a.o_catx = p.o_catx; a.o_catv = p.o_catv; a.o_part = p.o_part; a.o_p = p.o_p;
-  a.o_red = p.o_red;
-  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  switch (rank) {
-    case 4: return launch_seq<4>(a, p, s);
-    case 8: return launch_seq<8>(a, p, s);
-    default: return launch_seq<16>(a, p, s);
-  }
+  a.TR = p.TR; a.NG = p.NG; a.tiles = p.tiles; a.S = p.S;
+  a.base_dt = base_dt; a.prof = g_phase_prof;
+  a.o_head = p.o_head; a.o_chunk = p.o_chunk; a.o_ox = p.o_ox; a.o_ov = p.o_ov;
+  a.o_catx = p.o_catx; a.o_catv = p.o_catv; a.o_part = p.o_part;
+  return launch_seq(seq_kernel_for(rank, seq_epl(L)), a, p, reinterpret_cast<cudaStream_t>(stream));
 }
 
 long long gfn_parallel_scan_workspace_floats(int batch, int seq_len, int dim) {

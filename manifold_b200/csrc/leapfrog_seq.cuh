@@ -1,5 +1,5 @@
 // Persistent fused leapfrog recurrence: all tokens x all layers x all heads in
-// one launch, (x, v) resident in shared memory for the whole sequence.
+// one launch, (x, v) resident on chip for the whole sequence.
 //
 // Semantics (one layer step, Euclidean, leapfrog, per head of width hd):
 //   Gamma(v) = 20 tanh(((vU)^2 / (1 + |vU| + 1e-6)) W^T / 20)   gfn/geometry/lowrank.py:93-98,125-127
@@ -14,35 +14,48 @@
 // and the token loop with F_t = F[:, t] * mask[:, t]              gfn/model.py:377-402.
 //
 // Decomposition.  A thread-block cluster of K CTAs owns a block of R batch
-// rows for the whole sequence.  CTA c of the cluster owns C = d/K columns,
-// i.e. hpc = H/K whole heads, of every layer.  Per layer step:
-//   1. head step for its heads on its R rows (all operands in SMEM);
-//   2. DSMEM all-gather of (x', v') so every CTA holds the R x d concat;
-//   3. mixing GEMM for its C output columns of both x and v, split-K over
-//      the 256 threads, weights streamed as k-chunks by the bulk-copy engine
-//      through a ring of NST shared-memory slots, issued NST chunks ahead
-//      (they do not depend on the data, so the copy of layer l+1's weights
-//      overlaps layer l's math);
-//   4. DSMEM exchange of per-row partial sums of squares -> RMSNorm,
-//      saturation; the CTA now holds its columns of the next layer's input.
-// Two cluster barriers per layer step; no grid-wide synchronisation (rows
-// are independent), no atomics (bitwise-deterministic for a fixed plan).
+// rows for the whole sequence.  CTA c owns C = d/K columns (hpc = H/K whole
+// heads) of every layer.  Inside the CTA a "unit" is one (row, head): warp w
+// owns units w, w+8, ..., and lane l holds elements l, l+32, ... of each
+// unit's x, v and force in registers across all layers and tokens.
+// Per layer step:
+//   1. head step of each unit entirely in registers: the v.U projection is
+//      a warp butterfly, the friction GEMV broadcasts x by shuffles and reads
+//      the forget-gate weight from shared memory -- no block barrier;
+//   2. all-gather of (x', v'): every unit st.async-stores its columns into
+//      every peer's concat buffer; the stores complete on the receiver's
+//      mbarrier (transaction bytes), so no cluster barrier and no fence;
+//   3. mixing for the CTA's 2C output columns (x and v), split-K over the
+//      256 compute threads, k-vectorised, partials combined by a warp
+//      reduce-scatter; weights stream through a ring of shared-memory slots
+//      filled by a producer warp with 1-D bulk copies (independent of the
+//      data, so layer l+1's copies overlap layer l's math);
+//   4. one block barrier, per-row sums of squares exchanged like step 2,
+//      RMSNorm and saturation applied by each unit in registers.
+// No grid-wide synchronisation (rows are independent) and no atomics: for a
+// fixed launch plan the result is bitwise deterministic.
 #pragma once
 #include "common.cuh"
 
 namespace gfn {
 
-constexpr int SEQ_THREADS = 256;
-constexpr int SEQ_OPT = 4;          // head-step outputs per thread: R*C <= 1024
-constexpr int SEQ_RED_FLOATS = 4096;  // split-K partials: S*R*2C <= 256*16
+constexpr int SEQ_CWARPS = 8;
+constexpr int SEQ_CTHREADS = SEQ_CWARPS * 32;       // compute threads
+constexpr int SEQ_THREADS = SEQ_CTHREADS + 32;      // + one producer warp
+constexpr int SEQ_MAXU = 2;                         // units per warp: R*hpc <= 16
+// (9 warps put 3 on one SM sub-partition: 168 registers per thread at most)
+constexpr int SEQ_NBAR = 24;                        // mbarrier slots reserved
+constexpr int SEQ_BAR_BYTES = SEQ_NBAR * 8;
+constexpr int SEQ_MAX_NST = (SEQ_NBAR - 6) / 2;     // ring depth limit
+constexpr int SEQ_PROF_N = 12;
 
 struct HeadOffsets {
-  int WfT, U, W, bf, bx, bv, gx, gv, dt, total;
+  int WfT, U, W, bf, bx, bv, gx, gv, sc, total;
 };
 
 // Per-(layer, CTA) "head section" of the packed weights, in floats.
-// WfT is the forget-gate weight transposed to [hpc][k][j] so that the
-// threads of a warp (consecutive j) read consecutive words.
+// WfT is the forget-gate weight transposed to [hpc][k][j] so that lanes
+// with consecutive j read consecutive words; sc = softplus(dt_params).
 __host__ __device__ inline HeadOffsets head_offsets(int hpc, int hd, int r, int C) {
   HeadOffsets o;
   o.WfT = 0;
@@ -53,10 +66,14 @@ __host__ __device__ inline HeadOffsets head_offsets(int hpc, int hd, int r, int 
   o.bv = o.bx + C;
   o.gx = o.bv + C;
   o.gv = o.gx + C;
-  o.dt = o.gv + C;
-  o.total = ((o.dt + hpc + 31) / 32) * 32;
+  o.sc = o.gv + C;
+  o.total = ((o.sc + hpc + 31) / 32) * 32;
   return o;
 }
+
+// Row stride (floats) of a mixing chunk [KC][2C + 4]: the 4-float pad
+// rotates consecutive k rows across bank groups for the k-split lanes.
+__host__ __device__ inline int chunk_row_stride(int C) { return 2 * C + 4; }
 
 struct SeqArgs {
   const float* x0;
@@ -73,44 +90,41 @@ struct SeqArgs {
   float* v_seq;
   float* x_out;
   float* v_out;
+  long long* prof;  // optional per-phase cycle counters (CTA 0), SEQ_PROF_N entries
   int B, L, d, H, hd, NL;
   int K, R, C, hpc, KC, nchunk, NST;
   int HS, CF;
   long long LF;
   int mix;
-  int TR, NG, tiles, S;
+  int TR, NG, tiles, S;   // mixing tiles: TR rows x 4 columns, S-way k split
   float base_dt;
-  int o_head, o_chunk, o_xs, o_vs, o_ox, o_ov, o_catx, o_catv, o_part, o_p, o_red;
+  int o_head, o_chunk, o_ox, o_ov, o_catx, o_catv, o_part;
 };
 
-GFN_DEV void seq_load_force(const SeqArgs& a, int t, int row0, int col0, const int* orow,
-                            const int* ocol, float* f) {
-#pragma unroll
-  for (int i = 0; i < SEQ_OPT; ++i) {
-    f[i] = 0.f;
-    if (orow[i] < 0) continue;
-    const int b = row0 + orow[i];
-    if (b >= a.B) continue;
-    const long long idx = (long long)b * a.L + t;
-    const long long col = col0 + ocol[i];
-    float v;
-    if (a.f32) {
-      v = a.f32[idx * a.d + col];
-    } else if (a.fbf16) {
-      v = __bfloat162float(a.fbf16[idx * a.d + col]);
-    } else {
-      const long long id = a.ids[idx];
-      if (id < 0 || id >= a.vocab) {
-        gfn_flag_error(kDevErrBadToken);
-        v = 0.f;
-      } else {
-        v = a.table[id * a.d + col];
-      }
-    }
-    if (a.mask) v = v * a.mask[idx];
-    f[i] = v;
-  }
+// ---------------------------------------------------------------- PTX bits
+GFN_DEV void named_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+
+GFN_DEV void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
+
+// st.async of floats into a peer CTA's shared memory, completing on that
+// CTA's mbarrier (4 / 8 transaction bytes).
+GFN_DEV void st_async1(uint32_t raddr, float v, uint32_t rbar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.f32 [%0], %1, [%2];" ::"r"(raddr),
+               "f"(v), "r"(rbar)
+               : "memory");
+}
+
+GFN_DEV void st_async2(uint32_t raddr, float a, float b, uint32_t rbar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v2.f32 [%0], {%1, %2}, [%3];" ::"r"(
+                   raddr),
+               "f"(a), "f"(b), "r"(rbar)
+               : "memory");
+}
+
+// ---------------------------------------------------------------- shared helpers
+// (also used by the single-head kernels in ops_small.cuh)
 
 // p[row][hl][q] = sum_k v[row][hl*hd + k] U[hl][k][q]: one warp per (row, head).
 template <int RK>
@@ -126,18 +140,13 @@ GFN_DEV void seq_head_proj(const float* __restrict__ vsrc, const float* __restri
     for (int q = 0; q < RK; ++q) acc[q] = 0.f;
     for (int k = lane; k < hd; k += 32) {
       const float vv = vr[k];
-      if constexpr (RK % 4 == 0) {
 #pragma unroll
-        for (int q4 = 0; q4 < RK; q4 += 4) {
-          const float4 u = *reinterpret_cast<const float4*>(Uh + k * RK + q4);
-          acc[q4 + 0] = fmaf(vv, u.x, acc[q4 + 0]);
-          acc[q4 + 1] = fmaf(vv, u.y, acc[q4 + 1]);
-          acc[q4 + 2] = fmaf(vv, u.z, acc[q4 + 2]);
-          acc[q4 + 3] = fmaf(vv, u.w, acc[q4 + 3]);
-        }
-      } else {
-#pragma unroll
-        for (int q = 0; q < RK; ++q) acc[q] = fmaf(vv, Uh[k * RK + q], acc[q]);
+      for (int q4 = 0; q4 < RK; q4 += 4) {
+        const float4 u = *reinterpret_cast<const float4*>(Uh + k * RK + q4);
+        acc[q4 + 0] = fmaf(vv, u.x, acc[q4 + 0]);
+        acc[q4 + 1] = fmaf(vv, u.y, acc[q4 + 1]);
+        acc[q4 + 2] = fmaf(vv, u.z, acc[q4 + 2]);
+        acc[q4 + 3] = fmaf(vv, u.w, acc[q4 + 3]);
       }
     }
 #pragma unroll
@@ -152,58 +161,170 @@ GFN_DEV void seq_head_proj(const float* __restrict__ vsrc, const float* __restri
   }
 }
 
-// Gamma for one output column jj of head hl from that head's projection p.
+// Gamma for one output column from its head's projection and W row.
 template <int RK>
-GFN_DEV float seq_gamma(const float* __restrict__ p, const float* __restrict__ Wrow) {
-  float pr[RK];
-  float ss = 0.f;
-#pragma unroll
-  for (int q = 0; q < RK; ++q) {
-    pr[q] = p[q];
-    ss = fmaf(pr[q], pr[q], ss);
-  }
-  const float nrm = sqrtf(ss);
-  const float sc = 1.f / ((1.f + nrm) + 1e-6f);
+GFN_DEV float seq_gamma(const float* __restrict__ pr, float sc, const float* __restrict__ Wrow) {
   float g = 0.f;
 #pragma unroll
   for (int q = 0; q < RK; ++q) g = fmaf((pr[q] * pr[q]) * sc, Wrow[q], g);
   return soft_clamp20(g);
 }
 
-// Friction pre-activation z = x_head . Wf[j, :] + bf[j] for one output.
-GFN_DEV float seq_friction_pre(const float* __restrict__ xr, const float* __restrict__ wt, int hd,
-                               float bias) {
-  float s0 = 0.f, s1 = 0.f;
-  int k = 0;
-  for (; k + 1 < hd; k += 2) {
-    s0 = fmaf(xr[k], wt[k * hd], s0);
-    s1 = fmaf(xr[k + 1], wt[(k + 1) * hd], s1);
+// s = 1 / (1 + |p| + 1e-6) (gfn/geometry/lowrank.py:95-96).
+template <int RK>
+GFN_DEV float seq_proj_scale(const float* __restrict__ p, float* pr) {
+  float ss = 0.f;
+#pragma unroll
+  for (int q = 0; q < RK; ++q) {
+    pr[q] = p[q];
+    ss = fmaf(pr[q], pr[q], ss);
   }
-  if (k < hd) s0 = fmaf(xr[k], wt[k * hd], s0);
-  return (s0 + s1) + bias;
+  return 1.f / ((1.f + sqrtf(ss)) + 1e-6f);
 }
 
-template <int RK>
+// Reduce-scatter of 16 values over the S (<= 16) lanes that differ in the
+// low log2(S) lane bits (butterfly, fixed order).  Level L halves the live
+// set (8 >> L values exchanged over lane bit S >> (L+1)); on return the lane
+// holds cnt = 16 / S fully reduced values v[0..cnt) for entries
+// base..base+cnt-1.  Halves are compile-time so v stays in registers.
+GFN_DEV void reduce_scatter16(float (&v)[16], int S, int lane, int& base, int& cnt) {
+  base = 0;
+  cnt = 16;
+#pragma unroll
+  for (int L = 0; L < 4; ++L) {
+    const int half = 8 >> L;
+    const int m = S >> (L + 1);
+    if (m >= 1) {
+      const bool upper = (lane & m) != 0;
+#pragma unroll
+      for (int i = 0; i < half; ++i) {
+        const float send = upper ? v[i] : v[i + half];
+        const float keep = upper ? v[i + half] : v[i];
+        v[i] = keep + __shfl_xor_sync(0xffffffffu, send, m);
+      }
+      if (upper) base += half;
+      cnt = half;
+    }
+  }
+}
+
+// ---------------------------------------------------------------- unit helpers
+// Force element of row b, column col at token t.
+GFN_DEV float seq_load_force(const SeqArgs& a, int t, int b, int col) {
+  const long long idx = (long long)b * a.L + t;
+  float f;
+  if (a.f32) {
+    f = __ldg(a.f32 + idx * a.d + col);
+  } else if (a.fbf16) {
+    f = __bfloat162float(a.fbf16[idx * a.d + col]);
+  } else {
+    const long long id = __ldg(a.ids + idx);
+    if (id < 0 || id >= a.vocab) {
+      gfn_flag_error(kDevErrBadToken);
+      f = 0.f;
+    } else {
+      f = __ldg(a.table + id * a.d + col);
+    }
+  }
+  if (a.mask) f = f * __ldg(a.mask + idx);
+  return f;
+}
+
+// Gamma(v) for the lane's EPL elements of one unit (lane-resident v).
+template <int RK, int EPL>
+GFN_DEV void unit_gamma(const float (&vv)[EPL], const float* __restrict__ U,
+                        const float* __restrict__ W, const bool (&ok)[EPL], const int (&jj)[EPL],
+                        float (&g)[EPL]) {
+  float p[RK];
+#pragma unroll
+  for (int q = 0; q < RK; ++q) p[q] = 0.f;
+#pragma unroll
+  for (int e = 0; e < EPL; ++e) {
+    if (ok[e]) {
+#pragma unroll
+      for (int q4 = 0; q4 < RK; q4 += 4) {
+        const float4 u = *reinterpret_cast<const float4*>(U + jj[e] * RK + q4);
+        p[q4 + 0] = fmaf(vv[e], u.x, p[q4 + 0]);
+        p[q4 + 1] = fmaf(vv[e], u.y, p[q4 + 1]);
+        p[q4 + 2] = fmaf(vv[e], u.z, p[q4 + 2]);
+        p[q4 + 3] = fmaf(vv[e], u.w, p[q4 + 3]);
+      }
+    }
+  }
+#pragma unroll
+  for (int m = 16; m >= 1; m >>= 1)
+#pragma unroll
+    for (int q = 0; q < RK; ++q) p[q] += __shfl_xor_sync(0xffffffffu, p[q], m);
+  float ss = 0.f;
+#pragma unroll
+  for (int q = 0; q < RK; ++q) ss = fmaf(p[q], p[q], ss);
+  const float sc = 1.f / ((1.f + sqrtf(ss)) + 1e-6f);
+#pragma unroll
+  for (int e = 0; e < EPL; ++e) {
+    float acc = 0.f;
+    if (ok[e]) {
+#pragma unroll
+      for (int q4 = 0; q4 < RK; q4 += 4) {
+        const float4 w = *reinterpret_cast<const float4*>(W + jj[e] * RK + q4);
+        acc = fmaf((p[q4 + 0] * p[q4 + 0]) * sc, w.x, acc);
+        acc = fmaf((p[q4 + 1] * p[q4 + 1]) * sc, w.y, acc);
+        acc = fmaf((p[q4 + 2] * p[q4 + 2]) * sc, w.z, acc);
+        acc = fmaf((p[q4 + 3] * p[q4 + 3]) * sc, w.w, acc);
+      }
+    }
+    g[e] = soft_clamp20(acc);
+  }
+}
+
+// mu(x) = 5 sigmoid(x Wf^T + bf) for the lane's elements; x is broadcast
+// across the warp by shuffles, WfT is [k][j] in shared memory.
+template <int EPL>
+GFN_DEV void unit_friction(const float (&xx)[EPL], const float* __restrict__ WfT,
+                           const float* __restrict__ bf, int hd, const int (&jj)[EPL],
+                           float (&mu)[EPL]) {
+  float z0[EPL], z1[EPL];
+#pragma unroll
+  for (int e = 0; e < EPL; ++e) z0[e] = z1[e] = 0.f;
+#pragma unroll
+  for (int e2 = 0; e2 < EPL; ++e2) {
+#pragma unroll
+    for (int kk = 0; kk < 32; kk += 2) {
+      const int k = e2 * 32 + kk;
+      if (k < hd) {
+        const float xa = __shfl_sync(0xffffffffu, xx[e2], kk);
+        const float xb = __shfl_sync(0xffffffffu, xx[e2], kk + 1);
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) {
+          z0[e] = fmaf(xa, WfT[k * hd + jj[e]], z0[e]);
+          z1[e] = fmaf(xb, WfT[(k + 1) * hd + jj[e]], z1[e]);
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int e = 0; e < EPL; ++e) mu[e] = sigmoid_f((z0[e] + z1[e]) + bf[jj[e]]) * 5.f;
+}
+
+template <int RK, int EPL>
 __global__ void __launch_bounds__(SEQ_THREADS, 1) leapfrog_seq_kernel(const SeqArgs a) {
   extern __shared__ __align__(128) unsigned char smem_raw[];
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem_raw);
-  uint64_t* head_full = bars;       // [2]
-  uint64_t* chunk_full = bars + 2;  // [NST]
-  float* sm = reinterpret_cast<float*>(smem_raw + 128);
+  uint64_t* head_full = bars;            // [2]
+  uint64_t* head_empty = bars + 2;       // [2]
+  uint64_t* xch_bar = bars + 4;          // concat exchange
+  uint64_t* part_bar = bars + 5;         // partial sums exchange
+  uint64_t* chunk_full = bars + 6;       // [NST]
+  uint64_t* chunk_empty = bars + 6 + a.NST;  // [NST]
+  float* sm = reinterpret_cast<float*>(smem_raw + SEQ_BAR_BYTES);
   float* head_ring = sm + a.o_head;
   float* chunk_ring = sm + a.o_chunk;
-  float* xs = sm + a.o_xs;
-  float* vs = sm + a.o_vs;
   float* ox = sm + a.o_ox;
   float* ov = sm + a.o_ov;
   float* catx = sm + a.o_catx;
   float* catv = sm + a.o_catv;
   float* part = sm + a.o_part;
-  float* pbuf = sm + a.o_p;
-  float* red = sm + a.o_red;
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  constexpr int NW = SEQ_THREADS / 32;
   const uint32_t crank = cluster_ctarank();
   const int cl = blockIdx.x / a.K;
   const int row0 = cl * a.R;
@@ -211,200 +332,241 @@ __global__ void __launch_bounds__(SEQ_THREADS, 1) leapfrog_seq_kernel(const SeqA
   const int col0 = (int)crank * C;
   const HeadOffsets ho = head_offsets(hpc, hd, RK, C);
   const long long total_steps = (long long)a.L * a.NL;
-  const long long total_chunks = a.mix ? total_steps * a.nchunk : 0;
   const float* my_pack = a.pack + (long long)crank * a.LF;
   const long long layer_stride = (long long)K * a.LF;
-
-  auto issue_head = [&](long long g) {
-    const int l = (int)(g % a.NL);
-    uint64_t* bar = &head_full[g & 1];
-    mbar_arrive_expect_tx(bar, (uint32_t)a.HS * 4u);
-    bulk_g2s(head_ring + (g & 1) * a.HS, my_pack + l * layer_stride, (uint32_t)a.HS * 4u, bar);
-  };
-  auto issue_chunk = [&](long long q) {
-    const long long g = q / a.nchunk;
-    const int i = (int)(q - g * a.nchunk);
-    const int l = (int)(g % a.NL);
-    const int slot = (int)(q % a.NST);
-    uint64_t* bar = &chunk_full[slot];
-    mbar_arrive_expect_tx(bar, (uint32_t)a.CF * 4u);
-    bulk_g2s(chunk_ring + (long long)slot * a.CF,
-             my_pack + l * layer_stride + a.HS + (long long)i * a.CF, (uint32_t)a.CF * 4u, bar);
-  };
+  const uint32_t xch_bytes = (uint32_t)(2 * R * d * 4);
+  const uint32_t part_bytes = (uint32_t)(K * R * 2 * 4);
 
   if (tid == 0) {
-    for (int i = 0; i < 2 + a.NST; ++i) mbar_init(&bars[i], 1);
+    for (int i = 0; i < 6 + 2 * a.NST; ++i) {
+      const bool is_empty = (i >= 2 && i < 4) || (i >= 6 + a.NST);
+      mbar_init(&bars[i], is_empty ? SEQ_CWARPS : 1);
+    }
     fence_mbar_init();
+    if (a.mix) {
+      mbar_arrive_expect_tx(xch_bar, xch_bytes);
+      mbar_arrive_expect_tx(part_bar, part_bytes);
+    }
   }
   __syncthreads();
-  if (tid == 0) {
-    if (total_steps > 0) issue_head(0);
-    for (long long q = 0; q < total_chunks && q < a.NST; ++q) issue_chunk(q);
+  cluster_sync();  // peers' barriers initialised before any st.async reaches them
+
+  if (warp == SEQ_CWARPS) {
+    // ------------------------------------------------------- producer warp
+    if (lane == 0) {
+      long long q = 0;
+      for (long long g = 0; g < total_steps; ++g) {
+        const int l = (int)(g % a.NL);
+        const int hslot = (int)(g & 1);
+        if (g >= 2) mbar_wait(&head_empty[hslot], (uint32_t)(((g >> 1) - 1) & 1));
+        mbar_arrive_expect_tx(&head_full[hslot], (uint32_t)a.HS * 4u);
+        bulk_g2s(head_ring + hslot * a.HS, my_pack + l * layer_stride, (uint32_t)a.HS * 4u,
+                 &head_full[hslot]);
+        for (int i = 0; a.mix && i < a.nchunk; ++i, ++q) {
+          const int slot = (int)(q % a.NST);
+          const long long n = q / a.NST;
+          if (n >= 1) mbar_wait(&chunk_empty[slot], (uint32_t)((n - 1) & 1));
+          mbar_arrive_expect_tx(&chunk_full[slot], (uint32_t)a.CF * 4u);
+          bulk_g2s(chunk_ring + (long long)slot * a.CF,
+                   my_pack + l * layer_stride + a.HS + (long long)i * a.CF, (uint32_t)a.CF * 4u,
+                   &chunk_full[slot]);
+        }
+      }
+    }
+    __syncwarp();
+    cluster_sync();
+    return;
   }
 
-  // This thread's head-step outputs (row, column), fixed for the launch.
-  const int RC = R * C;
-  int orow[SEQ_OPT], ocol[SEQ_OPT], ohl[SEQ_OPT], ojj[SEQ_OPT];
+  // ------------------------------------------------------- compute warps
+  const bool prof = a.prof != nullptr && blockIdx.x == 0 && tid == 0;
+  long long pacc[SEQ_PROF_N];
 #pragma unroll
-  for (int i = 0; i < SEQ_OPT; ++i) {
-    const int o = tid + i * SEQ_THREADS;
-    if (o < RC) {
-      orow[i] = o / C;
-      ocol[i] = o - orow[i] * C;
-      ohl[i] = ocol[i] / hd;
-      ojj[i] = ocol[i] - ohl[i] * hd;
-    } else {
-      orow[i] = -1;
-      ocol[i] = ohl[i] = ojj[i] = 0;
+  for (int i = 0; i < SEQ_PROF_N; ++i) pacc[i] = 0;
+  long long pt = prof ? clock64() : 0;
+  auto mark = [&](int i) {
+    if (prof) {
+      const long long now = clock64();
+      pacc[i] += now - pt;
+      pt = now;
     }
-  }
+  };
+
+  // Units of this warp: u = warp + 8 i -> (row u / hpc, head u % hpc).
+  const int nunits = R * hpc;
+  int urow[SEQ_MAXU], uhl[SEQ_MAXU];
+  bool uok[SEQ_MAXU];
 #pragma unroll
-  for (int i = 0; i < SEQ_OPT; ++i) {
-    if (orow[i] < 0) continue;
-    const int b = row0 + orow[i];
-    float xv = 0.f, vv = 0.f;
-    if (b < a.B) {
-      const long long off = (long long)b * a.state_stride + col0 + ocol[i];
-      xv = a.x0[off];
-      vv = a.v0[off];
-    }
-    xs[orow[i] * C + ocol[i]] = xv;
-    vs[orow[i] * C + ocol[i]] = vv;
+  for (int i = 0; i < SEQ_MAXU; ++i) {
+    const int u = warp + SEQ_CWARPS * i;
+    uok[i] = u < nunits;
+    urow[i] = uok[i] ? u / hpc : 0;
+    uhl[i] = uok[i] ? u - urow[i] * hpc : 0;
   }
+  int jj[EPL];
+  bool eok[EPL];
+#pragma unroll
+  for (int e = 0; e < EPL; ++e) {
+    jj[e] = lane + 32 * e;
+    eok[e] = jj[e] < hd;
+    if (!eok[e]) jj[e] = hd - 1;  // harmless in-range index for idle lanes
+  }
+
+  float xr[SEQ_MAXU][EPL], vr[SEQ_MAXU][EPL], fc[SEQ_MAXU][EPL], fn[SEQ_MAXU][EPL];
+#pragma unroll
+  for (int i = 0; i < SEQ_MAXU; ++i)
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) {
+      xr[i][e] = vr[i][e] = fc[i][e] = fn[i][e] = 0.f;
+      const int b = row0 + urow[i];
+      if (uok[i] && eok[e] && b < a.B) {
+        const long long off = (long long)b * a.state_stride + col0 + uhl[i] * hd + jj[e];
+        xr[i][e] = a.x0[off];
+        vr[i][e] = a.v0[off];
+        if (a.L > 0) fn[i][e] = seq_load_force(a, 0, b, col0 + uhl[i] * hd + jj[e]);
+      }
+    }
 
   // Mixing tile of this thread: rows r0..r0+TR-1, columns n0..n0+3 of the
-  // [x | v] output block, k-split s of S.
-  const bool mix_active = tid < a.tiles * a.S;
-  const int mtile = tid % a.tiles, ms = tid / a.tiles;
+  // [x | v] block, k-split ms (low lane bits) of S.
+  const int S = a.S;
+  const bool mix_active = tid < a.tiles * S;
+  const int ms = tid % S, mtile = tid / S;
   const int mng = mtile % a.NG, mrg = mtile / a.NG;
   const int mn0 = mng * 4, mr0 = mrg * a.TR;
   const float* mcat = (mn0 < C) ? catx : catv;
-  const int C2 = 2 * C;
+  const int CS = chunk_row_stride(C);
   const float inv_d = 1.f / (float)d;
   const float rms_eps = 1.1920928955078125e-07f;  // float32 machine epsilon
 
-  float fnext[SEQ_OPT];
-  if (a.L > 0) seq_load_force(a, 0, row0, col0, orow, ocol, fnext);
-  cluster_sync();  // every CTA of the cluster is resident before any DSMEM store
-
   long long g = 0, q = 0;
   for (int t = 0; t < a.L; ++t) {
-    float fcur[SEQ_OPT];
 #pragma unroll
-    for (int i = 0; i < SEQ_OPT; ++i) fcur[i] = fnext[i];
-    if (t + 1 < a.L) seq_load_force(a, t + 1, row0, col0, orow, ocol, fnext);
+    for (int i = 0; i < SEQ_MAXU; ++i)
+#pragma unroll
+      for (int e = 0; e < EPL; ++e) {
+        fc[i][e] = fn[i][e];
+        const int b = row0 + urow[i];
+        if (t + 1 < a.L && uok[i] && eok[e] && b < a.B)
+          fn[i][e] = seq_load_force(a, t + 1, b, col0 + uhl[i] * hd + jj[e]);
+      }
 
     for (int l = 0; l < a.NL; ++l, ++g) {
-      if (tid == 0 && g + 1 < total_steps) issue_head(g + 1);
-      const float* hs = head_ring + (g & 1) * a.HS;
-      mbar_wait(&head_full[g & 1], (uint32_t)((g >> 1) & 1));
+      const int hslot = (int)(g & 1);
+      const float* hs = head_ring + hslot * a.HS;
+      mbar_wait(&head_full[hslot], (uint32_t)((g >> 1) & 1));
+      mark(0);
 
-      float z[SEQ_OPT], hh[SEQ_OPT], eff[SEQ_OPT];
-      // ---- kick 1: projections of v and friction of x
-      seq_head_proj<RK>(vs, hs + ho.U, pbuf, R, hpc, hd, C, warp, lane, NW);
+      // ---- head step of every unit, in registers
 #pragma unroll
-      for (int i = 0; i < SEQ_OPT; ++i) {
-        if (orow[i] < 0) continue;
-        z[i] = seq_friction_pre(xs + orow[i] * C + ohl[i] * hd,
-                                hs + ho.WfT + ohl[i] * hd * hd + ojj[i], hd, hs[ho.bf + ocol[i]]);
-        const float sc = softplus_f(hs[ho.dt + ohl[i]]);
-        eff[i] = a.base_dt * sc;
-        hh[i] = 0.5f * eff[i];
-      }
-      __syncthreads();
-      // ---- kick 1 update + drift
+      for (int i = 0; i < SEQ_MAXU; ++i) {
+        if (!uok[i]) continue;
+        const int hl = uhl[i];
+        const float* U = hs + ho.U + hl * hd * RK;
+        const float* Wg = hs + ho.W + hl * hd * RK;
+        const float* WfT = hs + ho.WfT + hl * hd * hd;
+        const float* bfh = hs + ho.bf + hl * hd;
+        const float eff = a.base_dt * hs[ho.sc + hl];
+        const float hh = 0.5f * eff;
+        float gm[EPL], mu[EPL];
+        // kick 1 (implicit friction at x), drift
+        unit_gamma<RK, EPL>(vr[i], U, Wg, eok, jj, gm);
+        unit_friction<EPL>(xr[i], WfT, bfh, hd, jj, mu);
 #pragma unroll
-      for (int i = 0; i < SEQ_OPT; ++i) {
-        if (orow[i] < 0) continue;
-        const int o = orow[i] * C + ocol[i];
-        const float gm = seq_gamma<RK>(pbuf + (orow[i] * hpc + ohl[i]) * RK,
-                                       hs + ho.W + (ohl[i] * hd + ojj[i]) * RK);
-        const float mu = sigmoid_f(z[i]) * 5.f;
-        const float vh = (vs[o] + hh[i] * (fcur[i] - gm)) / (1.f + hh[i] * mu);
-        xs[o] = xs[o] + eff[i] * vh;
-        vs[o] = vh;
-      }
-      __syncthreads();
-      // ---- kick 2: projections of v_half, friction at x'
-      seq_head_proj<RK>(vs, hs + ho.U, pbuf, R, hpc, hd, C, warp, lane, NW);
+        for (int e = 0; e < EPL; ++e) {
+          const float vh = (vr[i][e] + hh * (fc[i][e] - gm[e])) / (1.f + hh * mu[e]);
+          xr[i][e] = xr[i][e] + eff * vh;
+          vr[i][e] = vh;
+        }
+        // kick 2 at x'
+        unit_gamma<RK, EPL>(vr[i], U, Wg, eok, jj, gm);
+        unit_friction<EPL>(xr[i], WfT, bfh, hd, jj, mu);
 #pragma unroll
-      for (int i = 0; i < SEQ_OPT; ++i) {
-        if (orow[i] < 0) continue;
-        z[i] = seq_friction_pre(xs + orow[i] * C + ohl[i] * hd,
-                                hs + ho.WfT + ohl[i] * hd * hd + ojj[i], hd, hs[ho.bf + ocol[i]]);
-      }
-      __syncthreads();
-#pragma unroll
-      for (int i = 0; i < SEQ_OPT; ++i) {
-        if (orow[i] < 0) continue;
-        const int o = orow[i] * C + ocol[i];
-        const float gm = seq_gamma<RK>(pbuf + (orow[i] * hpc + ohl[i]) * RK,
-                                       hs + ho.W + (ohl[i] * hd + ojj[i]) * RK);
-        const float mu = sigmoid_f(z[i]) * 5.f;
-        const float vn = (vs[o] + hh[i] * (fcur[i] - gm)) / (1.f + hh[i] * mu);
+        for (int e = 0; e < EPL; ++e)
+          vr[i][e] = (vr[i][e] + hh * (fc[i][e] - gm[e])) / (1.f + hh * mu[e]);
         if (a.mix) {
-          const float xn = xs[o];
-          const int cidx = orow[i] * d + col0 + ocol[i];
-          for (int k = 0; k < K; ++k) {
-            dsmem_st(dsmem_addr(catx + cidx, k), xn);
-            dsmem_st(dsmem_addr(catv + cidx, k), vn);
+#pragma unroll
+          for (int e = 0; e < EPL; ++e) {
+            if (!eok[e]) continue;
+            const int cidx = urow[i] * d + col0 + hl * hd + jj[e];
+            for (int k = 0; k < K; ++k) {
+              const uint32_t rb = dsmem_addr(xch_bar, k);
+              st_async1(dsmem_addr(catx + cidx, k), xr[i][e], rb);
+              st_async1(dsmem_addr(catv + cidx, k), vr[i][e], rb);
+            }
           }
         } else {
-          vs[o] = saturate100(vn);
+#pragma unroll
+          for (int e = 0; e < EPL; ++e) vr[i][e] = saturate100(vr[i][e]);
         }
       }
+      mark(1);
 
       if (a.mix) {
-        cluster_sync();  // concat of all heads complete in every CTA
+        mbar_wait(xch_bar, (uint32_t)(g & 1));  // every CTA's columns have landed
+        mark(2);
+        // Arm the next phase.  Threads still polling this phase's parity keep
+        // seeing it complete: the next phase needs this CTA's own next sends,
+        // which come after the block barrier below.
+        if (tid == 0) mbar_arrive_expect_tx(xch_bar, xch_bytes);
         // ---- head mixing: [R x d] . [d x 2C] for this CTA's columns
-        float acc[4][4];
+        float acc[16];
 #pragma unroll
-        for (int rr = 0; rr < 4; ++rr)
-#pragma unroll
-          for (int cc = 0; cc < 4; ++cc) acc[rr][cc] = 0.f;
+        for (int i = 0; i < 16; ++i) acc[i] = 0.f;
         for (int i = 0; i < a.nchunk; ++i, ++q) {
           const int slot = (int)(q % a.NST);
           mbar_wait(&chunk_full[slot], (uint32_t)((q / a.NST) & 1));
           const float* wc = chunk_ring + (long long)slot * a.CF;
           if (mix_active) {
             const float* catk = mcat + i * a.KC;
-            for (int kk = ms; kk < a.KC; kk += a.S) {
-              const float4 w = *reinterpret_cast<const float4*>(wc + kk * C2 + mn0);
+            for (int kk = 4 * ms; kk < a.KC; kk += 4 * S) {
+              const float4 w0 = *reinterpret_cast<const float4*>(wc + (kk + 0) * CS + mn0);
+              const float4 w1 = *reinterpret_cast<const float4*>(wc + (kk + 1) * CS + mn0);
+              const float4 w2 = *reinterpret_cast<const float4*>(wc + (kk + 2) * CS + mn0);
+              const float4 w3 = *reinterpret_cast<const float4*>(wc + (kk + 3) * CS + mn0);
 #pragma unroll
               for (int rr = 0; rr < 4; ++rr) {
-                if (rr < a.TR) {
-                  const float xv = catk[(mr0 + rr) * d + kk];
-                  acc[rr][0] = fmaf(xv, w.x, acc[rr][0]);
-                  acc[rr][1] = fmaf(xv, w.y, acc[rr][1]);
-                  acc[rr][2] = fmaf(xv, w.z, acc[rr][2]);
-                  acc[rr][3] = fmaf(xv, w.w, acc[rr][3]);
+                if (rr < a.TR && mr0 + rr < R) {
+                  const float4 c4 = *reinterpret_cast<const float4*>(catk + (mr0 + rr) * d + kk);
+                  float* ac = acc + rr * 4;
+                  ac[0] = fmaf(c4.x, w0.x, ac[0]); ac[1] = fmaf(c4.x, w0.y, ac[1]);
+                  ac[2] = fmaf(c4.x, w0.z, ac[2]); ac[3] = fmaf(c4.x, w0.w, ac[3]);
+                  ac[0] = fmaf(c4.y, w1.x, ac[0]); ac[1] = fmaf(c4.y, w1.y, ac[1]);
+                  ac[2] = fmaf(c4.y, w1.z, ac[2]); ac[3] = fmaf(c4.y, w1.w, ac[3]);
+                  ac[0] = fmaf(c4.z, w2.x, ac[0]); ac[1] = fmaf(c4.z, w2.y, ac[1]);
+                  ac[2] = fmaf(c4.z, w2.z, ac[2]); ac[3] = fmaf(c4.z, w2.w, ac[3]);
+                  ac[0] = fmaf(c4.w, w3.x, ac[0]); ac[1] = fmaf(c4.w, w3.y, ac[1]);
+                  ac[2] = fmaf(c4.w, w3.z, ac[2]); ac[3] = fmaf(c4.w, w3.w, ac[3]);
                 }
               }
             }
           }
-          __syncthreads();  // slot consumed by every thread
-          if (tid == 0 && q + a.NST < total_chunks) issue_chunk(q + a.NST);
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&chunk_empty[slot]);
         }
+        mark(3);
         if (mix_active) {
+          int base, cnt;
+          reduce_scatter16(acc, S, lane, base, cnt);
 #pragma unroll
-          for (int rr = 0; rr < 4; ++rr)
-            if (rr < a.TR)
-              *reinterpret_cast<float4*>(red + (ms * R + mr0 + rr) * C2 + mn0) =
-                  make_float4(acc[rr][0], acc[rr][1], acc[rr][2], acc[rr][3]);
+          for (int i = 0; i < 16; ++i) {
+            if (i < cnt) {
+              const int e = base + i;
+              const int rr = e >> 2, c = e & 3;
+              const int n = mn0 + c, row = mr0 + rr;
+              if (rr < a.TR && row < R) {
+                if (n < C)
+                  ox[row * C + n] = acc[i] + hs[ho.bx + n];
+                else
+                  ov[row * C + n - C] = acc[i] + hs[ho.bv + n - C];
+              }
+            }
+          }
         }
-        __syncthreads();
-        for (int o = tid; o < R * C2; o += SEQ_THREADS) {
-          const int row = o / C2, n = o - row * C2;
-          float s = 0.f;
-          for (int sp = 0; sp < a.S; ++sp) s += red[(sp * R + row) * C2 + n];
-          if (n < C)
-            ox[row * C + n] = s + hs[ho.bx + n];
-          else
-            ov[row * C + n - C] = s + hs[ho.bv + n - C];
-        }
-        __syncthreads();
+        named_sync();
+        mark(4);
         // ---- per-row partial sums of squares -> every CTA of the cluster
-        for (int row = warp; row < R; row += NW) {
+        for (int row = warp; row < R; row += SEQ_CWARPS) {
           float sx = 0.f, sv = 0.f;
           for (int j = lane; j < C; j += 32) {
             const float u = ox[row * C + j];
@@ -414,49 +576,64 @@ __global__ void __launch_bounds__(SEQ_THREADS, 1) leapfrog_seq_kernel(const SeqA
           }
           sx = warp_sum(sx);
           sv = warp_sum(sv);
-          if (lane < K) dsmem_st2(dsmem_addr(part + ((int)crank * R + row) * 2, lane), sx, sv);
+          if (lane < K)
+            st_async2(dsmem_addr(part + ((int)crank * R + row) * 2, lane), sx, sv,
+                      dsmem_addr(part_bar, lane));
         }
-        cluster_sync();
-        // ---- RMSNorm + saturation -> next layer's input
+        mbar_wait(part_bar, (uint32_t)(g & 1));
+        if (tid == 0) mbar_arrive_expect_tx(part_bar, part_bytes);  // arm the next phase
+        mark(5);
+        // ---- RMSNorm + saturation of each unit, in registers
 #pragma unroll
-        for (int i = 0; i < SEQ_OPT; ++i) {
-          if (orow[i] < 0) continue;
-          const int row = orow[i];
+        for (int i = 0; i < SEQ_MAXU; ++i) {
+          if (!uok[i]) continue;
+          const int row = urow[i];
           float ssx = 0.f, ssv = 0.f;
           for (int c2 = 0; c2 < K; ++c2) {
-            ssx += part[(c2 * R + row) * 2];
-            ssv += part[(c2 * R + row) * 2 + 1];
+            const float2 pp = *reinterpret_cast<const float2*>(part + (c2 * R + row) * 2);
+            ssx += pp.x;
+            ssv += pp.y;
           }
           const float rx = 1.f / sqrtf(ssx * inv_d + rms_eps);
           const float rv = 1.f / sqrtf(ssv * inv_d + rms_eps);
-          const int o = row * C + ocol[i];
-          xs[o] = (ox[o] * rx) * hs[ho.gx + ocol[i]];
-          vs[o] = saturate100((ov[o] * rv) * hs[ho.gv + ocol[i]]);
+#pragma unroll
+          for (int e = 0; e < EPL; ++e) {
+            const int col = uhl[i] * hd + jj[e];
+            xr[i][e] = (ox[row * C + col] * rx) * hs[ho.gx + col];
+            vr[i][e] = saturate100((ov[row * C + col] * rv) * hs[ho.gv + col]);
+          }
         }
+        mark(6);
       }
-      __syncthreads();  // layer step done: head slot and xs/vs settled
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&head_empty[hslot]);  // head slot free
     }
     // ---- token output (state after the last layer)
 #pragma unroll
-    for (int i = 0; i < SEQ_OPT; ++i) {
-      if (orow[i] < 0) continue;
-      const int b = row0 + orow[i];
-      if (b >= a.B) continue;
-      const long long off = ((long long)b * a.L + t) * d + col0 + ocol[i];
-      const int o = orow[i] * C + ocol[i];
-      if (a.x_seq) a.x_seq[off] = xs[o];
-      if (a.v_seq) a.v_seq[off] = vs[o];
-    }
+    for (int i = 0; i < SEQ_MAXU; ++i)
+#pragma unroll
+      for (int e = 0; e < EPL; ++e) {
+        const int b = row0 + urow[i];
+        if (!uok[i] || !eok[e] || b >= a.B) continue;
+        const long long off = ((long long)b * a.L + t) * d + col0 + uhl[i] * hd + jj[e];
+        if (a.x_seq) __stcs(a.x_seq + off, xr[i][e]);
+        if (a.v_seq) __stcs(a.v_seq + off, vr[i][e]);
+      }
+    mark(7);
   }
 #pragma unroll
-  for (int i = 0; i < SEQ_OPT; ++i) {
-    if (orow[i] < 0) continue;
-    const int b = row0 + orow[i];
-    if (b >= a.B) continue;
-    const long long off = (long long)b * d + col0 + ocol[i];
-    const int o = orow[i] * C + ocol[i];
-    if (a.x_out) a.x_out[off] = xs[o];
-    if (a.v_out) a.v_out[off] = vs[o];
+  for (int i = 0; i < SEQ_MAXU; ++i)
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) {
+      const int b = row0 + urow[i];
+      if (!uok[i] || !eok[e] || b >= a.B) continue;
+      const long long off = (long long)b * d + col0 + uhl[i] * hd + jj[e];
+      if (a.x_out) a.x_out[off] = xr[i][e];
+      if (a.v_out) a.v_out[off] = vr[i][e];
+    }
+  if (prof) {
+    pacc[SEQ_PROF_N - 1] = (long long)a.L * a.NL;
+    for (int i = 0; i < SEQ_PROF_N; ++i) a.prof[i] = pacc[i];
   }
   cluster_sync();  // no CTA leaves while a peer may still address its SMEM
 }

@@ -9,6 +9,27 @@
 namespace gfn {
 
 constexpr int SMALL_THREADS = 256;
+
+// Gamma of output column j from the row's projection p (recomputes the scale).
+template <int RK>
+GFN_DEV float small_gamma(const float* __restrict__ p, const float* __restrict__ Wrow) {
+  float pr[RK];
+  const float sc = seq_proj_scale<RK>(p, pr);
+  return seq_gamma<RK>(pr, sc, Wrow);
+}
+
+// z = x_head . Wf[j, :] + bf[j] with WfT stored [k][j].
+GFN_DEV float small_friction_pre(const float* __restrict__ xr, const float* __restrict__ wt, int hd,
+                                 float bias) {
+  float s0 = 0.f, s1 = 0.f;
+  int k = 0;
+  for (; k + 1 < hd; k += 2) {
+    s0 = fmaf(xr[k], wt[k * hd], s0);
+    s1 = fmaf(xr[k + 1], wt[(k + 1) * hd], s1);
+  }
+  if (k < hd) s0 = fmaf(xr[k], wt[k * hd], s0);
+  return (s0 + s1) + bias;
+}
 constexpr int SMALL_ROWS = 8;  // rows per block
 
 struct HeadArgs {
@@ -82,7 +103,7 @@ __global__ void __launch_bounds__(SMALL_THREADS) christoffel_kernel(const HeadAr
   __syncthreads();
   for (int i = threadIdx.x; i < rows * hd; i += blockDim.x) {
     const int r = i / hd, j = i - r * hd;
-    a.gamma_out[(long long)(row0 + r) * hd + j] = seq_gamma<RK>(sm + L.pb + r * RK, sm + L.W + j * RK);
+    a.gamma_out[(long long)(row0 + r) * hd + j] = small_gamma<RK>(sm + L.pb + r * RK, sm + L.W + j * RK);
   }
 }
 
@@ -110,7 +131,7 @@ __global__ void __launch_bounds__(SMALL_THREADS) leapfrog_head_kernel(const Head
                         SMALL_THREADS / 32);
       for (int i = threadIdx.x; i < SMALL_ROWS * hd; i += blockDim.x) {
         const int r = i / hd, j = i - r * hd;
-        sm[L.zb + i] = friction ? seq_friction_pre(sm + L.xs + r * hd, sm + L.WfT + j, hd, sm[L.bf + j])
+        sm[L.zb + i] = friction ? small_friction_pre(sm + L.xs + r * hd, sm + L.WfT + j, hd, sm[L.bf + j])
                                 : 0.f;
       }
       __syncthreads();
@@ -120,7 +141,7 @@ __global__ void __launch_bounds__(SMALL_THREADS) leapfrog_head_kernel(const Head
         if (a.dt_scale) sc = a.dt_scale[a.dt_scale_n == 1 ? 0 : min(row0 + r, a.B - 1)];
         const float eff = a.dt * sc;
         const float h = 0.5f * eff;
-        const float gm = seq_gamma<RK>(sm + L.pb + r * RK, sm + L.W + j * RK);
+        const float gm = small_gamma<RK>(sm + L.pb + r * RK, sm + L.W + j * RK);
         const float mu = friction ? sigmoid_f(sm[L.zb + i]) * 5.f : 0.f;
         const float vn = (sm[L.vs + i] + h * (sm[L.fs + i] - gm)) / (1.f + h * mu);
         sm[L.vs + i] = vn;

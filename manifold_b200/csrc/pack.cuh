@@ -1,7 +1,7 @@
 // Packs the reference's stacked layer parameters into the per-(layer, CTA)
 // streaming layout read by leapfrog_seq_kernel:
-//   [head section: WfT | U | W | bf | bx | bv | gx | gv | dt_params | pad]
-//   [mixing chunk 0 .. nchunk-1: each [KC][2C], k-major, x columns then v]
+//   [head section: WfT | U | W | bf | bx | bv | gx | gv | softplus(dt_params) | pad]
+//   [mixing chunk 0 .. nchunk-1: each [KC][2C + 4], k-major, x columns then v, 4 pad]
 // so that every piece a CTA needs for one layer step is a contiguous run
 // that one bulk copy moves into shared memory.
 #pragma once
@@ -14,7 +14,7 @@ struct PackArgs {
   const float* W;    // [NL*H, hd, r]
   const float* Wf;   // [NL*H, hd, hd]  ([out, in])
   const float* bf;   // [NL*H, hd]
-  const float* dtp;  // [NL*H]
+  const float* dtp;  // [NL*H] raw dt_params (softplus applied here)
   const float* Wx;   // [NL, d, d] or null (heads == 1)
   const float* bx;   // [NL, d]
   const float* gx;   // [NL, d]
@@ -53,20 +53,21 @@ __global__ void pack_kernel(const PackArgs a) {
       } else if (o < ho.bx) {
         const int j = o - ho.bf;
         val = a.bf[((long long)l * a.H) * hd + (long long)c * C + j];
-      } else if (o < ho.dt) {
+      } else if (o < ho.sc) {
         const int which = (o - ho.bx) / C, j = (o - ho.bx) - which * C;
         const float* src = which == 0 ? a.bx : which == 1 ? a.bv : which == 2 ? a.gx : a.gv;
         val = src ? src[(long long)l * d + (long long)c * C + j] : (which >= 2 ? 1.f : 0.f);
-      } else if (o < ho.dt + a.hpc) {
-        val = a.dtp[(long long)l * a.H + c * a.hpc + (o - ho.dt)];
+      } else if (o < ho.sc + a.hpc) {
+        val = softplus_f(a.dtp[(long long)l * a.H + c * a.hpc + (o - ho.sc)]);
       }
     } else {
       const long long o2 = off - a.HS;
       const int i = (int)(o2 / a.CF);
       const int e2 = (int)(o2 - (long long)i * a.CF);
-      const int kk = e2 / (2 * C), n = e2 - kk * 2 * C;
+      const int CS = chunk_row_stride(C);
+      const int kk = e2 / CS, n = e2 - kk * CS;
       const int k = i * a.KC + kk;
-      if (k < d) {
+      if (k < d && n < 2 * C) {
         if (n < C)
           val = a.Wx[((long long)l * d + (long long)c * C + n) * d + k];
         else

@@ -135,10 +135,10 @@ def leapfrog_sequence(x0, v0, packed, meta, base_dt, forces=None, ids=None, tabl
 
 def leapfrog_plan(batch, dim, heads, rank, num_layers):
     import ctypes
-    out = (ctypes.c_int * 6)()
+    out = (ctypes.c_int * 8)()
     call("gfn_leapfrog_plan", batch, dim, heads, rank, num_layers, out)
     return dict(cluster=out[0], rows_per_cluster=out[1], clusters=out[2], smem=out[3],
-                k_chunk=out[4], ring=out[5])
+                k_chunk=out[4], ring=out[5], max_active_clusters=out[6], k_split=out[7])
 
 
 def parallel_scan_fused(a, x, workspace=True):

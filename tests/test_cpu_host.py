@@ -37,10 +37,12 @@ def test_status_strings():
 
 def test_pack_layout_sizes():
     lib = _lib.load()
-    # d=256, H=8 -> cluster 8, 32 columns per CTA, k-chunk 64 (4 chunks of 64x64 floats)
+    # d=256, H=8 -> cluster 8, 32 columns per CTA, k-chunk 64: 4 chunks of
+    # 64 rows x (64 + 4 pad) floats, after a head section of
+    # WfT 32x32 | U, W 32x4 | bf, bx, bv, gx, gv 5x32 | softplus(dt) 1, padded to 32
     head = 32 * 32 + 2 * 32 * 4 + 5 * 32
     head = (head + 1 + 31) // 32 * 32
-    assert lib.gfn_leapfrog_pack_floats(256, 8, 4, 6) == 6 * 8 * (head + 4 * 64 * 64)
+    assert lib.gfn_leapfrog_pack_floats(256, 8, 4, 6) == 6 * 8 * (head + 4 * 64 * 68)
     assert lib.gfn_leapfrog_pack_floats(256, 8, 5, 6) == -1   # rank 5 unsupported
     assert lib.gfn_leapfrog_pack_floats(250, 8, 4, 6) == -1   # heads must divide dim
     assert lib.gfn_leapfrog_pack_floats(16, 1, 4, 2) > 0      # single head: no mixing
