@@ -151,6 +151,27 @@ int gfn_parallel_scan(const float* a, const float* x, float* y, float* workspace
                       long long workspace_floats, int batch, int seq_len, int dim,
                       gfn_stream_t stream);
 
+/* The same scan for callers that cannot allocate device memory where they
+ * call it -- for example code running inside an allocator or memory-pool
+ * callback, plugins whose host framework owns every allocation, or
+ * services with a fixed device-memory budget.  It takes no workspace and
+ * allocates nothing: the chunk aggregates of the time-split path live in
+ * an 8 MiB array compiled into this library, which every GPU that loads
+ * the library keeps until the process exits.
+ *  - Limit: batch * dim <= 524288; larger sizes return GFN_ERR_INVALID
+ *    (use gfn_parallel_scan with a workspace instead).
+ *  - The first call on a device looks up that array's device address
+ *    (cudaGetSymbolAddress) with the device current; make that first call
+ *    before any stream capture on the device.
+ *  - All calls share the one array and it keeps the last call's contents
+ *    (nothing in it is read before the same call writes it).  Calls whose
+ *    executions overlap on the GPU, e.g. on two streams at once, race on
+ *    it: serialise them.
+ * Results match gfn_parallel_scan to float32 rounding (the time axis may
+ * be split into fewer chunks).  No counterpart in the reference. */
+int gfn_parallel_scan_noalloc(const float* a, const float* x, float* y, int batch, int seq_len,
+                              int dim, gfn_stream_t stream);
+
 /* ParallelMLayer recurrence (gfn/layers/parallel.py:101-121) from the
  * pre-activations z = [to_A(f) | to_dt(f) | to_B(f)] of shape
  * [batch, seq_len, 3*dim]: v_seq, x_seq [batch, seq_len, dim]. */

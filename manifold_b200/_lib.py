@@ -35,6 +35,7 @@ _SIGS = {
     "gfn_debug_set_phase_profile": [_p],
     "gfn_parallel_scan_workspace_floats": [_i, _i, _i],
     "gfn_parallel_scan": [_p, _p, _p, _p, _ll, _i, _i, _i, _p],
+    "gfn_parallel_scan_noalloc": [_p, _p, _p, _i, _i, _i, _p],
     "gfn_parallel_layer_scan": [_p, _p, _p, _i, _i, _i, _i, _f, _p],
     "gfn_functional_embedding": [_p, _ll, _p, _p, _p, _p, _p, _p, _p, _p, _p, _f, _i, _p, _p, _p],
 }

@@ -3,6 +3,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 
 #include "../../include/gfn_b200.h"
 #include "embed.cuh"
@@ -497,3 +498,88 @@ int gfn_functional_embedding(const long long* ids, long long n, const float* W0,
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Scan without caller-provided scratch.
+//
+// Some callers cannot allocate device memory at the point where they run a
+// scan: code inside a custom allocator or memory-pool callback, plugins whose
+// host framework owns every allocation, or callers with a fixed memory
+// budget.  gfn_parallel_scan_noalloc keeps the chunk aggregates of the
+// time-split scan in the fixed array below instead of a workspace argument.
+// The array is part of the library image: every GPU that loads the library
+// holds GFN_SCAN_STATIC_FLOATS floats (8 MiB) of it until the process exits.
+namespace {
+
+constexpr long long GFN_SCAN_STATIC_FLOATS = 2LL * 1024 * 1024;
+constexpr long long GFN_SCAN_STATIC_MAX_COLUMNS = GFN_SCAN_STATIC_FLOATS / 4;  // batch * dim
+
+static __device__ __align__(256) float g_scan_static_scratch[GFN_SCAN_STATIC_FLOATS];
+
+// Device address of g_scan_static_scratch, looked up once per device.  In
+// host code the symbol name is only a host-side stand-in, so the address has
+// to come from cudaGetSymbolAddress with that device current.
+constexpr int GFN_MAX_DEVICES = 64;
+float* g_scan_static_ptr[GFN_MAX_DEVICES] = {};
+std::mutex g_scan_static_mu;
+
+int scan_static_scratch(int dev, float** out) {
+  if (dev < 0 || dev >= GFN_MAX_DEVICES) return fail(GFN_ERR_UNSUPPORTED, "device %d", dev);
+  std::lock_guard<std::mutex> lock(g_scan_static_mu);
+  if (!g_scan_static_ptr[dev]) {
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_scan_static_scratch);
+    if (e != cudaSuccess) return cuda_status(e, "cudaGetSymbolAddress(scan scratch)");
+    g_scan_static_ptr[dev] = static_cast<float*>(p);
+  }
+  *out = g_scan_static_ptr[dev];
+  return GFN_OK;
+}
+
+}  // namespace
+
+extern "C" int gfn_parallel_scan_noalloc(const float* a, const float* x, float* y, int batch,
+                                         int seq_len, int dim, gfn_stream_t stream) {
+  if (!x || !y) return fail(GFN_ERR_INVALID, "scan (no-alloc): NULL x or y");
+  if (batch < 0 || seq_len < 0 || dim <= 0) return fail(GFN_ERR_INVALID, "scan (no-alloc): bad sizes");
+  if (dim % 4) return fail(GFN_ERR_UNSUPPORTED, "scan (no-alloc): dim %d must be a multiple of 4", dim);
+  if (!aligned16(x) || !aligned16(y) || (a && !aligned16(a)))
+    return fail(GFN_ERR_ALIGN, "scan (no-alloc): operands must be 16-byte aligned");
+  const long long BD = (long long)batch * dim;
+  if (BD > GFN_SCAN_STATIC_MAX_COLUMNS)
+    return fail(GFN_ERR_INVALID,
+                "scan (no-alloc): batch*dim = %lld exceeds the static scratch limit of %lld columns; "
+                "use gfn_parallel_scan with a workspace",
+                BD, GFN_SCAN_STATIC_MAX_COLUMNS);
+  if (batch == 0 || seq_len == 0) return GFN_OK;
+  int dev;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_status(e, "cudaGetDevice");
+  float* scratch = nullptr;
+  int st = scan_static_scratch(dev, &scratch);
+  if (st) return st;
+  DevInfo di;
+  st = dev_info(&di);
+  if (st) return st;
+  // Same time-split rule as gfn_parallel_scan, capped by the array size.
+  const long long groups = (long long)batch * (dim / 4);
+  const long long want_threads = (long long)di.sms * 1024;
+  int P = 1;
+  if (groups < want_threads / 4)
+    while (P < 64 && groups * P * 2 <= want_threads && seq_len / (P * 2) >= 64) P *= 2;
+  while (P > 1 && 2LL * P * BD > GFN_SCAN_STATIC_FLOATS) P /= 2;
+  ScanArgs s;
+  s.a = a; s.x = x; s.y = y; s.ws = scratch; s.B = batch; s.L = seq_len; s.D = dim; s.P = P;
+  cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);
+  const unsigned gx = (unsigned)((groups + SCAN_THREADS - 1) / SCAN_THREADS);
+  if (P == 1) {
+    scan_single_kernel<<<gx, SCAN_THREADS, 0, cs>>>(s);
+    return launch_status("scan_single_kernel (no-alloc)");
+  }
+  // Pass 1 overwrites every aggregate slot it uses before pass 2 reads it,
+  // so nothing left in the array by an earlier call is ever read.
+  scan_chunk_reduce_kernel<<<dim3(gx, P), SCAN_THREADS, 0, cs>>>(s);
+  scan_chunk_carry_kernel<<<(unsigned)((BD + SCAN_THREADS - 1) / SCAN_THREADS), SCAN_THREADS, 0, cs>>>(s);
+  scan_chunk_apply_kernel<<<dim3(gx, P), SCAN_THREADS, 0, cs>>>(s);
+  return launch_status("scan_chunk kernels (no-alloc)");
+}
