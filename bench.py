@@ -292,10 +292,10 @@ def phase_profile(step, i, state, dev):
     _lib.call("gfn_debug_set_phase_profile", None)
     v = buf.tolist()
     n = max(1, v[11])
-    names = ["head_wait", "head_step_and_send", "exchange_wait", "mixing", "reduce_and_sync",
-             "norm_exchange", "norm", "token_io"]
+    names = ["head_wait", "head_step_and_send", "exchange_wait", "mixing_compute",
+             "reduce_and_sync", "norm_exchange", "norm", "token_io", "mixing_chunk_wait"]
     out = {nm: round(v[k] / n, 1) for k, nm in enumerate(names)}
-    out["total"] = round(sum(v[:8]) / n, 1)
+    out["total"] = round(sum(v[:9]) / n, 1)
     return {"phase_cycles_per_layer_step": out, "layer_steps": n}
 
 

@@ -10,7 +10,7 @@ import os
 import torch
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(_HERE, "libgfn_b200.so")
+LIB_PATH = os.environ.get("GFN_B200_LIB") or os.path.join(_HERE, "libgfn_b200.so")
 
 _c_float_p = ctypes.c_void_p
 _i = ctypes.c_int

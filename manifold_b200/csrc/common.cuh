@@ -59,10 +59,12 @@ GFN_DEV bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 // keeps executing the same barrier sequence so that no peer CTA is left
 // waiting on it; the results of such a launch are garbage and the host
 // reports the error.
-GFN_DEV bool mbar_wait(uint64_t* bar, uint32_t parity) {
+GFN_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t sleep_ns = 32) {
   for (uint32_t i = 0; i < (1u << 22); ++i) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (i > 1024) __nanosleep(64);
+    // Back off at once: a warp spinning on a barrier must not take issue
+    // slots from the compute warps sharing its scheduler.
+    __nanosleep(sleep_ns);
   }
   gfn_flag_error(kDevErrMbarTimeout);
   return false;

@@ -79,10 +79,21 @@ int make_layout(int d, int H, int r, int NL, Layout* L) {
   L->d = d; L->H = H; L->hd = hd; L->r = r; L->NL = NL;
   L->K = K; L->C = d / K; L->hpc = H / K;
   L->mix = H > 1;
+  // k-chunk (~8 KB of each of x and v weights).  With C a power of two the
+  // kernel finds a concat element's column block by shifts, so a chunk may
+  // span blocks; otherwise the chunk is a multiple of 4 dividing C.
+  const bool c_pow2 = (L->C & (L->C - 1)) == 0;
   int KC = 2048 / L->C;
-  if (KC < 4) KC = 4;
-  if (KC > d) KC = d;
-  while (d % KC) --KC;
+  if (c_pow2) {
+    int p = 4;
+    while (p * 2 <= KC && d % (p * 2) == 0) p *= 2;
+    KC = p;
+  } else {
+    if (KC > L->C) KC = L->C;
+    KC -= KC % 4;
+    if (KC < 4) KC = 4;
+    while (L->C % KC) KC -= 4;
+  }
   L->KC = KC;
   L->nchunk = L->mix ? d / KC : 0;
   L->CF = KC * chunk_row_stride(L->C);
@@ -93,6 +104,7 @@ int make_layout(int d, int H, int r, int NL, Layout* L) {
 
 struct SeqPlan {
   Layout L;
+  int NW;  // compute warps
   int R, TR, NG, tiles, S, NST, nclusters, max_active;
   size_t smem;
   int o_head, o_chunk, o_ox, o_ov, o_catx, o_catv, o_part;
@@ -114,26 +126,33 @@ size_t plan_smem(const Layout& L, int R, int NST, SeqPlan* p) {
 // The kernel instance for (rank, elements per lane).
 using SeqKernel = void (*)(SeqArgs);
 
-SeqKernel seq_kernel_for(int r, int epl) {
-#define GFN_K(RK, E) if (r == RK && epl == E) return leapfrog_seq_kernel<RK, E>;
-  GFN_K(4, 1) GFN_K(4, 2) GFN_K(4, 4) GFN_K(8, 1) GFN_K(8, 2) GFN_K(8, 4)
-  GFN_K(16, 1) GFN_K(16, 2) GFN_K(16, 4)
+SeqKernel seq_kernel_for(int r, int epl, int nw) {
+#define GFN_K(RK, E, W) \
+  if (r == RK && epl == E && nw == W) return leapfrog_seq_kernel<RK, E, W>;
+  GFN_K(4, 1, 8) GFN_K(4, 2, 16) GFN_K(4, 4, 16) GFN_K(8, 1, 8) GFN_K(8, 2, 16) GFN_K(8, 4, 16)
+  GFN_K(16, 1, 8) GFN_K(16, 2, 16) GFN_K(16, 4, 16)
 #undef GFN_K
   return nullptr;
 }
+
+// Heads of width <= 32 (one element per lane, short per-CTA work): 8 compute
+// warps with 168 registers each; wider heads need the latency hiding of 16.
+int seq_warps(const Layout& L) { return L.hd <= 32 ? 8 : 16; }
+int seq_maxu(int nw) { return nw == 8 ? SeqShape<8>::MAXU : SeqShape<16>::MAXU; }
 
 int seq_epl(const Layout& L) { return L.hd <= 32 ? 1 : L.hd <= 64 ? 2 : 4; }
 
 // Row-block geometry for R rows: mixing tiles and the split-K factor.
 bool plan_rows(const Layout& L, int R, SeqPlan* p) {
-  if (R < 1 || R * L.hpc > SEQ_CWARPS * SEQ_MAXU) return false;
+  const int CT = p->NW * 32;
+  if (R < 1 || R * L.hpc > p->NW * seq_maxu(p->NW)) return false;
   const int TR = R < 4 ? R : 4;
   const int NG = 2 * L.C / 4;
   const int tiles = NG * ((R + TR - 1) / TR);
-  if (L.mix && tiles > SEQ_CTHREADS) return false;
+  if (L.mix && tiles > CT) return false;
   p->R = R; p->TR = TR; p->NG = NG; p->tiles = L.mix ? tiles : 1;
   int S = 1;
-  while (L.mix && S < 16 && S * 2 * tiles <= SEQ_CTHREADS) S *= 2;
+  while (L.mix && S < 16 && S * 2 * tiles <= CT) S *= 2;
   p->S = S;
   return true;
 }
@@ -143,7 +162,7 @@ int set_cluster_cfg(cudaLaunchConfig_t* cfg, cudaLaunchAttribute* attr, const Se
   attr[0].val.clusterDim.x = p.L.K;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
-  cfg->blockDim = dim3(SEQ_THREADS);
+  cfg->blockDim = dim3(p.NW * 32 + 32);
   cfg->dynamicSmemBytes = p.smem;
   cfg->attrs = attr;
   cfg->numAttrs = 1;
@@ -166,11 +185,15 @@ int query_active_clusters(SeqKernel kern, const SeqPlan& p, int* out) {
 // at once: a persistent cluster left for a second wave doubles the time.
 int make_plan(int B, const Layout& L, const DevInfo& di, SeqPlan* p) {
   p->L = L;
-  SeqKernel kern = seq_kernel_for(L.r, seq_epl(L));
+  p->NW = seq_warps(L);
+  SeqKernel kern = seq_kernel_for(L.r, seq_epl(L), p->NW);
   if (!kern) return fail(GFN_ERR_UNSUPPORTED, "no kernel for rank %d head_dim %d", L.r, L.hd);
   auto fit = [&](int R) -> bool {
     if (!plan_rows(L, R, p)) return false;
-    for (int NST = SEQ_MAX_NST < 6 ? SEQ_MAX_NST : 6; NST >= 2; --NST) {
+    // Ring depth: up to two layers of chunks (+2), so the copies of the next
+    // layer's weights are in flight a whole layer ahead, as shared memory allows.
+    const int want = L.mix ? 2 * L.nchunk + 2 : 2;
+    for (int NST = want < SEQ_MAX_NST ? want : SEQ_MAX_NST; NST >= 2; --NST) {
       const size_t smem = plan_smem(L, R, NST, p);
       if (smem <= (size_t)di.max_smem) {
         p->NST = NST;
@@ -181,7 +204,7 @@ int make_plan(int B, const Layout& L, const DevInfo& di, SeqPlan* p) {
     return false;
   };
   int Rmax = 0;
-  for (int R = 1; R <= B && R <= SEQ_CWARPS * SEQ_MAXU; ++R)
+  for (int R = 1; R <= B && R <= p->NW * seq_maxu(p->NW); ++R)
     if (fit(R)) Rmax = R;
   if (Rmax == 0)
     return fail(GFN_ERR_RESOURCES, "no sequence plan fits %d bytes of shared memory", di.max_smem);
@@ -416,7 +439,9 @@ int gfn_leapfrog_sequence_forward(const float* x_init, const float* v_init,
   a.base_dt = base_dt; a.prof = g_phase_prof;
   a.o_head = p.o_head; a.o_chunk = p.o_chunk; a.o_ox = p.o_ox; a.o_ov = p.o_ov;
   a.o_catx = p.o_catx; a.o_catv = p.o_catv; a.o_part = p.o_part;
-  return launch_seq(seq_kernel_for(rank, seq_epl(L)), a, p, reinterpret_cast<cudaStream_t>(stream));
+  a.logC = (L.C & (L.C - 1)) == 0 ? __builtin_ctz(L.C) : -1;
+  return launch_seq(seq_kernel_for(rank, seq_epl(L), p.NW), a, p,
+                    reinterpret_cast<cudaStream_t>(stream));
 }
 
 long long gfn_parallel_scan_workspace_floats(int batch, int seq_len, int dim) {

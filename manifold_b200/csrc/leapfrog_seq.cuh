@@ -39,12 +39,17 @@
 
 namespace gfn {
 
-constexpr int SEQ_CWARPS = 8;
-constexpr int SEQ_CTHREADS = SEQ_CWARPS * 32;       // compute threads
-constexpr int SEQ_THREADS = SEQ_CTHREADS + 32;      // + one producer warp
-constexpr int SEQ_MAXU = 2;                         // units per warp: R*hpc <= 16
-// (9 warps put 3 on one SM sub-partition: 168 registers per thread at most)
-constexpr int SEQ_NBAR = 24;                        // mbarrier slots reserved
+// The kernel runs NW compute warps (8 or 16) plus one producer warp.  With
+// 9 warps a thread may hold 168 registers (3 warps share an SM
+// sub-partition), with 17 warps ~96; units per warp follow from that.
+template <int NW>
+struct SeqShape {
+  static constexpr int CWARPS = NW;
+  static constexpr int CTHREADS = NW * 32;
+  static constexpr int THREADS = CTHREADS + 32;
+  static constexpr int MAXU = NW == 8 ? 3 : 2;  // units per warp: R*hpc <= NW*MAXU
+};
+constexpr int SEQ_NBAR = 48;                        // mbarrier slots reserved
 constexpr int SEQ_BAR_BYTES = SEQ_NBAR * 8;
 constexpr int SEQ_MAX_NST = (SEQ_NBAR - 6) / 2;     // ring depth limit
 constexpr int SEQ_PROF_N = 12;
@@ -97,12 +102,14 @@ struct SeqArgs {
   long long LF;
   int mix;
   int TR, NG, tiles, S;   // mixing tiles: TR rows x 4 columns, S-way k split
+  int logC;               // log2(C) when C is a power of two, else -1
   float base_dt;
   int o_head, o_chunk, o_ox, o_ov, o_catx, o_catv, o_part;
 };
 
 // ---------------------------------------------------------------- PTX bits
-GFN_DEV void named_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+template <int CT>
+GFN_DEV void named_sync() { asm volatile("bar.sync 1, %0;" ::"n"(CT) : "memory"); }
 
 GFN_DEV void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
@@ -121,6 +128,16 @@ GFN_DEV void st_async2(uint32_t raddr, float a, float b, uint32_t rbar) {
                    raddr),
                "f"(a), "f"(b), "r"(rbar)
                : "memory");
+}
+
+// Bulk copy of this CTA's shared memory into a peer CTA's shared memory,
+// completing on the peer's mbarrier (bytes a multiple of 16, 16-B aligned).
+GFN_DEV void bulk_s2peer(uint32_t rdst, const void* src, uint32_t bytes, uint32_t rbar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          rdst),
+      "r"(smem_u32(src)), "r"(bytes), "r"(rbar)
+      : "memory");
 }
 
 // ---------------------------------------------------------------- shared helpers
@@ -305,8 +322,11 @@ GFN_DEV void unit_friction(const float (&xx)[EPL], const float* __restrict__ WfT
   for (int e = 0; e < EPL; ++e) mu[e] = sigmoid_f((z0[e] + z1[e]) + bf[jj[e]]) * 5.f;
 }
 
-template <int RK, int EPL>
-__global__ void __launch_bounds__(SEQ_THREADS, 1) leapfrog_seq_kernel(const SeqArgs a) {
+template <int RK, int EPL, int NW>
+__global__ void __launch_bounds__(SeqShape<NW>::THREADS, 1) leapfrog_seq_kernel(const SeqArgs a) {
+  constexpr int SEQ_CWARPS = SeqShape<NW>::CWARPS;
+  constexpr int SEQ_CTHREADS = SeqShape<NW>::CTHREADS;
+  constexpr int SEQ_MAXU = SeqShape<NW>::MAXU;
   extern __shared__ __align__(128) unsigned char smem_raw[];
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem_raw);
   uint64_t* head_full = bars;            // [2]
@@ -334,7 +354,10 @@ __global__ void __launch_bounds__(SEQ_THREADS, 1) leapfrog_seq_kernel(const SeqA
   const long long total_steps = (long long)a.L * a.NL;
   const float* my_pack = a.pack + (long long)crank * a.LF;
   const long long layer_stride = (long long)K * a.LF;
-  const uint32_t xch_bytes = (uint32_t)(2 * R * d * 4);
+  // Concat buffers are [K][R][C]: CTA c's columns for all rows are one
+  // contiguous block, copied to every peer with one bulk copy each.
+  const uint32_t blk_bytes = (uint32_t)(R * C * 4);
+  const uint32_t xch_bytes = 2u * (uint32_t)(K - 1) * blk_bytes;
   const uint32_t part_bytes = (uint32_t)(K * R * 2 * 4);
 
   if (tid == 0) {
@@ -344,7 +367,7 @@ __global__ void __launch_bounds__(SEQ_THREADS, 1) leapfrog_seq_kernel(const SeqA
     }
     fence_mbar_init();
     if (a.mix) {
-      mbar_arrive_expect_tx(xch_bar, xch_bytes);
+      if (K > 1) mbar_arrive_expect_tx(xch_bar, xch_bytes);
       mbar_arrive_expect_tx(part_bar, part_bytes);
     }
   }
@@ -354,23 +377,28 @@ __global__ void __launch_bounds__(SEQ_THREADS, 1) leapfrog_seq_kernel(const SeqA
   if (warp == SEQ_CWARPS) {
     // ------------------------------------------------------- producer warp
     if (lane == 0) {
-      long long q = 0;
+      // Ring position tracked incrementally (no integer division per chunk).
+      int slot = 0, l = 0;
+      uint32_t empty_phase = 0;  // parity of the release this slot's next fill waits for
+      bool first_lap = true;
       for (long long g = 0; g < total_steps; ++g) {
-        const int l = (int)(g % a.NL);
         const int hslot = (int)(g & 1);
-        if (g >= 2) mbar_wait(&head_empty[hslot], (uint32_t)(((g >> 1) - 1) & 1));
+        if (g >= 2) mbar_wait(&head_empty[hslot], (uint32_t)(((g >> 1) - 1) & 1), 128);
         mbar_arrive_expect_tx(&head_full[hslot], (uint32_t)a.HS * 4u);
         bulk_g2s(head_ring + hslot * a.HS, my_pack + l * layer_stride, (uint32_t)a.HS * 4u,
                  &head_full[hslot]);
-        for (int i = 0; a.mix && i < a.nchunk; ++i, ++q) {
-          const int slot = (int)(q % a.NST);
-          const long long n = q / a.NST;
-          if (n >= 1) mbar_wait(&chunk_empty[slot], (uint32_t)((n - 1) & 1));
+        for (int i = 0; a.mix && i < a.nchunk; ++i) {
+          if (!first_lap) mbar_wait(&chunk_empty[slot], empty_phase, 128);
           mbar_arrive_expect_tx(&chunk_full[slot], (uint32_t)a.CF * 4u);
           bulk_g2s(chunk_ring + (long long)slot * a.CF,
                    my_pack + l * layer_stride + a.HS + (long long)i * a.CF, (uint32_t)a.CF * 4u,
                    &chunk_full[slot]);
+          if (++slot == a.NST) {
+            slot = 0;
+            if (first_lap) first_lap = false; else empty_phase ^= 1u;
+          }
         }
+        if (++l == a.NL) l = 0;
       }
     }
     __syncwarp();
@@ -379,16 +407,20 @@ __global__ void __launch_bounds__(SEQ_THREADS, 1) leapfrog_seq_kernel(const SeqA
   }
 
   // ------------------------------------------------------- compute warps
+  // Optional phase counters: thread 0 of CTA 0 keeps them in shared memory
+  // (not registers) so the counters cost the hot path nothing when off.
   const bool prof = a.prof != nullptr && blockIdx.x == 0 && tid == 0;
-  long long pacc[SEQ_PROF_N];
-#pragma unroll
-  for (int i = 0; i < SEQ_PROF_N; ++i) pacc[i] = 0;
-  long long pt = prof ? clock64() : 0;
+  __shared__ long long pacc[SEQ_PROF_N];
+  __shared__ long long pt_s;
+  if (prof) {
+    for (int i = 0; i < SEQ_PROF_N; ++i) pacc[i] = 0;
+    pt_s = clock64();
+  }
   auto mark = [&](int i) {
     if (prof) {
       const long long now = clock64();
-      pacc[i] += now - pt;
-      pt = now;
+      pacc[i] += now - pt_s;
+      pt_s = now;
     }
   };
 
@@ -439,7 +471,9 @@ __global__ void __launch_bounds__(SEQ_THREADS, 1) leapfrog_seq_kernel(const SeqA
   const float inv_d = 1.f / (float)d;
   const float rms_eps = 1.1920928955078125e-07f;  // float32 machine epsilon
 
-  long long g = 0, q = 0;
+  long long g = 0;
+  int cslot = 0;            // chunk ring position of the consumers
+  uint32_t cphase = 0;
   for (int t = 0; t < a.L; ++t) {
 #pragma unroll
     for (int i = 0; i < SEQ_MAXU; ++i)
@@ -488,12 +522,9 @@ __global__ void __launch_bounds__(SEQ_THREADS, 1) leapfrog_seq_kernel(const SeqA
 #pragma unroll
           for (int e = 0; e < EPL; ++e) {
             if (!eok[e]) continue;
-            const int cidx = urow[i] * d + col0 + hl * hd + jj[e];
-            for (int k = 0; k < K; ++k) {
-              const uint32_t rb = dsmem_addr(xch_bar, k);
-              st_async1(dsmem_addr(catx + cidx, k), xr[i][e], rb);
-              st_async1(dsmem_addr(catv + cidx, k), vr[i][e], rb);
-            }
+            const int cidx = ((int)crank * R + urow[i]) * C + hl * hd + jj[e];
+            catx[cidx] = xr[i][e];
+            catv[cidx] = vr[i][e];
           }
         } else {
 #pragma unroll
@@ -503,23 +534,45 @@ __global__ void __launch_bounds__(SEQ_THREADS, 1) leapfrog_seq_kernel(const SeqA
       mark(1);
 
       if (a.mix) {
-        mbar_wait(xch_bar, (uint32_t)(g & 1));  // every CTA's columns have landed
+        // Own block complete -> bulk-copy it into every peer's concat buffer
+        // (completing on the peer's mbarrier).  The generic-proxy writes
+        // must be visible to the async proxy that reads the source.
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        named_sync<SEQ_CTHREADS>();
+        if (tid < K && tid != (int)crank) {
+          const uint32_t off = (uint32_t)((int)crank * R * C);
+          const uint32_t rb = dsmem_addr(xch_bar, tid);
+          bulk_s2peer(dsmem_addr(catx + off, tid), catx + off, blk_bytes, rb);
+          bulk_s2peer(dsmem_addr(catv + off, tid), catv + off, blk_bytes, rb);
+        }
+        if (K > 1) mbar_wait(xch_bar, (uint32_t)(g & 1));  // every CTA's columns have landed
         mark(2);
         // Arm the next phase.  Threads still polling this phase's parity keep
         // seeing it complete: the next phase needs this CTA's own next sends,
         // which come after the block barrier below.
-        if (tid == 0) mbar_arrive_expect_tx(xch_bar, xch_bytes);
+        if (tid == 0 && K > 1) mbar_arrive_expect_tx(xch_bar, xch_bytes);
         // ---- head mixing: [R x d] . [d x 2C] for this CTA's columns
         float acc[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) acc[i] = 0.f;
-        for (int i = 0; i < a.nchunk; ++i, ++q) {
-          const int slot = (int)(q % a.NST);
-          mbar_wait(&chunk_full[slot], (uint32_t)((q / a.NST) & 1));
+        for (int i = 0; i < a.nchunk; ++i) {
+          const int slot = cslot;
+          mbar_wait(&chunk_full[slot], cphase);
+          if (++cslot == a.NST) {  // ring position, tracked without division
+            cslot = 0;
+            cphase ^= 1u;
+          }
+          mark(8);
           const float* wc = chunk_ring + (long long)slot * a.CF;
           if (mix_active) {
-            const float* catk = mcat + i * a.KC;
+            const int k0 = i * a.KC;
             for (int kk = 4 * ms; kk < a.KC; kk += 4 * S) {
+              // concat element k lives in column block k / C (C = 2^logC when a
+              // chunk spans blocks; otherwise the chunk lies inside one block)
+              const int kg = k0 + kk;
+              const float* cblk = a.logC >= 0
+                  ? mcat + ((kg >> a.logC) * R) * C + (kg & (C - 1))
+                  : mcat + ((kg / C) * R) * C + (kg % C);
               const float4 w0 = *reinterpret_cast<const float4*>(wc + (kk + 0) * CS + mn0);
               const float4 w1 = *reinterpret_cast<const float4*>(wc + (kk + 1) * CS + mn0);
               const float4 w2 = *reinterpret_cast<const float4*>(wc + (kk + 2) * CS + mn0);
@@ -527,7 +580,7 @@ __global__ void __launch_bounds__(SEQ_THREADS, 1) leapfrog_seq_kernel(const SeqA
 #pragma unroll
               for (int rr = 0; rr < 4; ++rr) {
                 if (rr < a.TR && mr0 + rr < R) {
-                  const float4 c4 = *reinterpret_cast<const float4*>(catk + (mr0 + rr) * d + kk);
+                  const float4 c4 = *reinterpret_cast<const float4*>(cblk + (mr0 + rr) * C);
                   float* ac = acc + rr * 4;
                   ac[0] = fmaf(c4.x, w0.x, ac[0]); ac[1] = fmaf(c4.x, w0.y, ac[1]);
                   ac[2] = fmaf(c4.x, w0.z, ac[2]); ac[3] = fmaf(c4.x, w0.w, ac[3]);
@@ -543,6 +596,7 @@ __global__ void __launch_bounds__(SEQ_THREADS, 1) leapfrog_seq_kernel(const SeqA
           }
           __syncwarp();
           if (lane == 0) mbar_arrive(&chunk_empty[slot]);
+          mark(3);
         }
         mark(3);
         if (mix_active) {
@@ -563,7 +617,7 @@ __global__ void __launch_bounds__(SEQ_THREADS, 1) leapfrog_seq_kernel(const SeqA
             }
           }
         }
-        named_sync();
+        named_sync<SEQ_CTHREADS>();
         mark(4);
         // ---- per-row partial sums of squares -> every CTA of the cluster
         for (int row = warp; row < R; row += SEQ_CWARPS) {
