@@ -237,3 +237,211 @@ def manifold_scan_forward(forces, players, heads, scan=parallel_scan):
     for pp in players:
         cur, _ = parallel_mlayer(cur, pp, heads, scan)
     return cur
+
+
+# ----------------------------------------------------------------------------
+# Backward (BPTT) of the leapfrog loop path
+# ----------------------------------------------------------------------------
+# The reference's training path is torch autograd through the loop of
+# gfn/model.py:377-402 (its fused CUDA backwards are incomplete or excluded for
+# leapfrog).  This is the same gradient written out by hand: every layer step
+# is recomputed from its stored input state and differentiated in reverse.
+
+def _gamma_fwd(v, U, W):
+    dt = v.dtype.type
+    p = v @ U
+    n = np.sqrt(np.sum(p * p, axis=-1, keepdims=True))
+    s = dt(1.0) / ((dt(1.0) + n) + dt(1e-6))
+    q = (p * p) * s
+    G = dt(20.0) * np.tanh((q @ W.T) / dt(20.0))
+    return G, (v, p, n, s, q, G)
+
+
+def _gamma_bwd(dG, cache, U, W):
+    """d/d(v, U, W) of G = 20 tanh(((vU)^2 s) W^T / 20), s = 1/(1+|vU|+1e-6)."""
+    v, p, n, s, q, G = cache
+    dt = v.dtype.type
+    dg = dG * (dt(1.0) - (G / dt(20.0)) ** 2)
+    dW = dg.T @ q
+    dq = dg @ W
+    dp = dq * dt(2.0) * p * s
+    ds = np.sum(dq * p * p, axis=-1, keepdims=True)
+    dn = -ds * s * s
+    safe = np.where(n > 0, n, dt(1.0))
+    dp = dp + np.where(n > 0, dn * p / safe, dt(0.0))
+    return dp @ U.T, v.T @ dp, dW
+
+
+def _head_fwd(x, v, F, U, W, Wf, bf, eff, h):
+    dt = x.dtype.type
+    G1, c1 = _gamma_fwd(v, U, W)
+    mu1 = sigmoid(x @ Wf.T + bf) * dt(5.0)
+    D1 = dt(1.0) + h * mu1
+    vh = (v + h * (F - G1)) / D1
+    x2 = x + eff * vh
+    G2, c2 = _gamma_fwd(vh, U, W)
+    mu2 = sigmoid(x2 @ Wf.T + bf) * dt(5.0)
+    D2 = dt(1.0) + h * mu2
+    v2 = (vh + h * (F - G2)) / D2
+    return x2, v2, (x, v, F, G1, c1, mu1, D1, vh, x2, G2, c2, mu2, D2, v2)
+
+
+def _head_bwd(dx2, dv2, cache, U, W, Wf, eff, h):
+    x, v, F, G1, c1, mu1, D1, vh, x2, G2, c2, mu2, D2, v2 = cache
+    dt = x.dtype.type
+    dN2 = dv2 / D2
+    dD2 = -dv2 * v2 / D2
+    dmu2 = dD2 * h
+    dh = np.sum(dD2 * mu2)
+    dvh = dN2.copy()
+    dF = dN2 * h
+    dG2 = -dN2 * h
+    dh += np.sum(dN2 * (F - G2))
+    dz2 = dmu2 * mu2 * (dt(1.0) - mu2 / dt(5.0))
+    dx2t = dx2 + dz2 @ Wf
+    dWf = dz2.T @ x2
+    dbf = dz2.sum(0)
+    dvg, dU, dW = _gamma_bwd(dG2, c2, U, W)
+    dvh += dvg
+    dx = dx2t.copy()
+    dvh += eff * dx2t
+    deff = np.sum(dx2t * vh)
+    dN1 = dvh / D1
+    dD1 = -dvh * vh / D1
+    dmu1 = dD1 * h
+    dh += np.sum(dD1 * mu1)
+    dv = dN1.copy()
+    dF += dN1 * h
+    dG1 = -dN1 * h
+    dh += np.sum(dN1 * (F - G1))
+    dz1 = dmu1 * mu1 * (dt(1.0) - mu1 / dt(5.0))
+    dx += dz1 @ Wf
+    dWf += dz1.T @ x
+    dbf += dz1.sum(0)
+    dvg, dU1, dW1 = _gamma_bwd(dG1, c1, U, W)
+    dv += dvg
+    dU += dU1
+    dW += dW1
+    deff += dt(0.5) * dh
+    return dx, dv, dF, dict(U=dU, W=dW, Wf=dWf, bf=dbf, eff=deff)
+
+
+def _rms_fwd(z, g):
+    dt = z.dtype
+    ms = np.mean(z * z, axis=-1, keepdims=True)
+    r = dt.type(1.0) / np.sqrt(ms + dt.type(_rms_eps(dt)))
+    y = z * r
+    return y * g, (z, r, y)
+
+
+def _rms_bwd(dout, cache, g):
+    z, r, y = cache
+    d = z.shape[-1]
+    dy = dout * g
+    dg = np.sum(dout * y, axis=0)
+    dz = r * dy - (r ** 3 / z.dtype.type(d)) * z * np.sum(dy * z, axis=-1, keepdims=True)
+    return dz, dg
+
+
+def mlayer_step_cached(x, v, F, lp, heads, base_dt):
+    """mlayer_step that also returns what its backward needs."""
+    B, d = x.shape
+    hd = d // heads
+    dtp = x.dtype.type
+    sc = softplus(lp["dt_params"].astype(x.dtype))
+    xo = np.empty_like(x)
+    vo = np.empty_like(v)
+    hc = []
+    for h in range(heads):
+        sl = slice(h * hd, (h + 1) * hd)
+        eff = dtp(base_dt) * sc[h]
+        hh = dtp(0.5) * eff
+        xh, vh, c = _head_fwd(x[:, sl], v[:, sl], F[:, sl], lp["U"][h], lp["W"][h], lp["Wf"][h],
+                              lp["bf"][h], eff, hh)
+        xo[:, sl] = xh
+        vo[:, sl] = vh
+        hc.append((c, eff, hh))
+    if heads > 1:
+        zx = xo @ lp["Wx"].T + lp["bx"]
+        zv = vo @ lp["Wv"].T + lp["bv"]
+        xn, cx = _rms_fwd(zx, lp["gx"])
+        w, cv = _rms_fwd(zv, lp["gv"])
+        mix = (xo, vo, cx, cv)
+    else:
+        xn, w, mix = xo, vo, None
+    vn = dtp(100.0) * np.tanh(w / dtp(100.0))
+    return xn, vn, (hc, mix, vn, sc)
+
+
+def mlayer_step_backward(dxn, dvn, cache, lp, heads, base_dt):
+    """Gradients of one MLayer step: (dx_in, dv_in, dF, param grads)."""
+    hc, mix, vn, sc = cache
+    dtp = dxn.dtype.type
+    B, d = dxn.shape
+    hd = d // heads
+    grads = {}
+    dw = dvn * (dtp(1.0) - (vn / dtp(100.0)) ** 2)
+    if heads > 1:
+        xo, vo, cx, cv = mix
+        dzx, grads["gx"] = _rms_bwd(dxn, cx, lp["gx"])
+        dzv, grads["gv"] = _rms_bwd(dw, cv, lp["gv"])
+        grads["bx"] = dzx.sum(0)
+        grads["bv"] = dzv.sum(0)
+        grads["Wx"] = dzx.T @ xo
+        grads["Wv"] = dzv.T @ vo
+        dxo = dzx @ lp["Wx"]
+        dvo = dzv @ lp["Wv"]
+    else:
+        dxo, dvo = dxn, dw
+    dx = np.empty_like(dxn)
+    dv = np.empty_like(dxn)
+    dF = np.empty_like(dxn)
+    gU = np.empty_like(lp["U"])
+    gW = np.empty_like(lp["W"])
+    gWf = np.empty_like(lp["Wf"])
+    gbf = np.empty_like(lp["bf"])
+    gdt = np.empty_like(lp["dt_params"])
+    th = lp["dt_params"].astype(dxn.dtype)
+    for h in range(heads):
+        sl = slice(h * hd, (h + 1) * hd)
+        c, eff, hh = hc[h]
+        a, b, f, g = _head_bwd(dxo[:, sl], dvo[:, sl], c, lp["U"][h], lp["W"][h], lp["Wf"][h],
+                               eff, hh)
+        dx[:, sl], dv[:, sl], dF[:, sl] = a, b, f
+        gU[h], gW[h], gWf[h], gbf[h] = g["U"], g["W"], g["Wf"], g["bf"]
+        # eff = base_dt * softplus(theta): d theta = d eff * base_dt * sigmoid(theta)
+        gdt[h] = g["eff"] * dtp(base_dt) * sigmoid(th[h:h + 1])[0]
+    grads.update(U=gU, W=gW, Wf=gWf, bf=gbf, dt_params=gdt)
+    return dx, dv, dF, grads
+
+
+def manifold_backward(x0, v0, forces, layers, heads, base_dt, gx_seq, gv_seq,
+                      gx_final=None, gv_final=None, mask=None):
+    """Gradients of L = <gx_seq, x_seq> + <gv_seq, v_seq> (+ <gx_final, x_L> +
+    <gv_final, v_L>) through manifold_forward.  Returns dict with x0, v0
+    ([B, d]), forces ([B, L, d]) and 'layers' (list of per-layer param grads)."""
+    B, L, d = forces.shape
+    NL = len(layers)
+    x, v = x0.copy(), v0.copy()
+    inputs = []
+    for t in range(L):
+        F = forces[:, t] if mask is None else forces[:, t] * mask[:, t, None].astype(forces.dtype)
+        for lp in layers:
+            inputs.append((x, v, F))
+            x, v = mlayer_step(x, v, F, lp, heads, base_dt)
+    dx = np.zeros_like(x0) if gx_final is None else gx_final.astype(x0.dtype).copy()
+    dv = np.zeros_like(v0) if gv_final is None else gv_final.astype(v0.dtype).copy()
+    dforces = np.zeros_like(forces)
+    lg = [None] * NL
+    for t in reversed(range(L)):
+        dx = dx + gx_seq[:, t]
+        dv = dv + gv_seq[:, t]
+        dF_t = np.zeros_like(x0)
+        for l in reversed(range(NL)):
+            xi, vi, F = inputs[t * NL + l]
+            _, _, cache = mlayer_step_cached(xi, vi, F, layers[l], heads, base_dt)
+            dx, dv, dF, g = mlayer_step_backward(dx, dv, cache, layers[l], heads, base_dt)
+            dF_t += dF
+            lg[l] = g if lg[l] is None else {k: lg[l][k] + g[k] for k in g}
+        dforces[:, t] = dF_t if mask is None else dF_t * mask[:, t, None].astype(forces.dtype)
+    return dict(x0=dx, v0=dv, forces=dforces, layers=lg)

@@ -24,6 +24,16 @@ CASES = {
     "c5s":   dict(V=32000, d=512, NL=8, H=8, rank=32, B=2, L=4, dt=0.1, seed=15),
 }
 
+# Gradient (BPTT) cases: upstream gradients on x_seq, v_seq and the final
+# state, gradients taken by the reference's autograd.  "gc5" has the C5 layer
+# shapes; its d x d mixing-weight gradients are stored as row/column sums.
+GRAD_CASES = {
+    "gsmall": dict(V=7, d=32, NL=2, H=2, rank=8, B=3, L=4, dt=0.1, seed=31),
+    "gh1":    dict(V=5, d=16, NL=2, H=1, rank=4, B=2, L=3, dt=0.1, seed=32),
+    "gmask":  dict(V=7, d=64, NL=3, H=4, rank=16, B=4, L=6, dt=0.05, seed=33, mask=True),
+    "gc5":    dict(V=300, d=512, NL=2, H=8, rank=32, B=2, L=3, dt=0.1, seed=34),
+}
+
 
 def head_rank(cfg):
     return max(4, cfg["rank"] // cfg["H"])

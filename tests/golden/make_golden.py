@@ -151,6 +151,51 @@ def gen_units():
     print("units", len(out))
 
 
+def gen_grad_case(name, cfg):
+    """Reference autograd gradients of <Gx, x_seq> + <Gv, v_seq> + <gx, x_L> + <gv, v_L>."""
+    P = C.make_params(cfg)
+    inp = C.make_inputs(cfg)
+    m = build_reference(cfg, P).train()
+    rng = np.random.default_rng(cfg["seed"] + 5)
+    B, L, d = cfg["B"], cfg["L"], cfg["d"]
+    Gx = rng.standard_normal((B, L, d)).astype(np.float32)
+    Gv = rng.standard_normal((B, L, d)).astype(np.float32)
+    gxf = rng.standard_normal((B, d)).astype(np.float32)
+    gvf = rng.standard_normal((B, d)).astype(np.float32)
+    F = T(P["emb"][inp["ids"]]).requires_grad_(True)
+    mask = T(inp["mask"]) if "mask" in inp else None
+    with contextlib.redirect_stdout(io.StringIO()):
+        _, (x, v), _, v_seq, x_seq, _ = m(force_manual=F, attention_mask=mask)
+    loss = (torch.stack(x_seq, 1) * T(Gx)).sum() + (torch.stack(v_seq, 1) * T(Gv)).sum() \
+        + (x * T(gxf)).sum() + (v * T(gvf)).sum()
+    loss.backward()
+    out = dict(ids=inp["ids"], Gx=Gx, Gv=Gv, gxf=gxf, gvf=gvf, g_forces=F.grad.numpy(),
+               g_x0=m.x0.grad.numpy()[0], g_v0=m.v0.grad.numpy()[0],
+               x_seq=torch.stack(x_seq, 1).detach().numpy())
+    if "mask" in inp:
+        out["mask"] = inp["mask"]
+    big = name == "gc5"
+    for l, layer in enumerate(m.layers):
+        out[f"l{l}_dt_params"] = layer.dt_params.grad.numpy()
+        out[f"l{l}_U"] = np.stack([c.U.grad.numpy() for c in layer.christoffels])
+        out[f"l{l}_W"] = np.stack([c.W.grad.numpy() for c in layer.christoffels])
+        out[f"l{l}_Wf"] = np.stack([c.forget_gate.weight.grad.numpy() for c in layer.christoffels])
+        out[f"l{l}_bf"] = np.stack([c.forget_gate.bias.grad.numpy() for c in layer.christoffels])
+        if cfg["H"] > 1:
+            for nm, mod in (("x", "out_proj_x"), ("v", "out_proj_v")):
+                gW = getattr(layer, mod).weight.grad.numpy()
+                if big:
+                    out[f"l{l}_W{nm}_rowsum"] = gW.sum(1)
+                    out[f"l{l}_W{nm}_colsum"] = gW.sum(0)
+                    out[f"l{l}_W{nm}_corner"] = gW[:16, :16]
+                else:
+                    out[f"l{l}_W{nm}"] = gW
+                out[f"l{l}_b{nm}"] = getattr(layer, mod).bias.grad.numpy()
+                out[f"l{l}_g{nm}"] = getattr(layer, "mixed_norm_" + nm).weight.grad.numpy()
+    np.savez_compressed(os.path.join(HERE, f"{name}.npz"), **out)
+    print(name, len(out))
+
+
 INIT_CONFIGS = {
     "c1_init": dict(vocab_size=2, dim=128, depth=4, rank=16, heads=4, integrator_type="leapfrog",
                     base_dt=0.1),
@@ -188,8 +233,12 @@ if __name__ == "__main__":
             gen_units()
         elif n == "init":
             gen_init()
+        elif n in C.GRAD_CASES:
+            gen_grad_case(n, C.GRAD_CASES[n])
         else:
             gen_model_case(n, C.CASES[n])
     if not sys.argv[1:]:
         gen_units()
         gen_init()
+        for n, cfg in C.GRAD_CASES.items():
+            gen_grad_case(n, cfg)
