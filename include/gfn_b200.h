@@ -139,6 +139,66 @@ int gfn_debug_set_phase_profile(long long* device_counters);
 int gfn_leapfrog_plan(int batch, int dim, int heads, int rank, int num_layers, int* out8);
 
 /* ------------------------------------------------------------------------
+ * Training (BPTT).  The reference trains this path with torch autograd
+ * through its per-token loop (gfn/model.py:377-402, train mode) -- its CUDA
+ * backwards launch_leapfrog_backward (gfn/cuda/cuda_kernels.cpp:123) and
+ * launch_recurrent_manifold_backward (:54-72) are incomplete or unused for
+ * leapfrog.  These entries give the same gradients.
+ *
+ * Training pack: the inference pack plus the untransposed forget-gate weight
+ * and transposed mixing chunks (same arguments as gfn_leapfrog_pack). */
+long long gfn_leapfrog_pack_train_floats(int dim, int heads, int rank, int num_layers);
+int gfn_leapfrog_pack_train(const float* U_stack, const float* W_stack,
+                            const float* W_forget_stack, const float* b_forget_stack,
+                            const float* dt_params, const float* mix_x_w, const float* mix_x_b,
+                            const float* norm_x_w, const float* mix_v_w, const float* mix_v_b,
+                            const float* norm_v_w, int dim, int heads, int rank, int num_layers,
+                            float* packed, long long packed_floats, gfn_stream_t stream);
+
+/* gfn_leapfrog_sequence_forward on the training pack that also stores every
+ * layer step's input state: traj [2][num_layers][seq_len][batch][dim]
+ * (x then v), the checkpoints the backward replays from. */
+int gfn_leapfrog_sequence_forward_train(const float* x_init, const float* v_init,
+                                        long long state_row_stride, const float* forces_f32,
+                                        const void* forces_bf16, const long long* token_ids,
+                                        const float* embed_table, long long vocab,
+                                        const float* mask, const float* packed_train,
+                                        long long packed_floats, int batch, int seq_len, int dim,
+                                        int heads, int rank, int num_layers, float base_dt,
+                                        float* x_seq, float* v_seq, float* x_final, float* v_final,
+                                        float* traj, gfn_stream_t stream);
+
+/* Reverse replay.  Upstream gradients: gx_seq, gv_seq [batch, seq_len, dim]
+ * (dL/dx_seq, dL/dv_seq), gx_final, gv_final [batch, dim]; any may be NULL.
+ * Outputs: dx_init, dv_init [batch, dim] (per row), d_forces [batch,
+ * seq_len, dim] (may be NULL; already multiplied by the mask), and the
+ * per-step gradient signals in `workspace`, from which the host forms the
+ * parameter gradients (all tensors row-major, N = num_layers*seq_len*batch
+ * rows in [layer][token][row] order, S = N*dim):
+ *   [0S,1S) x'  [1S,2S) v'   (head-step outputs = mixing inputs)
+ *   [2S,3S) dzx [3S,4S) dzv  (grads of the mixing pre-activations)
+ *   [4S,5S) dL/dxn * RMSNorm_x(z) [5S,6S) the v analogue   (norm-weight grads)
+ *   [6S,7S) dz1 [7S,8S) dz2  (friction pre-activation grads, kick 1 / kick 2)
+ *   [8S,9S) v_half [9S,10S) dg1 [10S,11S) dg2  (Gamma pre-clamp grads)
+ *   then 4 blocks of N*heads*rank: q1, q2, dp1, dp2, then N*heads d dt_eff.
+ * dWx = sum_n dzx^T x', dbx = sum dzx, dgx = sum block 4, dWf = sum dz1^T x
+ * + dz2^T x', dbf = sum (dz1 + dz2), dU = sum v^T dp1 + v_half^T dp2, dW =
+ * sum dg1^T q1 + dg2^T q2 (per head), d dt_params = sum d dt_eff * base_dt *
+ * sigmoid(dt_params).  head_dim <= 64. */
+long long gfn_leapfrog_backward_workspace_floats(int batch, int seq_len, int dim, int heads,
+                                                 int rank, int num_layers);
+int gfn_leapfrog_sequence_backward(const float* traj, const float* forces_f32,
+                                   const void* forces_bf16, const long long* token_ids,
+                                   const float* embed_table, long long vocab, const float* mask,
+                                   const float* packed_train, long long packed_floats,
+                                   const float* gx_seq, const float* gv_seq,
+                                   const float* gx_final, const float* gv_final, int batch,
+                                   int seq_len, int dim, int heads, int rank, int num_layers,
+                                   float base_dt, float* dx_init, float* dv_init, float* d_forces,
+                                   float* workspace, long long workspace_floats,
+                                   gfn_stream_t stream);
+
+/* ------------------------------------------------------------------------
  * y_t = a_t y_{t-1} + x_t along t of [batch, seq_len, dim] (a NULL: a == 1).
  * Replaces parallel_scan_fused (gfn/cuda/src/layers/parallel_scan_fused.cu:81,
  * called from gfn/scan.py:20); semantics gfn/scan.py:11-104.

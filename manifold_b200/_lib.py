@@ -34,6 +34,14 @@ _SIGS = {
     "gfn_leapfrog_plan": [_i, _i, _i, _i, _i, _p],
     "gfn_debug_set_phase_profile": [_p],
     "gfn_parallel_scan_workspace_floats": [_i, _i, _i],
+    "gfn_leapfrog_pack_train_floats": [_i, _i, _i, _i],
+    "gfn_leapfrog_pack_train": [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i, _i, _i, _i, _p, _ll,
+                                _p],
+    "gfn_leapfrog_sequence_forward_train": [_p, _p, _ll, _p, _p, _p, _p, _ll, _p, _p, _ll, _i, _i,
+                                            _i, _i, _i, _i, _f, _p, _p, _p, _p, _p, _p],
+    "gfn_leapfrog_backward_workspace_floats": [_i, _i, _i, _i, _i, _i],
+    "gfn_leapfrog_sequence_backward": [_p, _p, _p, _p, _p, _ll, _p, _p, _ll, _p, _p, _p, _p, _i, _i,
+                                       _i, _i, _i, _i, _f, _p, _p, _p, _p, _ll, _p],
     "gfn_parallel_scan": [_p, _p, _p, _p, _ll, _i, _i, _i, _p],
     "gfn_parallel_scan_noalloc": [_p, _p, _p, _i, _i, _i, _p],
     "gfn_parallel_layer_scan": [_p, _p, _p, _i, _i, _i, _i, _f, _p],
@@ -45,6 +53,8 @@ _RESTYPES = {
     "gfn_build_info": ctypes.c_char_p,
     "gfn_leapfrog_pack_floats": ctypes.c_longlong,
     "gfn_parallel_scan_workspace_floats": ctypes.c_longlong,
+    "gfn_leapfrog_pack_train_floats": ctypes.c_longlong,
+    "gfn_leapfrog_backward_workspace_floats": ctypes.c_longlong,
 }
 
 EXPORTED = tuple(_SIGS)

@@ -8,6 +8,7 @@
 #include "../../include/gfn_b200.h"
 #include "embed.cuh"
 #include "leapfrog_seq.cuh"
+#include "leapfrog_bwd.cuh"
 #include "ops_small.cuh"
 #include "pack.cuh"
 #include "scan.cuh"
@@ -64,6 +65,10 @@ int dev_info(DevInfo* out) {
 struct Layout {
   int d, H, hd, r, NL, K, C, hpc, KC, nchunk, HS, CF, mix;
   long long LF;
+  // training layout: head section + untransposed Wf (HST floats), forward and
+  // transposed mixing chunks
+  int HST;
+  long long LFT;
 };
 
 int make_layout(int d, int H, int r, int NL, Layout* L) {
@@ -99,6 +104,8 @@ int make_layout(int d, int H, int r, int NL, Layout* L) {
   L->CF = KC * chunk_row_stride(L->C);
   L->HS = head_offsets(L->hpc, hd, r, L->C).total;
   L->LF = (long long)L->HS + (long long)L->nchunk * L->CF;
+  L->HST = L->HS + ((L->hpc * hd * hd + 31) / 32) * 32;
+  L->LFT = (long long)L->HST + 2LL * L->nchunk * L->CF;
   return GFN_OK;
 }
 
@@ -195,7 +202,7 @@ int make_plan(int B, const Layout& L, const DevInfo& di, SeqPlan* p) {
     const int want = L.mix ? 2 * L.nchunk + 2 : 2;
     for (int NST = want < SEQ_MAX_NST ? want : SEQ_MAX_NST; NST >= 2; --NST) {
       const size_t smem = plan_smem(L, R, NST, p);
-      if (smem <= (size_t)di.max_smem) {
+      if (smem + 256 <= (size_t)di.max_smem) {  // 256 B: the kernels' static shared memory
         p->NST = NST;
         p->smem = smem;
         return true;
@@ -240,6 +247,84 @@ int launch_seq(SeqKernel kern, const SeqArgs& a, const SeqPlan& p, cudaStream_t 
 }
 
 }  // namespace
+
+static int pack_impl(bool train, const float* U_stack, const float* W_stack, const float* W_forget_stack,
+                      const float* b_forget_stack, const float* dt_params, const float* mix_x_w,
+                      const float* mix_x_b, const float* norm_x_w, const float* mix_v_w,
+                      const float* mix_v_b, const float* norm_v_w, int dim, int heads, int rank,
+                      int num_layers, float* packed, long long packed_floats, gfn_stream_t stream) {
+  Layout L;
+  int st = make_layout(dim, heads, rank, num_layers, &L);
+  if (st) return st;
+  if (!U_stack || !W_stack || !W_forget_stack || !b_forget_stack || !dt_params || !packed)
+    return fail(GFN_ERR_INVALID, "pack: NULL head parameter");
+  if (L.mix && (!mix_x_w || !mix_v_w))
+    return fail(GFN_ERR_INVALID, "pack: heads > 1 needs the mixing weights");
+  const long long LFx = train ? L.LFT : L.LF;
+  const long long need = (long long)num_layers * L.K * LFx;
+  if (packed_floats < need) return fail(GFN_ERR_INVALID, "pack: buffer %lld < %lld floats", packed_floats, need);
+  if (!aligned16(packed)) return fail(GFN_ERR_ALIGN, "pack: output not 16-byte aligned");
+  PackArgs a;
+  a.U = U_stack; a.W = W_stack; a.Wf = W_forget_stack; a.bf = b_forget_stack; a.dtp = dt_params;
+  a.Wx = mix_x_w; a.bx = mix_x_b; a.gx = norm_x_w; a.Wv = mix_v_w; a.bv = mix_v_b; a.gv = norm_v_w;
+  a.out = packed; a.NL = num_layers; a.d = dim; a.H = heads; a.hd = L.hd; a.r = rank; a.K = L.K;
+  a.C = L.C; a.hpc = L.hpc; a.KC = L.KC; a.nchunk = L.nchunk; a.HS = L.HS; a.CF = L.CF; a.LF = LFx;
+  a.train = train ? 1 : 0; a.HST = L.HST;
+  long long blocks = (need + 255) / 256;
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  pack_kernel<<<(unsigned)blocks, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(a);
+  return launch_status("pack_kernel");
+}
+
+
+static int seq_forward_impl(bool train, float* traj, const float* x_init, const float* v_init,
+                                  long long state_row_stride, const float* forces_f32,
+                                  const void* forces_bf16, const long long* token_ids,
+                                  const float* embed_table, long long vocab, const float* mask,
+                                  const float* packed, long long packed_floats, int batch,
+                                  int seq_len, int dim, int heads, int rank, int num_layers,
+                                  float base_dt, float* x_seq, float* v_seq, float* x_final,
+                                  float* v_final, gfn_stream_t stream) {
+  Layout L;
+  int st = make_layout(dim, heads, rank, num_layers, &L);
+  if (st) return st;
+  if (batch < 0 || seq_len < 0) return fail(GFN_ERR_INVALID, "sequence: batch=%d seq_len=%d", batch, seq_len);
+  if (!x_init || !v_init || !packed) return fail(GFN_ERR_INVALID, "sequence: NULL state or weights");
+  if (state_row_stride < 0) return fail(GFN_ERR_INVALID, "sequence: negative state stride");
+  const int nsrc = (forces_f32 != nullptr) + (forces_bf16 != nullptr) + (token_ids != nullptr);
+  if (seq_len > 0 && nsrc != 1)
+    return fail(GFN_ERR_INVALID, "sequence: give exactly one of forces_f32, forces_bf16, token_ids");
+  if (token_ids && (!embed_table || vocab <= 0))
+    return fail(GFN_ERR_INVALID, "sequence: token_ids need embed_table and vocab > 0");
+  const long long LFx = train ? L.LFT : L.LF;
+  const long long need = (long long)num_layers * L.K * LFx;
+  if (packed_floats < need) return fail(GFN_ERR_INVALID, "sequence: packed %lld < %lld floats", packed_floats, need);
+  if (!aligned16(packed)) return fail(GFN_ERR_ALIGN, "sequence: packed weights not 16-byte aligned");
+  if (batch == 0) return GFN_OK;
+  DevInfo di;
+  st = dev_info(&di);
+  if (st) return st;
+  SeqPlan p;
+  st = make_plan(batch, L, di, &p);
+  if (st) return st;
+  SeqArgs a = {};
+  a.x0 = x_init; a.v0 = v_init; a.state_stride = state_row_stride;
+  a.f32 = forces_f32; a.fbf16 = reinterpret_cast<const __nv_bfloat16*>(forces_bf16);
+  a.ids = token_ids; a.table = embed_table; a.vocab = vocab; a.mask = mask; a.pack = packed;
+  a.x_seq = x_seq; a.v_seq = v_seq; a.x_out = x_final; a.v_out = v_final;
+  a.B = batch; a.L = seq_len; a.d = dim; a.H = heads; a.hd = L.hd; a.NL = num_layers;
+  a.K = L.K; a.R = p.R; a.C = L.C; a.hpc = L.hpc; a.KC = L.KC; a.nchunk = L.nchunk; a.NST = p.NST;
+  a.HS = L.HS; a.CF = L.CF; a.LF = LFx; a.mix = L.mix;
+  a.chunk_base = train ? L.HST : L.HS; a.traj = traj;
+  a.TR = p.TR; a.NG = p.NG; a.tiles = p.tiles; a.S = p.S;
+  a.base_dt = base_dt; a.prof = g_phase_prof;
+  a.o_head = p.o_head; a.o_chunk = p.o_chunk; a.o_ox = p.o_ox; a.o_ov = p.o_ov;
+  a.o_catx = p.o_catx; a.o_catv = p.o_catv; a.o_part = p.o_part;
+  a.logC = (L.C & (L.C - 1)) == 0 ? __builtin_ctz(L.C) : -1;
+  return launch_seq(seq_kernel_for(rank, seq_epl(L), p.NW), a, p,
+                    reinterpret_cast<cudaStream_t>(stream));
+}
+
 
 extern "C" {
 
@@ -377,25 +462,26 @@ int gfn_leapfrog_pack(const float* U_stack, const float* W_stack, const float* W
                       const float* mix_x_b, const float* norm_x_w, const float* mix_v_w,
                       const float* mix_v_b, const float* norm_v_w, int dim, int heads, int rank,
                       int num_layers, float* packed, long long packed_floats, gfn_stream_t stream) {
+  return pack_impl(false, U_stack, W_stack, W_forget_stack, b_forget_stack, dt_params, mix_x_w,
+                   mix_x_b, norm_x_w, mix_v_w, mix_v_b, norm_v_w, dim, heads, rank, num_layers,
+                   packed, packed_floats, stream);
+}
+
+long long gfn_leapfrog_pack_train_floats(int dim, int heads, int rank, int num_layers) {
   Layout L;
-  int st = make_layout(dim, heads, rank, num_layers, &L);
-  if (st) return st;
-  if (!U_stack || !W_stack || !W_forget_stack || !b_forget_stack || !dt_params || !packed)
-    return fail(GFN_ERR_INVALID, "pack: NULL head parameter");
-  if (L.mix && (!mix_x_w || !mix_v_w))
-    return fail(GFN_ERR_INVALID, "pack: heads > 1 needs the mixing weights");
-  const long long need = (long long)num_layers * L.K * L.LF;
-  if (packed_floats < need) return fail(GFN_ERR_INVALID, "pack: buffer %lld < %lld floats", packed_floats, need);
-  if (!aligned16(packed)) return fail(GFN_ERR_ALIGN, "pack: output not 16-byte aligned");
-  PackArgs a;
-  a.U = U_stack; a.W = W_stack; a.Wf = W_forget_stack; a.bf = b_forget_stack; a.dtp = dt_params;
-  a.Wx = mix_x_w; a.bx = mix_x_b; a.gx = norm_x_w; a.Wv = mix_v_w; a.bv = mix_v_b; a.gv = norm_v_w;
-  a.out = packed; a.NL = num_layers; a.d = dim; a.H = heads; a.hd = L.hd; a.r = rank; a.K = L.K;
-  a.C = L.C; a.hpc = L.hpc; a.KC = L.KC; a.nchunk = L.nchunk; a.HS = L.HS; a.CF = L.CF; a.LF = L.LF;
-  long long blocks = (need + 255) / 256;
-  if (blocks > 148 * 16) blocks = 148 * 16;
-  pack_kernel<<<(unsigned)blocks, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(a);
-  return launch_status("pack_kernel");
+  if (make_layout(dim, heads, rank, num_layers, &L) != GFN_OK) return -1;
+  return (long long)num_layers * L.K * L.LFT;
+}
+
+int gfn_leapfrog_pack_train(const float* U_stack, const float* W_stack,
+                            const float* W_forget_stack, const float* b_forget_stack,
+                            const float* dt_params, const float* mix_x_w, const float* mix_x_b,
+                            const float* norm_x_w, const float* mix_v_w, const float* mix_v_b,
+                            const float* norm_v_w, int dim, int heads, int rank, int num_layers,
+                            float* packed, long long packed_floats, gfn_stream_t stream) {
+  return pack_impl(true, U_stack, W_stack, W_forget_stack, b_forget_stack, dt_params, mix_x_w,
+                   mix_x_b, norm_x_w, mix_v_w, mix_v_b, norm_v_w, dim, heads, rank, num_layers,
+                   packed, packed_floats, stream);
 }
 
 int gfn_leapfrog_sequence_forward(const float* x_init, const float* v_init,
@@ -406,42 +492,26 @@ int gfn_leapfrog_sequence_forward(const float* x_init, const float* v_init,
                                   int seq_len, int dim, int heads, int rank, int num_layers,
                                   float base_dt, float* x_seq, float* v_seq, float* x_final,
                                   float* v_final, gfn_stream_t stream) {
-  Layout L;
-  int st = make_layout(dim, heads, rank, num_layers, &L);
-  if (st) return st;
-  if (batch < 0 || seq_len < 0) return fail(GFN_ERR_INVALID, "sequence: batch=%d seq_len=%d", batch, seq_len);
-  if (!x_init || !v_init || !packed) return fail(GFN_ERR_INVALID, "sequence: NULL state or weights");
-  if (state_row_stride < 0) return fail(GFN_ERR_INVALID, "sequence: negative state stride");
-  const int nsrc = (forces_f32 != nullptr) + (forces_bf16 != nullptr) + (token_ids != nullptr);
-  if (seq_len > 0 && nsrc != 1)
-    return fail(GFN_ERR_INVALID, "sequence: give exactly one of forces_f32, forces_bf16, token_ids");
-  if (token_ids && (!embed_table || vocab <= 0))
-    return fail(GFN_ERR_INVALID, "sequence: token_ids need embed_table and vocab > 0");
-  const long long need = (long long)num_layers * L.K * L.LF;
-  if (packed_floats < need) return fail(GFN_ERR_INVALID, "sequence: packed %lld < %lld floats", packed_floats, need);
-  if (!aligned16(packed)) return fail(GFN_ERR_ALIGN, "sequence: packed weights not 16-byte aligned");
-  if (batch == 0) return GFN_OK;
-  DevInfo di;
-  st = dev_info(&di);
-  if (st) return st;
-  SeqPlan p;
-  st = make_plan(batch, L, di, &p);
-  if (st) return st;
-  SeqArgs a = {};
-  a.x0 = x_init; a.v0 = v_init; a.state_stride = state_row_stride;
-  a.f32 = forces_f32; a.fbf16 = reinterpret_cast<const __nv_bfloat16*>(forces_bf16);
-  a.ids = token_ids; a.table = embed_table; a.vocab = vocab; a.mask = mask; a.pack = packed;
-  a.x_seq = x_seq; a.v_seq = v_seq; a.x_out = x_final; a.v_out = v_final;
-  a.B = batch; a.L = seq_len; a.d = dim; a.H = heads; a.hd = L.hd; a.NL = num_layers;
-  a.K = L.K; a.R = p.R; a.C = L.C; a.hpc = L.hpc; a.KC = L.KC; a.nchunk = L.nchunk; a.NST = p.NST;
-  a.HS = L.HS; a.CF = L.CF; a.LF = L.LF; a.mix = L.mix;
-  a.TR = p.TR; a.NG = p.NG; a.tiles = p.tiles; a.S = p.S;
-  a.base_dt = base_dt; a.prof = g_phase_prof;
-  a.o_head = p.o_head; a.o_chunk = p.o_chunk; a.o_ox = p.o_ox; a.o_ov = p.o_ov;
-  a.o_catx = p.o_catx; a.o_catv = p.o_catv; a.o_part = p.o_part;
-  a.logC = (L.C & (L.C - 1)) == 0 ? __builtin_ctz(L.C) : -1;
-  return launch_seq(seq_kernel_for(rank, seq_epl(L), p.NW), a, p,
-                    reinterpret_cast<cudaStream_t>(stream));
+  return seq_forward_impl(false, nullptr, x_init, v_init, state_row_stride, forces_f32, forces_bf16,
+                          token_ids, embed_table, vocab, mask, packed, packed_floats, batch, seq_len,
+                          dim, heads, rank, num_layers, base_dt, x_seq, v_seq, x_final, v_final,
+                          stream);
+}
+
+int gfn_leapfrog_sequence_forward_train(const float* x_init, const float* v_init,
+                                        long long state_row_stride, const float* forces_f32,
+                                        const void* forces_bf16, const long long* token_ids,
+                                        const float* embed_table, long long vocab,
+                                        const float* mask, const float* packed_train,
+                                        long long packed_floats, int batch, int seq_len, int dim,
+                                        int heads, int rank, int num_layers, float base_dt,
+                                        float* x_seq, float* v_seq, float* x_final, float* v_final,
+                                        float* traj, gfn_stream_t stream) {
+  if (!traj) return fail(GFN_ERR_INVALID, "forward_train: traj is NULL");
+  return seq_forward_impl(true, traj, x_init, v_init, state_row_stride, forces_f32, forces_bf16,
+                          token_ids, embed_table, vocab, mask, packed_train, packed_floats, batch,
+                          seq_len, dim, heads, rank, num_layers, base_dt, x_seq, v_seq, x_final,
+                          v_final, stream);
 }
 
 long long gfn_parallel_scan_workspace_floats(int batch, int seq_len, int dim) {
@@ -608,3 +678,172 @@ extern "C" int gfn_parallel_scan_noalloc(const float* a, const float* x, float* 
   scan_chunk_apply_kernel<<<dim3(gx, P), SCAN_THREADS, 0, cs>>>(s);
   return launch_status("scan_chunk kernels (no-alloc)");
 }
+
+// ---------------------------------------------------------------------------
+// BPTT backward
+namespace {
+
+struct BwdPlan {
+  SeqPlan s;  // rows, mixing tiles (NW = BWD_NW)
+  int NST, max_active;
+  size_t smem;
+  int o_head, o_chunk, o_ox, o_ov, o_catx, o_catv, o_dcx, o_dcv, o_part, o_part2, o_px, o_pv;
+};
+
+size_t bwd_smem(const Layout& L, int R, int NST, BwdPlan* p) {
+  int off = 0;
+  auto take = [&](int n) { int o = off; off += ((n + 31) / 32) * 32; return o; };
+  p->o_head = take(2 * L.HST);
+  p->o_chunk = take(L.mix ? NST * L.CF : 0);
+  p->o_ox = take(R * L.C);
+  p->o_ov = take(R * L.C);
+  p->o_catx = take(L.mix ? R * L.d : 0);
+  p->o_catv = take(L.mix ? R * L.d : 0);
+  p->o_dcx = take(L.mix ? R * L.d : 0);
+  p->o_dcv = take(L.mix ? R * L.d : 0);
+  p->o_part = take(L.mix ? L.K * R * 2 : 0);
+  p->o_part2 = take(L.mix ? L.K * R * 2 : 0);
+  p->o_px = take(R * L.C);
+  p->o_pv = take(R * L.C);
+  return SEQ_BAR_BYTES + (size_t)off * 4;
+}
+
+using BwdKernel = void (*)(BwdArgs);
+BwdKernel bwd_kernel_for(int r, int epl) {
+#define GFN_B(RK, E) if (r == RK && epl == E) return leapfrog_bwd_kernel<RK, E>;
+  GFN_B(4, 1) GFN_B(4, 2) GFN_B(8, 1) GFN_B(8, 2) GFN_B(16, 1) GFN_B(16, 2)
+#undef GFN_B
+  return nullptr;
+}
+
+int bwd_cfg(BwdKernel kern, const BwdPlan& p, int K, unsigned grid, cudaStream_t stream,
+            cudaLaunchConfig_t* cfg, cudaLaunchAttribute* attr) {
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.smem);
+  if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(bwd smem)");
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = K;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  *cfg = cudaLaunchConfig_t{};
+  cfg->gridDim = dim3(grid);
+  cfg->blockDim = dim3(BWD_THREADS);
+  cfg->dynamicSmemBytes = p.smem;
+  cfg->stream = stream;
+  cfg->attrs = attr;
+  cfg->numAttrs = 1;
+  return GFN_OK;
+}
+
+int make_bwd_plan(int B, const Layout& L, const DevInfo& di, BwdPlan* p) {
+  BwdKernel kern = bwd_kernel_for(L.r, seq_epl(L));
+  if (!kern) return fail(GFN_ERR_UNSUPPORTED, "backward: no kernel for rank %d head_dim %d (<= 64)", L.r, L.hd);
+  p->s.L = L;
+  p->s.NW = BWD_NW;
+  auto fit = [&](int R) -> bool {
+    if (R * L.hpc > BWD_NW * BWD_MAXU || !plan_rows(L, R, &p->s)) return false;
+    const int want = L.mix ? 2 * 2 * L.nchunk + 2 : 2;
+    for (int NST = want < SEQ_MAX_NST - 1 ? want : SEQ_MAX_NST - 1; NST >= 2; --NST) {
+      const size_t smem = bwd_smem(L, R, NST, p);
+      if (smem + 256 <= (size_t)di.max_smem) {  // 256 B: the kernels' static shared memory
+        p->NST = NST;
+        p->smem = smem;
+        return true;
+      }
+    }
+    return false;
+  };
+  int Rmax = 0;
+  for (int R = 1; R <= B && R <= BWD_NW * BWD_MAXU; ++R)
+    if (fit(R)) Rmax = R;
+  if (Rmax == 0) return fail(GFN_ERR_RESOURCES, "no backward plan fits shared memory");
+  const int per_wave = di.sms / L.K > 0 ? di.sms / L.K : 1;
+  int R = (B + per_wave - 1) / per_wave;
+  if (R < 1) R = 1;
+  if (R > Rmax) R = Rmax;
+  for (int it = 0; it < 8; ++it) {
+    if (!fit(R)) return fail(GFN_ERR_RESOURCES, "backward plan for %d rows does not fit", R);
+    cudaLaunchConfig_t cfg;
+    cudaLaunchAttribute attr[1];
+    int st = bwd_cfg(kern, *p, L.K, (unsigned)L.K, nullptr, &cfg, attr);
+    if (st) return st;
+    int active = 0;
+    cudaError_t e = cudaOccupancyMaxActiveClusters(&active, kern, &cfg);
+    if (e != cudaSuccess) return cuda_status(e, "cudaOccupancyMaxActiveClusters(bwd)");
+    if (active <= 0) return fail(GFN_ERR_RESOURCES, "backward: a %d-CTA cluster cannot be scheduled", L.K);
+    p->max_active = active;
+    const int need = (B + active - 1) / active;
+    if (need <= R || R == Rmax) break;
+    R = need < Rmax ? need : Rmax;
+  }
+  p->s.nclusters = (B + p->s.R - 1) / p->s.R;
+  return GFN_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+long long gfn_leapfrog_backward_workspace_floats(int batch, int seq_len, int dim, int heads,
+                                                 int rank, int num_layers) {
+  if (batch < 0 || seq_len < 0 || dim <= 0 || heads <= 0 || rank <= 0 || num_layers <= 0) return -1;
+  const long long steps = (long long)num_layers * seq_len * batch;
+  return BWD_NSIG * steps * dim + BWD_NSMALL * steps * heads * rank + steps * heads;
+}
+
+int gfn_leapfrog_sequence_backward(const float* traj, const float* forces_f32,
+                                   const void* forces_bf16, const long long* token_ids,
+                                   const float* embed_table, long long vocab, const float* mask,
+                                   const float* packed_train, long long packed_floats,
+                                   const float* gx_seq, const float* gv_seq,
+                                   const float* gx_final, const float* gv_final, int batch,
+                                   int seq_len, int dim, int heads, int rank, int num_layers,
+                                   float base_dt, float* dx_init, float* dv_init, float* d_forces,
+                                   float* workspace, long long workspace_floats,
+                                   gfn_stream_t stream) {
+  Layout L;
+  int st = make_layout(dim, heads, rank, num_layers, &L);
+  if (st) return st;
+  if (batch < 0 || seq_len < 0) return fail(GFN_ERR_INVALID, "backward: bad sizes");
+  if (!traj || !packed_train || !dx_init || !dv_init || !workspace)
+    return fail(GFN_ERR_INVALID, "backward: NULL traj, weights, output or workspace");
+  const int nsrc = (forces_f32 != nullptr) + (forces_bf16 != nullptr) + (token_ids != nullptr);
+  if (seq_len > 0 && nsrc != 1)
+    return fail(GFN_ERR_INVALID, "backward: give exactly one force source (as in the forward)");
+  const long long need = (long long)num_layers * L.K * L.LFT;
+  if (packed_floats < need) return fail(GFN_ERR_INVALID, "backward: packed %lld < %lld floats", packed_floats, need);
+  const long long wneed = gfn_leapfrog_backward_workspace_floats(batch, seq_len, dim, heads, rank, num_layers);
+  if (workspace_floats < wneed)
+    return fail(GFN_ERR_INVALID, "backward: workspace %lld < %lld floats", workspace_floats, wneed);
+  if (!aligned16(packed_train)) return fail(GFN_ERR_ALIGN, "backward: packed weights not 16-byte aligned");
+  if (batch == 0 || seq_len == 0) return GFN_OK;
+  DevInfo di;
+  st = dev_info(&di);
+  if (st) return st;
+  BwdPlan p;
+  st = make_bwd_plan(batch, L, di, &p);
+  if (st) return st;
+  BwdArgs a = {};
+  a.f32 = forces_f32; a.fbf16 = reinterpret_cast<const __nv_bfloat16*>(forces_bf16);
+  a.ids = token_ids; a.table = embed_table; a.vocab = vocab; a.mask = mask;
+  a.pack = packed_train; a.traj = traj; a.gx_seq = gx_seq; a.gv_seq = gv_seq;
+  a.gx_fin = gx_final; a.gv_fin = gv_final; a.dx0 = dx_init; a.dv0 = dv_init; a.dforces = d_forces;
+  a.ws = workspace;
+  a.B = batch; a.L = seq_len; a.d = dim; a.H = heads; a.hd = L.hd; a.NL = num_layers;
+  a.K = L.K; a.R = p.s.R; a.C = L.C; a.hpc = L.hpc; a.KC = L.KC; a.nchunk = L.nchunk; a.NST = p.NST;
+  a.HS = L.HS; a.HST = L.HST; a.CF = L.CF; a.LF = L.LFT; a.mix = L.mix;
+  a.TR = p.s.TR; a.NG = p.s.NG; a.tiles = p.s.tiles; a.S = p.s.S;
+  a.logC = (L.C & (L.C - 1)) == 0 ? __builtin_ctz(L.C) : -1;
+  a.base_dt = base_dt;
+  a.o_head = p.o_head; a.o_chunk = p.o_chunk; a.o_ox = p.o_ox; a.o_ov = p.o_ov;
+  a.o_catx = p.o_catx; a.o_catv = p.o_catv; a.o_dcx = p.o_dcx; a.o_dcv = p.o_dcv;
+  a.o_part = p.o_part; a.o_part2 = p.o_part2; a.o_px = p.o_px; a.o_pv = p.o_pv;
+  BwdKernel kern = bwd_kernel_for(rank, seq_epl(L));
+  cudaLaunchConfig_t cfg;
+  cudaLaunchAttribute attr[1];
+  st = bwd_cfg(kern, p, L.K, (unsigned)(p.s.nclusters * L.K), reinterpret_cast<cudaStream_t>(stream),
+               &cfg, attr);
+  if (st) return st;
+  return cuda_status(cudaLaunchKernelEx(&cfg, kern, a), "leapfrog_bwd_kernel launch");
+}
+
+}  // extern "C"

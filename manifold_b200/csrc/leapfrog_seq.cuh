@@ -105,6 +105,8 @@ struct SeqArgs {
   int logC;               // log2(C) when C is a power of two, else -1
   float base_dt;
   int o_head, o_chunk, o_ox, o_ov, o_catx, o_catv, o_part;
+  int chunk_base;   // offset of the first weight chunk in a (layer, CTA) pack run
+  float* traj;      // optional [2][NL][L][B][d]: every layer step's input (x, v), for BPTT
 };
 
 // ---------------------------------------------------------------- PTX bits
@@ -391,7 +393,7 @@ __global__ void __launch_bounds__(SeqShape<NW>::THREADS, 1) leapfrog_seq_kernel(
           if (!first_lap) mbar_wait(&chunk_empty[slot], empty_phase, 128);
           mbar_arrive_expect_tx(&chunk_full[slot], (uint32_t)a.CF * 4u);
           bulk_g2s(chunk_ring + (long long)slot * a.CF,
-                   my_pack + l * layer_stride + a.HS + (long long)i * a.CF, (uint32_t)a.CF * 4u,
+                   my_pack + l * layer_stride + a.chunk_base + (long long)i * a.CF, (uint32_t)a.CF * 4u,
                    &chunk_full[slot]);
           if (++slot == a.NST) {
             slot = 0;
@@ -490,6 +492,20 @@ __global__ void __launch_bounds__(SeqShape<NW>::THREADS, 1) leapfrog_seq_kernel(
       const float* hs = head_ring + hslot * a.HS;
       mbar_wait(&head_full[hslot], (uint32_t)((g >> 1) & 1));
       mark(0);
+      if (a.traj) {  // checkpoint of this layer step's input for the backward
+        const long long BD = (long long)a.B * d;
+        const long long so = ((long long)l * a.L + t) * BD;
+#pragma unroll
+        for (int i = 0; i < SEQ_MAXU; ++i)
+#pragma unroll
+          for (int e = 0; e < EPL; ++e) {
+            const int b = row0 + urow[i];
+            if (!uok[i] || !eok[e] || b >= a.B) continue;
+            const long long off = so + (long long)b * d + col0 + uhl[i] * hd + jj[e];
+            a.traj[off] = xr[i][e];
+            a.traj[(long long)a.NL * a.L * BD + off] = vr[i][e];
+          }
+      }
 
       // ---- head step of every unit, in registers
 #pragma unroll

@@ -24,6 +24,12 @@ struct PackArgs {
   float* out;
   int NL, d, H, hd, r, K, C, hpc, KC, nchunk, HS, CF;
   long long LF;
+  // Training layout (train != 0): after the head section, the forget-gate
+  // weight untransposed [hpc][j][k] (padded to HST floats in total), then the
+  // nchunk forward chunks, then nchunk transposed chunks: element [kk][n] of
+  // transposed chunk i is Wx[i*KC + kk][c*C + n] (v columns after x), the
+  // operand of dx_cat = Wx^T dz for this CTA's input columns.
+  int train, HST;
 };
 
 __global__ void pack_kernel(const PackArgs a) {
@@ -38,7 +44,14 @@ __global__ void pack_kernel(const PackArgs a) {
     const int c = (int)(rem / a.LF);
     const long long off = rem - (long long)c * a.LF;
     float val = 0.f;
-    if (off < a.HS) {
+    const int chunk_base = a.train ? a.HST : a.HS;
+    if (a.train && off >= a.HS && off < a.HST) {
+      const int o2 = (int)(off - a.HS);
+      if (o2 < a.hpc * hd * hd) {
+        const int hl = o2 / (hd * hd), r2 = o2 - hl * hd * hd;
+        val = a.Wf[((long long)l * a.H + c * a.hpc + hl) * hd * hd + r2];
+      }
+    } else if (off < a.HS) {
       const int o = (int)off;
       if (o < ho.U) {
         const int hl = o / (hd * hd), r2 = o - hl * hd * hd, k = r2 / hd, jj = r2 - k * hd;
@@ -61,13 +74,20 @@ __global__ void pack_kernel(const PackArgs a) {
         val = softplus_f(a.dtp[(long long)l * a.H + c * a.hpc + (o - ho.sc)]);
       }
     } else {
-      const long long o2 = off - a.HS;
-      const int i = (int)(o2 / a.CF);
-      const int e2 = (int)(o2 - (long long)i * a.CF);
+      const long long o2 = off - chunk_base;
+      int i = (int)(o2 / a.CF);
+      const bool transposed = i >= a.nchunk;
+      if (transposed) i -= a.nchunk;
+      const int e2 = (int)(o2 - (long long)(transposed ? i + a.nchunk : i) * a.CF);
       const int CS = chunk_row_stride(C);
       const int kk = e2 / CS, n = e2 - kk * CS;
       const int k = i * a.KC + kk;
-      if (k < d && n < 2 * C) {
+      if (k < d && n < 2 * C && transposed) {
+        if (n < C)
+          val = a.Wx[((long long)l * d + k) * d + (long long)c * C + n];
+        else
+          val = a.Wv[((long long)l * d + k) * d + (long long)c * C + n - C];
+      } else if (k < d && n < 2 * C) {
         if (n < C)
           val = a.Wx[((long long)l * d + (long long)c * C + n) * d + k];
         else

@@ -116,6 +116,11 @@ class MLayer(nn.Module):
         packed, meta = self._pack.get([self])
         if force is None:
             force = torch.zeros_like(x)
+        if torch.is_grad_enabled() and any(t.requires_grad for t in
+                                           [x, v, force, *self.parameters()]):
+            from .training import leapfrog_sequence_train
+            _, _, xn, vn = leapfrog_sequence_train([self], x, v, force.reshape(B, 1, self.dim))
+            return xn, vn, torch.ones(B, self.heads, device=x.device, dtype=x.dtype), []
         _, _, xn, vn = ops.leapfrog_sequence(x, v, packed, meta, self.base_dt,
                                              forces=force.reshape(B, 1, self.dim),
                                              want_x_seq=False, want_v_seq=False)
