@@ -38,6 +38,10 @@ CONFIGS = {
     "c3": dict(V=50257, d=512, NL=12, H=8, rank=32, B=256, dt=0.1, chunk=64, functional=True,
                workload="C3 LM prefill: bf16 functional-embedding forces, fp32 state, d=512, "
                         "12 layers, 8 heads, batch 256"),
+    "c5": dict(V=32000, d=512, NL=8, H=8, rank=32, B=64, dt=0.1, chunk=1024, train=True,
+               workload="C5 BPTT training step fp32: d=512, 8 layers, 8 heads, rank 32, leapfrog, "
+                        "batch 64 per GPU, L=1024, Zipf ids over 32000, next-token CE, Adam; "
+                        "NCCL gradient all-reduce when N > 1"),
     "c1": dict(V=2, d=128, NL=4, H=4, rank=16, B=32, dt=0.1, chunk=20, parity=True,
                workload="C1 cumulative parity fp32: d=128, 4 layers, 4 heads, batch 32, L=20"),
 }
@@ -142,6 +146,102 @@ def make_ids(c, B, T, seed):
     if c.get("functional"):
         return C.zipf_ids(rng, c["V"], (B, T))
     return rng.integers(0, c["V"], (B, T)).astype(np.int64)
+
+
+def run_train(args, c):
+    """One step = forward (trajectory stored) + readout + next-token CE +
+    BPTT backward + gradient all-reduce (N > 1) + Adam step."""
+    import torch
+    import torch.distributed as dist
+    from manifold_b200.distributed import allreduce_gradients
+    from tests.golden import cases as C
+    world, rank, local = dist_env()
+    if world > 1:
+        dist.init_process_group("nccl")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    import manifold_b200 as gfn
+    cfg = dict(c, seed=1234)
+    P = C.make_params(dict(cfg, V=2))  # seeded layer weights; the embedding keeps its init
+    torch.manual_seed(0)
+    m = gfn.Manifold(**C.model_kwargs(cfg)).to(dev).train()
+    for layer, lp in zip(m.layers, P["layers"]):
+        C.load_into_layer(layer, cfg, lp)
+    params = list(m.parameters())
+    opt = torch.optim.Adam(params, lr=1e-4)
+    B, T, V = c["B"], args.chunk or c["chunk"], c["V"]
+    steps, warm = args.steps, args.warmup
+    host = [torch.from_numpy(make_ids(c, B, T + 1, 100 * rank + i)).pin_memory() for i in range(steps + warm)]
+    ce = torch.nn.CrossEntropyLoss()
+    stream = torch.cuda.current_stream(dev)
+    flush = torch.empty(256 * 1024 * 1024 // 4, device=dev, dtype=torch.float32)
+
+    def step(i):
+        ids = host[i].to(dev, non_blocking=True)
+        logits = m(ids[:, :T])[0]
+        loss = ce(logits.reshape(-1, V), ids[:, 1:].reshape(-1))
+        loss.backward()
+        if world > 1:
+            allreduce_gradients(params)
+        opt.step()
+        opt.zero_grad(set_to_none=True)
+        return loss
+
+    for i in range(warm):
+        step(i)
+    torch.cuda.synchronize(dev)
+    sampler = ClockSampler(local) if rank == 0 else None
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    if sampler:
+        sampler.start()
+        time.sleep(0.3)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    losses = []
+    for i in range(steps):
+        flush.zero_()
+        ev[i][0].record(stream)
+        loss = step(warm + i)
+        lv = loss.item()  # device -> host read of the step's result
+        ev[i][1].record(stream)
+        losses.append(lv)
+    torch.cuda.synchronize(dev)
+    clocks = sampler.stop() if sampler else None
+    ms = sum(a.elapsed_time(b) for a, b in ev)
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = t.item()
+    result = None
+    if rank == 0:
+        hbm, _, kind = measured_peaks()
+        tokens = world * B * T * steps
+        value = tokens / (ms / 1e3)
+        result = {
+            "metric": "recurrent tokens/sec (prefill+decode)",
+            "value": round(value, 1), "unit": "tokens/s", "n_gpus": world, "steps": steps,
+            "warmup": warm, "ms_per_step": round(ms / steps, 3), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded Zipf ids; seeded random weights)",
+            "config": {"workload": c["workload"], "batch_per_gpu": B, "tokens_per_step": T,
+                       "dim": c["d"], "layers": c["NL"], "heads": c["H"], "rank": c["rank"],
+                       "l2": "flushed (256 MB write) between timed steps",
+                       "parallelism": f"dp{world}"},
+            "e2e": {"value": round(value, 1), "unit": "tokens/s",
+                    "h2d_bytes_per_step": int(B * (T + 1) * 8), "d2h_bytes_per_step": 4,
+                    "note": "each timed step already copies its ids from pinned host memory and reads the loss back"},
+            "gpu_launches": steps * 4,
+            "roofline": {"bound": "hbm", "achieved": None, "peak": hbm, "unit": "GB/s", "frac": None,
+                         "traffic": None, "peak_source": kind,
+                         "note": "training step: recurrence forward + backward kernels, cuBLAS readout/CE and weight-gradient GEMMs"},
+            "loss": [round(x, 4) for x in losses],
+            "clocks": clocks,
+        }
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return result
 
 
 def run_ours(args, c):
@@ -363,7 +463,7 @@ def main():
     if args.impl == "reference":
         out = run_reference(args, c)
     else:
-        out = run_ours(args, c)
+        out = run_train(args, c) if c.get("train") else run_ours(args, c)
     if out is not None:
         print(json.dumps(out), flush=True)
 
