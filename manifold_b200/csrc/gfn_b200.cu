@@ -200,9 +200,11 @@ int make_plan(int B, const Layout& L, const DevInfo& di, SeqPlan* p) {
     // Ring depth: up to two layers of chunks (+2), so the copies of the next
     // layer's weights are in flight a whole layer ahead, as shared memory allows.
     const int want = L.mix ? 2 * L.nchunk + 2 : 2;
+    // two CTAs per SM for the 8-warp form: each gets a bit under half the SM
+    const size_t budget = p->NW == 8 ? (size_t)114 * 1024 : (size_t)di.max_smem;
     for (int NST = want < SEQ_MAX_NST ? want : SEQ_MAX_NST; NST >= 2; --NST) {
       const size_t smem = plan_smem(L, R, NST, p);
-      if (smem + 256 <= (size_t)di.max_smem) {  // 256 B: the kernels' static shared memory
+      if (smem + 256 <= budget) {  // 256 B: the kernels' static shared memory
         p->NST = NST;
         p->smem = smem;
         return true;
@@ -215,10 +217,9 @@ int make_plan(int B, const Layout& L, const DevInfo& di, SeqPlan* p) {
     if (fit(R)) Rmax = R;
   if (Rmax == 0)
     return fail(GFN_ERR_RESOURCES, "no sequence plan fits %d bytes of shared memory", di.max_smem);
-  const int per_wave = di.sms / L.K > 0 ? di.sms / L.K : 1;
-  int R = (B + per_wave - 1) / per_wave;
-  if (R < 1) R = 1;
-  if (R > Rmax) R = Rmax;
+  // Fewest rows per cluster (most clusters, shortest per-CTA chain) such
+  // that every cluster is resident in one wave.
+  int R = 1;
   for (int it = 0; it < 8; ++it) {
     if (!fit(R)) return fail(GFN_ERR_RESOURCES, "sequence plan for %d rows does not fit", R);
     int active = 0;

@@ -48,6 +48,9 @@ struct SeqShape {
   static constexpr int CTHREADS = NW * 32;
   static constexpr int THREADS = CTHREADS + 32;
   static constexpr int MAXU = NW == 8 ? 3 : 2;  // units per warp: R*hpc <= NW*MAXU
+  // The 8-warp form runs two CTAs per SM (two independent row blocks whose
+  // dependent chains interleave); the 16-warp form one.
+  static constexpr int MINB = NW == 8 ? 2 : 1;
 };
 constexpr int SEQ_NBAR = 48;                        // mbarrier slots reserved
 constexpr int SEQ_BAR_BYTES = SEQ_NBAR * 8;
@@ -325,7 +328,7 @@ GFN_DEV void unit_friction(const float (&xx)[EPL], const float* __restrict__ WfT
 }
 
 template <int RK, int EPL, int NW>
-__global__ void __launch_bounds__(SeqShape<NW>::THREADS, 1) leapfrog_seq_kernel(const SeqArgs a) {
+__global__ void __launch_bounds__(SeqShape<NW>::THREADS, SeqShape<NW>::MINB) leapfrog_seq_kernel(const SeqArgs a) {
   constexpr int SEQ_CWARPS = SeqShape<NW>::CWARPS;
   constexpr int SEQ_CTHREADS = SeqShape<NW>::CTHREADS;
   constexpr int SEQ_MAXU = SeqShape<NW>::MAXU;
