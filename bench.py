@@ -261,7 +261,11 @@ def run_ours(args, c):
     ids_dev = [t.to(dev) for t in ids_host]
     flush = torch.empty(256 * 1024 * 1024 // 4, device=dev, dtype=torch.float32)
     stream = torch.cuda.current_stream(dev)
-    packed, meta = m._pack.get(list(m.layers))
+    if args.path != "auto":
+        m.recurrence_path = args.path
+    layered = m._use_layered(B)
+    packed, meta = m._pack.get(list(m.layers), layered=layered)
+    seqfn = ops.leapfrog_layered_sequence if layered else ops.leapfrog_sequence
     if c.get("functional"):
         m.force_dtype = torch.bfloat16
 
@@ -273,12 +277,12 @@ def run_ours(args, c):
         with torch.no_grad():
             if c.get("functional"):
                 forces = m.embedding(ids_dev[i], out_dtype=torch.bfloat16)
-                xs, vs, xf, vf = ops.leapfrog_sequence(state[0], state[1], packed, meta, c["dt"],
-                                                       forces=forces, want_v_seq=want_v)
+                xs, vs, xf, vf = seqfn(state[0], state[1], packed, meta, c["dt"],
+                                       forces=forces, want_v_seq=want_v)
             else:
-                xs, vs, xf, vf = ops.leapfrog_sequence(state[0], state[1], packed, meta, c["dt"],
-                                                       ids=ids_dev[i], table=m.embedding.weight,
-                                                       want_v_seq=want_v)
+                xs, vs, xf, vf = seqfn(state[0], state[1], packed, meta, c["dt"],
+                                       ids=ids_dev[i], table=m.embedding.weight,
+                                       want_v_seq=want_v)
         return (xf, vf)
 
     state = (x, v)
@@ -363,7 +367,10 @@ def run_ours(args, c):
                        "plan": plan},
             "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s",
                     "h2d_bytes_per_step": int(B * T * 8), "d2h_bytes_per_step": int(2 * B * c["d"] * 4)},
-            "gpu_launches": steps * (2 if c.get("functional") else 1),
+            "gpu_launches": steps * ((2 * c["NL"] + 1) * T if layered else 1)
+            + (steps if c.get("functional") else 0),
+            "recurrence_path": "layered (head-step kernel + fp32 cuBLAS mixing GEMM per layer)"
+            if layered else "fused persistent cluster kernel",
             "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": hbm, "unit": "GB/s",
                          "frac": round(achieved / hbm, 5), "traffic": None,
                          "peak_source": peak_kind,
@@ -456,6 +463,8 @@ def main():
     ap.add_argument("--chunk", type=int, default=0, help="tokens per step (default per config)")
     ap.add_argument("--cpu-tokens", type=int, default=0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--path", default="auto", choices=["auto", "fused", "layered"],
+                    help="recurrence path (auto: by batch size)")
     ap.add_argument("--phase-profile", action="store_true",
                     help="print per-phase cycle counts of CTA 0 for one step instead")
     args = ap.parse_args()

@@ -199,6 +199,35 @@ int gfn_leapfrog_sequence_backward(const float* traj, const float* forces_f32,
                                    gfn_stream_t stream);
 
 /* ------------------------------------------------------------------------
+ * Layer-by-layer form of gfn_leapfrog_sequence_forward for large batches
+ * (heads > 1).  Same semantics, operands and results (gfn/model.py:377-402
+ * per token, gfn/layers/base.py:198-338 per layer); per token and layer it
+ * runs a head-step kernel (previous layer's RMSNorm/saturation fused in) and
+ * one batched fp32 GEMM (cuBLAS, no TF32) for both mixing projections, so
+ * the d x d mixing runs at GEMM rate when batch * dim is large.
+ * `packed` comes from gfn_leapfrog_layered_pack (same operands as
+ * gfn_leapfrog_pack); `workspace` holds at least
+ * gfn_leapfrog_layered_workspace_floats(batch, dim) floats.
+ */
+long long gfn_leapfrog_layered_pack_floats(int dim, int heads, int rank, int num_layers);
+int gfn_leapfrog_layered_pack(const float* U_stack, const float* W_stack,
+                              const float* W_forget_stack, const float* b_forget_stack,
+                              const float* dt_params, const float* mix_x_w, const float* mix_x_b,
+                              const float* norm_x_w, const float* mix_v_w, const float* mix_v_b,
+                              const float* norm_v_w, int dim, int heads, int rank, int num_layers,
+                              float* packed, long long packed_floats, gfn_stream_t stream);
+long long gfn_leapfrog_layered_workspace_floats(int batch, int dim);
+int gfn_leapfrog_layered_forward(const float* x_init, const float* v_init,
+                                 long long state_row_stride, const float* forces_f32,
+                                 const void* forces_bf16, const long long* token_ids,
+                                 const float* embed_table, long long vocab, const float* mask,
+                                 const float* packed, long long packed_floats, int batch,
+                                 int seq_len, int dim, int heads, int rank, int num_layers,
+                                 float base_dt, float* x_seq, float* v_seq, float* x_final,
+                                 float* v_final, float* workspace, long long workspace_floats,
+                                 gfn_stream_t stream);
+
+/* ------------------------------------------------------------------------
  * y_t = a_t y_{t-1} + x_t along t of [batch, seq_len, dim] (a NULL: a == 1).
  * Replaces parallel_scan_fused (gfn/cuda/src/layers/parallel_scan_fused.cu:81,
  * called from gfn/scan.py:20); semantics gfn/scan.py:11-104.

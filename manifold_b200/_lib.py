@@ -42,6 +42,12 @@ _SIGS = {
     "gfn_leapfrog_backward_workspace_floats": [_i, _i, _i, _i, _i, _i],
     "gfn_leapfrog_sequence_backward": [_p, _p, _p, _p, _p, _ll, _p, _p, _ll, _p, _p, _p, _p, _i, _i,
                                        _i, _i, _i, _i, _f, _p, _p, _p, _p, _ll, _p],
+    "gfn_leapfrog_layered_pack_floats": [_i, _i, _i, _i],
+    "gfn_leapfrog_layered_pack": [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i, _i, _i, _i, _p, _ll,
+                                  _p],
+    "gfn_leapfrog_layered_workspace_floats": [_i, _i],
+    "gfn_leapfrog_layered_forward": [_p, _p, _ll, _p, _p, _p, _p, _ll, _p, _p, _ll, _i, _i, _i, _i,
+                                     _i, _i, _f, _p, _p, _p, _p, _p, _ll, _p],
     "gfn_parallel_scan": [_p, _p, _p, _p, _ll, _i, _i, _i, _p],
     "gfn_parallel_scan_noalloc": [_p, _p, _p, _i, _i, _i, _p],
     "gfn_parallel_layer_scan": [_p, _p, _p, _i, _i, _i, _i, _f, _p],
@@ -55,6 +61,8 @@ _RESTYPES = {
     "gfn_parallel_scan_workspace_floats": ctypes.c_longlong,
     "gfn_leapfrog_pack_train_floats": ctypes.c_longlong,
     "gfn_leapfrog_backward_workspace_floats": ctypes.c_longlong,
+    "gfn_leapfrog_layered_pack_floats": ctypes.c_longlong,
+    "gfn_leapfrog_layered_workspace_floats": ctypes.c_longlong,
 }
 
 EXPORTED = tuple(_SIGS)

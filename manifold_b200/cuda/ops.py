@@ -133,6 +133,74 @@ def leapfrog_sequence(x0, v0, packed, meta, base_dt, forces=None, ids=None, tabl
     return x_seq, v_seq, x_f, v_f
 
 
+def leapfrog_layered_pack(U_stack, W_stack, Wf_stack, bf_stack, dt_params, mix):
+    """Pack stacked layer parameters for leapfrog_layered_sequence (heads > 1).
+
+    Same operands as leapfrog_pack; the layout keeps each head's weights
+    contiguous and the mixing matrices [out][in] for the batched GEMM.
+    """
+    NLH, hd, r = U_stack.shape
+    dev = U_stack.device
+    args = [_f32c(t, "stack") for t in (U_stack, W_stack, Wf_stack, bf_stack, dt_params)]
+    if mix is None:
+        raise GfnError("the layered path needs head mixing (heads > 1)")
+    mix = [_f32c(t, "mix") for t in mix]
+    num_layers, d, _ = mix[0].shape
+    heads = d // hd
+    n = _lib.load().gfn_leapfrog_layered_pack_floats(d, heads, r, num_layers)
+    if n < 0:
+        raise GfnError(f"layered pack: unsupported shape d={d} heads={heads} rank={r}")
+    packed = torch.empty(int(n), device=dev, dtype=torch.float32)
+    call("gfn_leapfrog_layered_pack", *[ptr(t) for t in args], *[ptr(t) for t in mix], d, heads, r,
+         num_layers, ptr(packed), packed.numel(), _lib.stream_of(dev))
+    return packed, dict(dim=d, heads=heads, rank=r, num_layers=num_layers, layered=True)
+
+
+def leapfrog_layered_sequence(x0, v0, packed, meta, base_dt, forces=None, ids=None, table=None,
+                              mask=None, want_x_seq=True, want_v_seq=True, workspace=None):
+    """leapfrog_sequence computed layer by layer (head step kernel + fp32
+    cuBLAS mixing GEMM per layer); the choice for large batches."""
+    require_cuda(x0, v0, packed, forces, ids, table, mask)
+    d = meta["dim"]
+    x0 = _f32c(x0, "x0")
+    v0 = _f32c(v0, "v0")
+    if forces is not None:
+        B, L, _ = forces.shape
+        forces = forces.contiguous()
+    elif ids is not None:
+        B, L = ids.shape
+        ids = ids.to(torch.int64).contiguous()
+        table = _f32c(table, "table")
+    else:
+        raise GfnError("leapfrog_layered_sequence needs forces or ids")
+    if x0.dim() == 1 or x0.shape[0] == 1:
+        stride = 0
+    else:
+        if x0.shape != (B, d) or v0.shape != (B, d):
+            raise GfnError(f"state must be [B={B}, d={d}]")
+        stride = d
+    dev = x0.device
+    x_seq = torch.empty(B, L, d, device=dev, dtype=torch.float32) if want_x_seq else None
+    v_seq = torch.empty(B, L, d, device=dev, dtype=torch.float32) if want_v_seq else None
+    x_f = torch.empty(B, d, device=dev, dtype=torch.float32)
+    v_f = torch.empty(B, d, device=dev, dtype=torch.float32)
+    f32 = forces if (forces is not None and forces.dtype == torch.float32) else None
+    fbf = forces if (forces is not None and forces.dtype == torch.bfloat16) else None
+    if forces is not None and f32 is None and fbf is None:
+        raise GfnError(f"forces must be float32 or bfloat16, got {forces.dtype}")
+    if mask is not None:
+        mask = mask.to(torch.float32).contiguous()
+    nws = _lib.load().gfn_leapfrog_layered_workspace_floats(B, d)
+    if workspace is None or workspace.numel() < nws:
+        workspace = torch.empty(int(nws), device=dev, dtype=torch.float32)
+    call("gfn_leapfrog_layered_forward", ptr(x0), ptr(v0), stride, ptr(f32), ptr(fbf), ptr(ids),
+         ptr(table), table.shape[0] if table is not None else 0, ptr(mask), ptr(packed),
+         packed.numel(), B, L, d, meta["heads"], meta["rank"], meta["num_layers"],
+         float(base_dt), ptr(x_seq), ptr(v_seq), ptr(x_f), ptr(v_f), ptr(workspace),
+         workspace.numel(), _lib.stream_of(dev))
+    return x_seq, v_seq, x_f, v_f
+
+
 def leapfrog_plan(batch, dim, heads, rank, num_layers):
     import ctypes
     out = (ctypes.c_int * 8)()

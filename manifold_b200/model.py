@@ -17,6 +17,10 @@ from .embeddings import FunctionalEmbedding, ImplicitEmbedding
 from .layers import MLayer, ParallelMLayer
 from .packing import PackCache
 
+# batch * dim from which recurrence() takes the layer-by-layer path (the
+# mixing becomes a GEMM with enough rows to fill the tensor-less fp32 pipes)
+LAYERED_MIN_ELEMS = 1 << 20
+
 
 class ImplicitReadout(nn.Module):
     """MLP readout to coordinate logits (gfn/readout.py:4-72)."""
@@ -130,6 +134,17 @@ class Manifold(nn.Module):
             return self.embedding(input_ids, out_dtype=self.force_dtype)
         return self.embedding(input_ids)
 
+    def _use_layered(self, batch):
+        """Layer-by-layer path (head-step kernel + fp32 GEMM mixing) for
+        large batches, the fused persistent kernel otherwise.  `recurrence_path`
+        ("auto", "fused", "layered") overrides the choice."""
+        path = getattr(self, "recurrence_path", "auto")
+        if self.heads == 1 or path == "fused":
+            return False
+        if path == "layered":
+            return True
+        return batch * self.dim >= LAYERED_MIN_ELEMS
+
     def recurrence(self, input_ids=None, attention_mask=None, state=None, force_manual=None,
                    want_v_seq=True):
         """The recurrence alone: (x_seq [B,L,d], v_seq [B,L,d] or None, (x, v), forces).
@@ -140,7 +155,10 @@ class Manifold(nn.Module):
             raise GfnError("recurrence() is the leapfrog loop path; use forward() for use_scan")
         src = force_manual if force_manual is not None else input_ids
         require_cuda(src)
-        packed, meta = self._pack.get(list(self.layers))
+        B = src.shape[0]
+        layered = self._use_layered(B)
+        packed, meta = self._pack.get(list(self.layers), layered=layered)
+        seq = ops.leapfrog_layered_sequence if layered else ops.leapfrog_sequence
         if state is None:
             x, v = self.x0, self.v0
         else:
@@ -148,14 +166,13 @@ class Manifold(nn.Module):
         mask = attention_mask
         base_dt = self.layers[0].base_dt
         if force_manual is None and isinstance(self.embedding, nn.Embedding):
-            x_seq, v_seq, xf, vf = ops.leapfrog_sequence(x, v, packed, meta, base_dt, ids=input_ids,
-                                                         table=self.embedding.weight, mask=mask,
-                                                         want_v_seq=want_v_seq)
+            x_seq, v_seq, xf, vf = seq(x, v, packed, meta, base_dt, ids=input_ids,
+                                       table=self.embedding.weight, mask=mask, want_v_seq=want_v_seq)
             forces = None
         else:
             forces = self._forces(input_ids, force_manual)
-            x_seq, v_seq, xf, vf = ops.leapfrog_sequence(x, v, packed, meta, base_dt, forces=forces,
-                                                         mask=mask, want_v_seq=want_v_seq)
+            x_seq, v_seq, xf, vf = seq(x, v, packed, meta, base_dt, forces=forces, mask=mask,
+                                       want_v_seq=want_v_seq)
         return x_seq, v_seq, (xf, vf), forces
 
     def forward(self, input_ids=None, attention_mask=None, state=None, force_manual=None,

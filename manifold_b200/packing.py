@@ -44,17 +44,31 @@ def stacks(layers):
 
 
 class PackCache:
-    """Holds the packed weights of a list of layers; re-packs on change."""
+    """Holds the packed weights of a list of layers; re-packs on change.
+
+    `layered=True` gives the layout of the layer-by-layer (large batch)
+    path; both layouts are cached independently.
+    """
 
     def __init__(self):
         self._key = None
         self.packed = None
         self.meta = None
+        self._lay = None
 
-    def get(self, layers):
+    def get(self, layers, layered=False):
         U, W, Wf, bf, dtp, mix = layer_tensors(layers)
         flat = U + W + Wf + bf + dtp + [t for m in mix for t in m]
         key = _key(flat)
+        if layered:
+            if self._lay is None or self._lay[0] != key:
+                with torch.no_grad():
+                    s = stacks(layers)
+                    mixt = (s["Wx"], s["bx"], s["gx"], s["Wv"], s["bv"], s["gv"])
+                    packed, meta = ops.leapfrog_layered_pack(s["U"], s["W"], s["Wf"], s["bf"],
+                                                             s["dtp"], mixt)
+                self._lay = (key, packed, meta)
+            return self._lay[1], self._lay[2]
         if key != self._key:
             with torch.no_grad():
                 s = stacks(layers)
