@@ -217,6 +217,15 @@ int gfn_leapfrog_layered_pack(const float* U_stack, const float* W_stack,
                               const float* norm_v_w, int dim, int heads, int rank, int num_layers,
                               float* packed, long long packed_floats, gfn_stream_t stream);
 long long gfn_leapfrog_layered_workspace_floats(int batch, int dim);
+/* Arithmetic of the layered path's mixing GEMM (process-wide; returns the
+ * previous mode, or a negative status for an unknown mode):
+ *   GFN_MIX_SPLIT_BF16 (default) each fp32 operand split into three bf16
+ *     pieces, the six cross products of order <= 2^-16 summed by one bf16
+ *     tensor-core GEMM with fp32 accumulation (K = 6 * dim): fp32-level
+ *     accuracy at tensor-core rate.
+ *   GFN_MIX_FP32_SIMT  plain fp32 SGEMM on the CUDA cores. */
+enum { GFN_MIX_SPLIT_BF16 = 0, GFN_MIX_FP32_SIMT = 1 };
+int gfn_leapfrog_layered_set_mixing(int mode);
 int gfn_leapfrog_layered_forward(const float* x_init, const float* v_init,
                                  long long state_row_stride, const float* forces_f32,
                                  const void* forces_bf16, const long long* token_ids,

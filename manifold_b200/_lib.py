@@ -46,6 +46,7 @@ _SIGS = {
     "gfn_leapfrog_layered_pack": [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i, _i, _i, _i, _p, _ll,
                                   _p],
     "gfn_leapfrog_layered_workspace_floats": [_i, _i],
+    "gfn_leapfrog_layered_set_mixing": [_i],
     "gfn_leapfrog_layered_forward": [_p, _p, _ll, _p, _p, _p, _p, _ll, _p, _p, _ll, _i, _i, _i, _i,
                                      _i, _i, _f, _p, _p, _p, _p, _p, _ll, _p],
     "gfn_parallel_scan": [_p, _p, _p, _p, _ll, _i, _i, _i, _p],

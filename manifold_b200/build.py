@@ -8,7 +8,7 @@ CSRC = os.path.join(HERE, "csrc")
 
 def build(verbose=False):
     """Run the csrc Makefile (incremental).  Raises on a compiler error."""
-    res = subprocess.run(["make", "-C", CSRC], capture_output=True, text=True)
+    res = subprocess.run(["make", "-j4", "-C", CSRC], capture_output=True, text=True)
     if verbose or res.returncode != 0:
         print(res.stdout)
         print(res.stderr)

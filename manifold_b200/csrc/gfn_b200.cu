@@ -3,6 +3,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <atomic>
 #include <mutex>
 
 #include "../../include/gfn_b200.h"
@@ -12,11 +13,12 @@
 #include "ops_small.cuh"
 #include "pack.cuh"
 #include "scan.cuh"
+#include "abi.h"
 
 using namespace gfn;
+using namespace gfn_abi;
 
-namespace {
-
+namespace gfn_abi {
 thread_local char g_msg[512] = "";
 long long* g_phase_prof = nullptr;  // gfn_debug_set_phase_profile
 
@@ -36,6 +38,9 @@ int cuda_status(cudaError_t e, const char* what) {
 int launch_status(const char* what) { return cuda_status(cudaGetLastError(), what); }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+}  // namespace gfn_abi
+
+namespace {
 
 struct DevInfo {
   int sms = 0;
@@ -59,18 +64,10 @@ int dev_info(DevInfo* out) {
   return GFN_OK;
 }
 
-// ------------------------------------------------------------------ plans
-// The weight layout (K, KC) depends only on (d, H, r); the row blocking R
-// also on the batch and the device.
-struct Layout {
-  int d, H, hd, r, NL, K, C, hpc, KC, nchunk, HS, CF, mix;
-  long long LF;
-  // training layout: head section + untransposed Wf (HST floats), forward and
-  // transposed mixing chunks
-  int HST;
-  long long LFT;
-};
+}  // namespace
 
+// ------------------------------------------------------------------ plans
+namespace gfn_abi {
 int make_layout(int d, int H, int r, int NL, Layout* L) {
   if (d <= 0 || H <= 0 || r <= 0 || NL <= 0 || d % H != 0)
     return fail(GFN_ERR_INVALID, "bad shape dim=%d heads=%d rank=%d layers=%d", d, H, r, NL);
@@ -108,6 +105,10 @@ int make_layout(int d, int H, int r, int NL, Layout* L) {
   L->LFT = (long long)L->HST + 2LL * L->nchunk * L->CF;
   return GFN_OK;
 }
+
+}  // namespace gfn_abi
+
+namespace {
 
 struct SeqPlan {
   Layout L;
@@ -849,157 +850,3 @@ int gfn_leapfrog_sequence_backward(const float* traj, const float* forces_f32,
 
 }  // extern "C"
 
-// ---------------------------------------------------------------------------
-// Layered path (large batches): fused pre kernel + batched cuBLAS SGEMM per layer
-#include <cublas_v2.h>
-#include "layered.cuh"
-
-namespace {
-
-std::mutex g_cublas_mu;
-cublasHandle_t g_cublas[64] = {};
-
-int cublas_for_device(cublasHandle_t* out) {
-  int dev;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return cuda_status(e, "cudaGetDevice");
-  if (dev < 0 || dev >= 64) return fail(GFN_ERR_UNSUPPORTED, "device %d", dev);
-  std::lock_guard<std::mutex> lock(g_cublas_mu);
-  if (!g_cublas[dev]) {
-    if (cublasCreate(&g_cublas[dev]) != CUBLAS_STATUS_SUCCESS)
-      return fail(GFN_ERR_CUDA, "cublasCreate failed");
-    // full fp32 products: no TF32
-    cublasSetMathMode(g_cublas[dev], CUBLAS_DEFAULT_MATH);
-  }
-  *out = g_cublas[dev];
-  return GFN_OK;
-}
-
-using LayPreKernel = void (*)(LayPreArgs);
-LayPreKernel lay_pre_for(int r, int epl) {
-#define GFN_L(RK, E) if (r == RK && epl == E) return layered_pre_kernel<RK, E>;
-  GFN_L(4, 1) GFN_L(4, 2) GFN_L(4, 4) GFN_L(8, 1) GFN_L(8, 2) GFN_L(8, 4)
-  GFN_L(16, 1) GFN_L(16, 2) GFN_L(16, 4)
-#undef GFN_L
-  return nullptr;
-}
-
-}  // namespace
-
-extern "C" {
-
-long long gfn_leapfrog_layered_pack_floats(int dim, int heads, int rank, int num_layers) {
-  Layout L;
-  if (make_layout(dim, heads, rank, num_layers, &L) != GFN_OK || heads < 2) return -1;
-  return (long long)num_layers * lay_offsets(heads, L.hd, rank, dim).total;
-}
-
-int gfn_leapfrog_layered_pack(const float* U_stack, const float* W_stack,
-                              const float* W_forget_stack, const float* b_forget_stack,
-                              const float* dt_params, const float* mix_x_w, const float* mix_x_b,
-                              const float* norm_x_w, const float* mix_v_w, const float* mix_v_b,
-                              const float* norm_v_w, int dim, int heads, int rank, int num_layers,
-                              float* packed, long long packed_floats, gfn_stream_t stream) {
-  Layout L;
-  int st = make_layout(dim, heads, rank, num_layers, &L);
-  if (st) return st;
-  if (heads < 2) return fail(GFN_ERR_UNSUPPORTED, "layered path needs heads > 1 (head mixing)");
-  if (!U_stack || !W_stack || !W_forget_stack || !b_forget_stack || !dt_params || !mix_x_w ||
-      !mix_x_b || !norm_x_w || !mix_v_w || !mix_v_b || !norm_v_w || !packed)
-    return fail(GFN_ERR_INVALID, "layered pack: NULL operand");
-  LayPackArgs a;
-  a.U = U_stack; a.W = W_stack; a.Wf = W_forget_stack; a.bf = b_forget_stack; a.dtp = dt_params;
-  a.Wx = mix_x_w; a.bx = mix_x_b; a.gx = norm_x_w; a.Wv = mix_v_w; a.bv = mix_v_b; a.gv = norm_v_w;
-  a.out = packed; a.NL = num_layers; a.d = dim; a.H = heads; a.hd = L.hd; a.r = rank;
-  a.LF = lay_offsets(heads, L.hd, rank, dim).total;
-  if (packed_floats < a.LF * num_layers) return fail(GFN_ERR_INVALID, "layered pack: buffer too small");
-  if (!aligned16(packed)) return fail(GFN_ERR_ALIGN, "layered pack: output not 16-byte aligned");
-  layered_pack_kernel<<<148 * 8, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(a);
-  return launch_status("layered_pack_kernel");
-}
-
-long long gfn_leapfrog_layered_workspace_floats(int batch, int dim) {
-  return 6LL * batch * dim + 2LL * batch + 4;
-}
-
-int gfn_leapfrog_layered_forward(const float* x_init, const float* v_init,
-                                 long long state_row_stride, const float* forces_f32,
-                                 const void* forces_bf16, const long long* token_ids,
-                                 const float* embed_table, long long vocab, const float* mask,
-                                 const float* packed, long long packed_floats, int batch,
-                                 int seq_len, int dim, int heads, int rank, int num_layers,
-                                 float base_dt, float* x_seq, float* v_seq, float* x_final,
-                                 float* v_final, float* workspace, long long workspace_floats,
-                                 gfn_stream_t stream) {
-  Layout L;
-  int st = make_layout(dim, heads, rank, num_layers, &L);
-  if (st) return st;
-  if (heads < 2) return fail(GFN_ERR_UNSUPPORTED, "layered path needs heads > 1 (head mixing)");
-  if (batch < 0 || seq_len < 0) return fail(GFN_ERR_INVALID, "layered: bad sizes");
-  if (!x_init || !v_init || !packed || !workspace) return fail(GFN_ERR_INVALID, "layered: NULL operand");
-  const int nsrc = (forces_f32 != nullptr) + (forces_bf16 != nullptr) + (token_ids != nullptr);
-  if (seq_len > 0 && nsrc != 1) return fail(GFN_ERR_INVALID, "layered: give exactly one force source");
-  if (token_ids && (!embed_table || vocab <= 0)) return fail(GFN_ERR_INVALID, "layered: ids need a table");
-  const LayOffsets lo = lay_offsets(heads, L.hd, rank, dim);
-  if (packed_floats < lo.total * num_layers) return fail(GFN_ERR_INVALID, "layered: packed too small");
-  if (workspace_floats < gfn_leapfrog_layered_workspace_floats(batch, dim))
-    return fail(GFN_ERR_INVALID, "layered: workspace too small");
-  if (batch == 0 || seq_len == 0) return GFN_OK;
-  const int epl = L.hd <= 32 ? 1 : L.hd <= 64 ? 2 : 4;
-  LayPreKernel pre = lay_pre_for(rank, epl);
-  if (!pre) return fail(GFN_ERR_UNSUPPORTED, "layered: rank %d", rank);
-  cublasHandle_t hb;
-  st = cublas_for_device(&hb);
-  if (st) return st;
-  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  if (cublasSetStream(hb, s) != CUBLAS_STATUS_SUCCESS) return fail(GFN_ERR_CUDA, "cublasSetStream");
-  const long long BD = (long long)batch * dim;
-  float* cat = workspace;
-  float* z = workspace + 2 * BD;
-  float* xs = workspace + 4 * BD;
-  float* vs = workspace + 5 * BD;
-  float* stat = workspace + 6 * BD;
-  const size_t pre_smem = (size_t)lo.hblock * 4;
-  cudaFuncSetAttribute(pre, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pre_smem);
-  const dim3 pre_grid((batch + LAY_ROWS - 1) / LAY_ROWS, heads);
-  const unsigned stat_blocks = (unsigned)((2LL * batch * 32 + 255) / 256);
-  const float one = 1.f, zero = 0.f;
-  for (int t = 0; t < seq_len; ++t) {
-    for (int l = 0; l < num_layers; ++l) {
-      const float* lay = packed + (long long)l * lo.total;
-      LayPreArgs a = {};
-      if (l == 0) {
-        a.x_in = t == 0 ? x_init : xs;
-        a.v_in = t == 0 ? v_init : vs;
-        a.in_stride = t == 0 ? state_row_stride : dim;
-      } else {
-        const float* prev = packed + (long long)(l - 1) * lo.total;
-        layered_rowstat_kernel<<<stat_blocks, 256, 0, s>>>(z, prev + lo.bx, prev + lo.bv, stat, batch, dim);
-        a.z = z;
-        a.stat = stat;
-        a.prev = prev;
-      }
-      a.f32 = forces_f32; a.fbf16 = reinterpret_cast<const __nv_bfloat16*>(forces_bf16);
-      a.ids = token_ids; a.table = embed_table; a.vocab = vocab; a.mask = mask;
-      a.t = t; a.L = seq_len; a.lay = lay; a.cat = cat; a.B = batch; a.d = dim; a.H = heads;
-      a.hd = L.hd; a.base_dt = base_dt;
-      pre<<<pre_grid, LAY_THREADS, pre_smem, s>>>(a);
-      // z[i] = cat[i] . W_i^T for i in {x, v}: column-major view z^T = W cat^T
-      if (cublasSgemmStridedBatched(hb, CUBLAS_OP_T, CUBLAS_OP_N, dim, batch, dim, &one,
-                                    lay + lo.Wx, dim, (long long)dim * dim, cat, dim, BD, &zero, z,
-                                    dim, BD, 2) != CUBLAS_STATUS_SUCCESS)
-        return fail(GFN_ERR_CUDA, "cublasSgemmStridedBatched failed");
-    }
-    const float* last = packed + (long long)(num_layers - 1) * lo.total;
-    layered_rowstat_kernel<<<stat_blocks, 256, 0, s>>>(z, last + lo.bx, last + lo.bv, stat, batch, dim);
-    layered_finalize_kernel<<<148 * 8, 256, 0, s>>>(z, stat, last, heads, L.hd, rank, batch, dim,
-                                                    seq_len, t, x_seq, v_seq, xs, vs);
-  }
-  cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return cuda_status(e, "layered kernels");
-  if (x_final) e = cudaMemcpyAsync(x_final, xs, BD * 4, cudaMemcpyDeviceToDevice, s);
-  if (e == cudaSuccess && v_final) e = cudaMemcpyAsync(v_final, vs, BD * 4, cudaMemcpyDeviceToDevice, s);
-  return cuda_status(e, "layered final state copy");
-}
-
-}  // extern "C"

@@ -22,10 +22,17 @@ constexpr int LAY_ROWS = 32;  // rows per pre-kernel block
 // Per-layer layered pack offsets (floats).  Per head: WfT [hd][hd], U, W
 // [hd][r], bf [hd] (each head block padded to 4); then softplus(dt) [H] (pad
 // 4), bx, bv, gx, gv [d], then Wx, Wv [d][d] ([out][in], contiguous pair).
+// Then the split-bf16 copy of the mixing weights WK [2][d][6d] (bf16): each
+// fp32 weight w = w0 + w1 + w2 (three bf16 pieces, round to nearest), laid
+// along K as [w0 w1 w0 w2 w1 w0] against the activations' [c0 c0 c1 c0 c1 c2],
+// so one bf16 GEMM with K = 6d and fp32 accumulation sums the six products
+// c_i w_j with i + j <= 2.  The dropped terms are below 2^-26 of |c w|.
 struct LayOffsets {
-  int head, hblock, sc, bx, bv, gx, gv, Wx, Wv;
+  int head, hblock, sc, bx, bv, gx, gv;
+  long long Wx, Wv, WK;
   long long total;
 };
+constexpr int LAY_SPLIT = 6;
 
 __host__ __device__ inline LayOffsets lay_offsets(int H, int hd, int r, int d) {
   LayOffsets o;
@@ -37,8 +44,9 @@ __host__ __device__ inline LayOffsets lay_offsets(int H, int hd, int r, int d) {
   o.gx = o.bv + d;
   o.gv = o.gx + d;
   o.Wx = o.gv + d;
-  o.Wv = o.Wx + d * d;
-  o.total = (long long)o.Wv + (long long)d * d;
+  o.Wv = o.Wx + (long long)d * d;
+  o.WK = o.Wv + (long long)d * d;
+  o.total = o.WK + (long long)LAY_SPLIT * d * d;  // 2 * d * 6d bf16
   return o;
 }
 
@@ -80,8 +88,30 @@ __global__ void layered_pack_kernel(const LayPackArgs a) {
       v = src[(long long)l * d + j];
     } else if (off < o.Wv) {
       v = a.Wx[(long long)l * d * d + (off - o.Wx)];
-    } else {
+    } else if (off < o.WK) {
       v = a.Wv[(long long)l * d * d + (off - o.Wv)];
+    } else {
+      // two bf16 of WK per float slot
+      const long long q = 2 * (off - o.WK);
+      __nv_bfloat16 pr[2];
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const long long qq = q + u;
+        const long long rowk = (long long)LAY_SPLIT * d;
+        const int which = (int)(qq / ((long long)d * rowk));
+        const long long rem = qq - (long long)which * d * rowk;
+        const int orow = (int)(rem / rowk), kk = (int)(rem - (long long)orow * rowk);
+        const int seg = kk / d, col = kk - seg * d;
+        const float w = (which == 0 ? a.Wx : a.Wv)[((long long)l * d + orow) * d + col];
+        const __nv_bfloat16 w0 = __float2bfloat16_rn(w);
+        const float r1 = w - __bfloat162float(w0);
+        const __nv_bfloat16 w1 = __float2bfloat16_rn(r1);
+        const __nv_bfloat16 w2 = __float2bfloat16_rn(r1 - __bfloat162float(w1));
+        // [w0 w1 w0 w2 w1 w0]
+        pr[u] = seg == 1 || seg == 4 ? w1 : seg == 3 ? w2 : w0;
+      }
+      v = __uint_as_float((unsigned)__bfloat16_as_ushort(pr[0]) |
+                          ((unsigned)__bfloat16_as_ushort(pr[1]) << 16));
     }
     a.out[e] = v;
   }
@@ -123,13 +153,14 @@ struct LayPreArgs {
   const float* mask;
   int t, L;
   const float* lay;     // this layer's pack run
-  float* cat;           // [2][B][d] head-step outputs (x', v')
+  float* cat;           // [2][B][d] head-step outputs (x', v'), or NULL
+  __nv_bfloat16* catk;  // [2][B][6d] split-bf16 head-step outputs, or NULL
   int B, d, H, hd;
   float base_dt;
 };
 
 template <int RK, int EPL>
-__global__ void __launch_bounds__(LAY_THREADS) layered_pre_kernel(const LayPreArgs a) {
+__global__ void __launch_bounds__(LAY_THREADS, EPL >= 4 ? 2 : 4) layered_pre_kernel(const LayPreArgs a) {
   extern __shared__ __align__(16) float hsm[];  // this head's WfT | U | W | bf
   const int hd = a.hd, d = a.d, B = a.B;
   const int h = blockIdx.y;
@@ -201,8 +232,24 @@ __global__ void __launch_bounds__(LAY_THREADS) layered_pre_kernel(const LayPreAr
       v[e] = (v[e] + hh * (F[e] - gm[e])) / (1.f + hh * mu[e]);
       if (eok[e]) {
         const int col = h * hd + jj[e];
-        a.cat[(long long)b * d + col] = x[e];
-        a.cat[((long long)B + b) * d + col] = v[e];
+        if (a.cat) {
+          a.cat[(long long)b * d + col] = x[e];
+          a.cat[((long long)B + b) * d + col] = v[e];
+        }
+        if (a.catk) {
+#pragma unroll
+          for (int w = 0; w < 2; ++w) {
+            const float c = w == 0 ? x[e] : v[e];
+            const __nv_bfloat16 c0 = __float2bfloat16_rn(c);
+            const float r1 = c - __bfloat162float(c0);
+            const __nv_bfloat16 c1 = __float2bfloat16_rn(r1);
+            const __nv_bfloat16 c2 = __float2bfloat16_rn(r1 - __bfloat162float(c1));
+            __nv_bfloat16* row = a.catk + ((long long)w * B + b) * (LAY_SPLIT * d) + col;
+            // [c0 c0 c1 c0 c1 c2]
+            row[0] = c0; row[d] = c0; row[2 * d] = c1;
+            row[3 * d] = c0; row[4 * d] = c1; row[5 * d] = c2;
+          }
+        }
       }
     }
   }

@@ -281,9 +281,19 @@ def test_errors_are_loud():
     assert ops.device_error(reset=True) == 0
 
 
+@pytest.fixture(params=["split_bf16", "fp32_simt"])
+def mixing(request):
+    from manifold_b200.cuda import ops
+    mode = ops.MIX_SPLIT_BF16 if request.param == "split_bf16" else ops.MIX_FP32_SIMT
+    prev = ops.set_layered_mixing(mode)
+    yield request.param
+    ops.set_layered_mixing(prev)
+
+
 @pytest.mark.parametrize("name", ["tiny", "mask", "c1", "c2s", "c3s", "c4s", "c5s"])
-def test_layered_sequence_matches_reference(name):
-    """The layer-by-layer (large batch) path against the same goldens."""
+def test_layered_sequence_matches_reference(name, mixing):
+    """The layer-by-layer (large batch) path against the same goldens, with
+    either mixing-GEMM arithmetic."""
     cfg = C.CASES[name]
     if cfg["H"] == 1:
         pytest.skip("layered path needs head mixing")
@@ -299,7 +309,7 @@ def test_layered_sequence_matches_reference(name):
     rowwise_close(v.cpu().numpy(), g["v_final"], SEQ_RTOL, SEQ_ATOL, "v_final")
 
 
-def test_layered_matches_fused_c4_shape():
+def test_layered_matches_fused_c4_shape(mixing):
     """C4 layer shape (d=1024, 16 heads, rank 64) at a batch of 512 with a
     carried state: layered and fused paths agree, and both continue a
     split sequence exactly like the unsplit one."""
@@ -318,4 +328,5 @@ def test_layered_matches_fused_c4_shape():
     rowwise_close(xl_seq.cpu().numpy(), xf_seq.cpu().numpy(), SEQ_RTOL, SEQ_ATOL, "x_seq")
     rowwise_close(vl_seq.cpu().numpy(), vf_seq.cpu().numpy(), SEQ_RTOL, SEQ_ATOL, "v_seq")
     torch.testing.assert_close(xs2, xl_seq[:, 2:], rtol=0, atol=0)
+    torch.testing.assert_close(x2, xl, rtol=0, atol=0)
     torch.testing.assert_close(v2, vl, rtol=0, atol=0)
