@@ -35,12 +35,23 @@ int cublas_for_device(cublasHandle_t* out) {
 }
 
 using LayPreKernel = void (*)(LayPreArgs);
-LayPreKernel lay_pre_for(int r, int epl) {
-#define GFN_L(RK, E) if (r == RK && epl == E) return layered_pre_kernel<RK, E>;
-  GFN_L(4, 1) GFN_L(4, 2) GFN_L(4, 4) GFN_L(8, 1) GFN_L(8, 2) GFN_L(8, 4)
-  GFN_L(16, 1) GFN_L(16, 2) GFN_L(16, 4)
+struct LayPreInst {
+  LayPreKernel fn;
+  int tr;
+  size_t smem;
+};
+
+bool lay_pre_for(int r, int hd, int hblock, LayPreInst* out) {
+#define GFN_L(RK, HD)                                                              \
+  if (r == RK && hd == HD) {                                                       \
+    *out = {layered_pre_kernel<RK, HD>, LayTile<HD>::TR, layered_pre_smem<RK, HD>(hblock)}; \
+    return true;                                                                   \
+  }
+  GFN_L(4, 16) GFN_L(4, 32) GFN_L(4, 64) GFN_L(4, 128)
+  GFN_L(8, 16) GFN_L(8, 32) GFN_L(8, 64) GFN_L(8, 128)
+  GFN_L(16, 16) GFN_L(16, 32) GFN_L(16, 64) GFN_L(16, 128)
 #undef GFN_L
-  return nullptr;
+  return false;
 }
 
 }  // namespace
@@ -102,6 +113,11 @@ int gfn_leapfrog_layered_forward(const float* x_init, const float* v_init,
   if (heads < 2) return fail(GFN_ERR_UNSUPPORTED, "layered path needs heads > 1 (head mixing)");
   if (batch < 0 || seq_len < 0) return fail(GFN_ERR_INVALID, "layered: bad sizes");
   if (!x_init || !v_init || !packed || !workspace) return fail(GFN_ERR_INVALID, "layered: NULL operand");
+  if (!aligned16(x_init) || !aligned16(v_init) || !aligned16(packed) || !aligned16(workspace) ||
+      (forces_f32 && !aligned16(forces_f32)) || (embed_table && !aligned16(embed_table)) ||
+      (forces_bf16 && (reinterpret_cast<uintptr_t>(forces_bf16) & 7u)) || state_row_stride % 4)
+    return fail(GFN_ERR_ALIGN, "layered: operands must be 16-byte aligned (bf16 forces 8-byte), "
+                "state row stride a multiple of 4");
   const int nsrc = (forces_f32 != nullptr) + (forces_bf16 != nullptr) + (token_ids != nullptr);
   if (seq_len > 0 && nsrc != 1) return fail(GFN_ERR_INVALID, "layered: give exactly one force source");
   if (token_ids && (!embed_table || vocab <= 0)) return fail(GFN_ERR_INVALID, "layered: ids need a table");
@@ -110,9 +126,10 @@ int gfn_leapfrog_layered_forward(const float* x_init, const float* v_init,
   if (workspace_floats < gfn_leapfrog_layered_workspace_floats(batch, dim))
     return fail(GFN_ERR_INVALID, "layered: workspace too small");
   if (batch == 0 || seq_len == 0) return GFN_OK;
-  const int epl = L.hd <= 32 ? 1 : L.hd <= 64 ? 2 : 4;
-  LayPreKernel pre = lay_pre_for(rank, epl);
-  if (!pre) return fail(GFN_ERR_UNSUPPORTED, "layered: rank %d", rank);
+  LayPreInst inst;
+  if (!lay_pre_for(rank, L.hd, lo.hblock, &inst))
+    return fail(GFN_ERR_UNSUPPORTED, "layered: head_dim %d must be 16, 32, 64 or 128", L.hd);
+  LayPreKernel pre = inst.fn;
   cublasHandle_t hb;
   st = cublas_for_device(&hb);
   if (st) return st;
@@ -126,9 +143,10 @@ int gfn_leapfrog_layered_forward(const float* x_init, const float* v_init,
   float* xs = workspace + 10 * BD;
   float* vs = workspace + 11 * BD;
   float* stat = workspace + 12 * BD;
-  const size_t pre_smem = (size_t)lo.hblock * 4;
-  cudaFuncSetAttribute(pre, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pre_smem);
-  const dim3 pre_grid((batch + LAY_ROWS - 1) / LAY_ROWS, heads);
+  const size_t pre_smem = inst.smem;
+  cudaError_t ae = cudaFuncSetAttribute(pre, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pre_smem);
+  if (ae != cudaSuccess) return cuda_status(ae, "layered: shared memory attribute");
+  const dim3 pre_grid((batch + inst.tr - 1) / inst.tr, heads);
   const unsigned stat_blocks = (unsigned)((2LL * batch * 32 + 255) / 256);
   const float one = 1.f, zero = 0.f;
   for (int t = 0; t < seq_len; ++t) {

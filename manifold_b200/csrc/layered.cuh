@@ -17,7 +17,6 @@
 namespace gfn {
 
 constexpr int LAY_THREADS = 256;
-constexpr int LAY_ROWS = 32;  // rows per pre-kernel block
 
 // Per-layer layered pack offsets (floats).  Per head: WfT [hd][hd], U, W
 // [hd][r], bf [hd] (each head block padded to 4); then softplus(dt) [H] (pad
@@ -159,100 +158,254 @@ struct LayPreArgs {
   float base_dt;
 };
 
-template <int RK, int EPL>
-__global__ void __launch_bounds__(LAY_THREADS, EPL >= 4 ? 2 : 4) layered_pre_kernel(const LayPreArgs a) {
-  extern __shared__ __align__(16) float hsm[];  // this head's WfT | U | W | bf
-  const int hd = a.hd, d = a.d, B = a.B;
-  const int h = blockIdx.y;
-  const LayOffsets o = lay_offsets(a.H, hd, RK, d);
-  const float* src = a.lay + h * o.hblock;
-  for (int i = threadIdx.x; i < o.hblock; i += blockDim.x) hsm[i] = src[i];
-  __syncthreads();
+// Tile of the head-step kernel: TR rows of one head; thread (ty, tx) owns
+// rows ty*RPT .. +RPT-1 and columns 4tx .. 4tx+3 of the head.
+template <int HD>
+struct LayTile {
+  static constexpr int TR = HD <= 64 ? 64 : 32;
+  static constexpr int CG = HD / 4;             // column groups of 4
+  static constexpr int RG = LAY_THREADS / CG;   // row groups
+  static constexpr int RPT = TR / RG;           // rows per thread
+  static constexpr int TRP = TR + 4;            // padded row count of the transposed tiles
+  static_assert(RPT >= 1 && RG * RPT == TR, "tile shape");
+};
+
+template <int N>
+GFN_DEV void lds_rows(const float* p, float (&r)[N]) {
+  if constexpr (N == 4) {
+    const float4 t = *reinterpret_cast<const float4*>(p);
+    r[0] = t.x; r[1] = t.y; r[2] = t.z; r[3] = t.w;
+  } else if constexpr (N == 2) {
+    const float2 t = *reinterpret_cast<const float2*>(p);
+    r[0] = t.x; r[1] = t.y;
+  } else {
+#pragma unroll
+    for (int i = 0; i < N; ++i) r[i] = p[i];
+  }
+}
+
+GFN_DEV float4 ldg4(const float* p) { return __ldg(reinterpret_cast<const float4*>(p)); }
+
+// p = v . U for every (row, q) of the tile, then ps = p^2 / (1 + |p| + 1e-6)
+// (gfn/geometry/lowrank.py:93-98 without the W contraction).
+template <int RK, int HD>
+GFN_DEV void tile_gamma_p(const float* vT, const float* U, float* ps) {
+  using T = LayTile<HD>;
+  for (int o = threadIdx.x; o < T::TR * RK; o += LAY_THREADS) {
+    const int r = o / RK, q = o - (o / RK) * RK;
+    float p = 0.f;
+#pragma unroll 16
+    for (int j = 0; j < HD; ++j) p = fmaf(vT[j * T::TRP + r], U[j * RK + q], p);
+    float ss = p * p;
+#pragma unroll
+    for (int m = 1; m < RK; m <<= 1) ss += __shfl_xor_sync(0xffffffffu, ss, m);
+    const float sc = 1.f / ((1.f + sqrtf(ss)) + 1e-6f);
+    ps[o] = (p * p) * sc;
+  }
+}
+
+// One implicit kick for the thread's micro-tile: friction mu = 5 sigma(x Wf^T
+// + b_f) from the transposed x tile (a TR x HD x HD product in registers),
+// Gamma from ps, then v_new = (v + h (F - Gamma)) / (1 + h mu)
+// (gfn/integrators/symplectic/leapfrog.py:72-114).
+template <int RK, int HD>
+GFN_DEV void tile_kick(const float* xT, const float* vT, const float* ps, const float* WfT,
+                       const float* Wg, const float* bfh, int r0, int c0, float hh,
+                       const float (&F)[LayTile<HD>::RPT][4], float (&vn)[LayTile<HD>::RPT][4]) {
+  using T = LayTile<HD>;
+  constexpr int RPT = T::RPT;
+  float acc[RPT][4];
+#pragma unroll
+  for (int i = 0; i < RPT; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
+#pragma unroll 8
+  for (int k = 0; k < HD; ++k) {
+    const float4 w = *reinterpret_cast<const float4*>(WfT + k * HD + c0);
+    float xr[RPT];
+    lds_rows<RPT>(xT + k * T::TRP + r0, xr);
+#pragma unroll
+    for (int i = 0; i < RPT; ++i) {
+      acc[i][0] = fmaf(xr[i], w.x, acc[i][0]);
+      acc[i][1] = fmaf(xr[i], w.y, acc[i][1]);
+      acc[i][2] = fmaf(xr[i], w.z, acc[i][2]);
+      acc[i][3] = fmaf(xr[i], w.w, acc[i][3]);
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int c = c0 + j;
+    float vr[RPT];
+    lds_rows<RPT>(vT + c * T::TRP + r0, vr);
+    const float bj = bfh[c];
+#pragma unroll
+    for (int i = 0; i < RPT; ++i) {
+      const float mu = sigmoid_f(acc[i][j] + bj) * 5.f;
+      float gsum = 0.f;
+#pragma unroll
+      for (int q = 0; q < RK; ++q) gsum = fmaf(ps[(r0 + i) * RK + q], Wg[c * RK + q], gsum);
+      const float g = soft_clamp20(gsum);
+      vn[i][j] = (vr[i] + hh * (F[i][j] - g)) / (1.f + hh * mu);
+    }
+  }
+}
+
+GFN_DEV void store_split6(__nv_bfloat16* row, int d, const float (&c)[4]) {
+  // [c0 c0 c1 c0 c1 c2] per column, 4 columns per 8-byte store
+  __nv_bfloat16 p0[4], p1[4], p2[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    p0[j] = __float2bfloat16_rn(c[j]);
+    const float r1 = c[j] - __bfloat162float(p0[j]);
+    p1[j] = __float2bfloat16_rn(r1);
+    p2[j] = __float2bfloat16_rn(r1 - __bfloat162float(p1[j]));
+  }
+  auto pack4 = [](const __nv_bfloat16 (&q)[4]) {
+    uint2 u;
+    u.x = (unsigned)__bfloat16_as_ushort(q[0]) | ((unsigned)__bfloat16_as_ushort(q[1]) << 16);
+    u.y = (unsigned)__bfloat16_as_ushort(q[2]) | ((unsigned)__bfloat16_as_ushort(q[3]) << 16);
+    return u;
+  };
+  const uint2 u0 = pack4(p0), u1 = pack4(p1), u2 = pack4(p2);
+  *reinterpret_cast<uint2*>(row) = u0;
+  *reinterpret_cast<uint2*>(row + d) = u0;
+  *reinterpret_cast<uint2*>(row + 2 * d) = u1;
+  *reinterpret_cast<uint2*>(row + 3 * d) = u0;
+  *reinterpret_cast<uint2*>(row + 4 * d) = u1;
+  *reinterpret_cast<uint2*>(row + 5 * d) = u2;
+}
+
+// Head step of one layer for TR rows of one head (grid: row tiles x heads).
+// Input: the carried state (first layer of a token) or the previous layer's
+// mixing output with its RMSNorm / saturation applied on load.  Output: the
+// concat (x', v') as fp32 (cat) or split bf16 (catk).
+template <int RK, int HD>
+__global__ void __launch_bounds__(LAY_THREADS, 2) layered_pre_kernel(const LayPreArgs a) {
+  using T = LayTile<HD>;
+  constexpr int RPT = T::RPT;
+  extern __shared__ __align__(16) float hsm[];
+  const int d = a.d, B = a.B, h = blockIdx.y;
+  const LayOffsets o = lay_offsets(a.H, HD, RK, d);
+  {
+    const float* src = a.lay + (long long)h * o.hblock;
+    for (int i = threadIdx.x * 4; i < o.hblock; i += LAY_THREADS * 4)
+      *reinterpret_cast<float4*>(hsm + i) = ldg4(src + i);
+  }
   const float* WfT = hsm;
-  const float* U = hsm + hd * hd;
-  const float* Wg = U + hd * RK;
-  const float* bfh = Wg + hd * RK;
+  const float* U = hsm + HD * HD;
+  const float* Wg = U + HD * RK;
+  const float* bfh = Wg + HD * RK;
+  float* xT = hsm + o.hblock;
+  float* vT = xT + HD * T::TRP;
+  float* ps = vT + HD * T::TRP;
+  const int tx = threadIdx.x % T::CG, ty = threadIdx.x / T::CG;
+  const int c0 = 4 * tx, r0 = ty * RPT;
+  const int gc = h * HD + c0;
+  const int row0 = blockIdx.x * T::TR;
   const float eff = a.base_dt * a.lay[o.sc + h];
   const float hh = 0.5f * eff;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  int jj[EPL];
-  bool eok[EPL];
+
+  float F[RPT][4];
 #pragma unroll
-  for (int e = 0; e < EPL; ++e) {
-    jj[e] = lane + 32 * e;
-    eok[e] = jj[e] < hd;
-    if (!eok[e]) jj[e] = hd - 1;
-  }
-  const LayOffsets po = lay_offsets(a.H, hd, RK, d);
-  const int rend = min(B, (int)(blockIdx.x + 1) * LAY_ROWS);
-  for (int b = blockIdx.x * LAY_ROWS + warp; b < rend; b += LAY_THREADS / 32) {
-    float x[EPL], v[EPL], F[EPL];
-    const long long idx = (long long)b * a.L + a.t;
-    long long id = 0;
-    if (a.ids) {
-      id = a.ids[idx];
-      if (id < 0 || id >= a.vocab) {
-        if (lane == 0) gfn_flag_error(kDevErrBadToken);
-        id = -1;
-      }
-    }
-    const float m = a.mask ? a.mask[idx] : 1.f;
-#pragma unroll
-    for (int e = 0; e < EPL; ++e) {
-      const int col = h * hd + jj[e];
+  for (int i = 0; i < RPT; ++i) {
+    const int b = row0 + r0 + i;
+    float xv[4] = {0.f, 0.f, 0.f, 0.f}, vv[4] = {0.f, 0.f, 0.f, 0.f};
+    F[i][0] = F[i][1] = F[i][2] = F[i][3] = 0.f;
+    if (b < B) {
       if (a.z) {
         const float rx = a.stat[b], rv = a.stat[B + b];
-        const float zx = a.z[(long long)b * d + col] + a.prev[po.bx + col];
-        const float zv = a.z[((long long)B + b) * d + col] + a.prev[po.bv + col];
-        x[e] = (zx * rx) * a.prev[po.gx + col];
-        v[e] = saturate100((zv * rv) * a.prev[po.gv + col]);
+        const float4 zx = ldg4(a.z + (long long)b * d + gc);
+        const float4 zv = ldg4(a.z + ((long long)B + b) * d + gc);
+        const float4 bx = ldg4(a.prev + o.bx + gc), bv = ldg4(a.prev + o.bv + gc);
+        const float4 gx = ldg4(a.prev + o.gx + gc), gv = ldg4(a.prev + o.gv + gc);
+        xv[0] = ((zx.x + bx.x) * rx) * gx.x; xv[1] = ((zx.y + bx.y) * rx) * gx.y;
+        xv[2] = ((zx.z + bx.z) * rx) * gx.z; xv[3] = ((zx.w + bx.w) * rx) * gx.w;
+        vv[0] = saturate100(((zv.x + bv.x) * rv) * gv.x);
+        vv[1] = saturate100(((zv.y + bv.y) * rv) * gv.y);
+        vv[2] = saturate100(((zv.z + bv.z) * rv) * gv.z);
+        vv[3] = saturate100(((zv.w + bv.w) * rv) * gv.w);
       } else {
-        x[e] = a.x_in[(long long)b * a.in_stride + col];
-        v[e] = a.v_in[(long long)b * a.in_stride + col];
+        const float4 x4 = ldg4(a.x_in + (long long)b * a.in_stride + gc);
+        const float4 v4 = ldg4(a.v_in + (long long)b * a.in_stride + gc);
+        xv[0] = x4.x; xv[1] = x4.y; xv[2] = x4.z; xv[3] = x4.w;
+        vv[0] = v4.x; vv[1] = v4.y; vv[2] = v4.z; vv[3] = v4.w;
       }
-      float f;
-      if (a.f32) f = a.f32[idx * d + col];
-      else if (a.fbf16) f = __bfloat162float(a.fbf16[idx * d + col]);
-      else f = id < 0 ? 0.f : a.table[id * d + col];
-      F[e] = a.mask ? f * m : f;
-    }
-    float gm[EPL], mu[EPL];
-    unit_gamma<RK, EPL>(v, U, Wg, eok, jj, gm);
-    unit_friction<EPL>(x, WfT, bfh, hd, jj, mu);
-#pragma unroll
-    for (int e = 0; e < EPL; ++e) {
-      const float vh = (v[e] + hh * (F[e] - gm[e])) / (1.f + hh * mu[e]);
-      x[e] = x[e] + eff * vh;
-      v[e] = vh;
-    }
-    unit_gamma<RK, EPL>(v, U, Wg, eok, jj, gm);
-    unit_friction<EPL>(x, WfT, bfh, hd, jj, mu);
-#pragma unroll
-    for (int e = 0; e < EPL; ++e) {
-      v[e] = (v[e] + hh * (F[e] - gm[e])) / (1.f + hh * mu[e]);
-      if (eok[e]) {
-        const int col = h * hd + jj[e];
-        if (a.cat) {
-          a.cat[(long long)b * d + col] = x[e];
-          a.cat[((long long)B + b) * d + col] = v[e];
-        }
-        if (a.catk) {
-#pragma unroll
-          for (int w = 0; w < 2; ++w) {
-            const float c = w == 0 ? x[e] : v[e];
-            const __nv_bfloat16 c0 = __float2bfloat16_rn(c);
-            const float r1 = c - __bfloat162float(c0);
-            const __nv_bfloat16 c1 = __float2bfloat16_rn(r1);
-            const __nv_bfloat16 c2 = __float2bfloat16_rn(r1 - __bfloat162float(c1));
-            __nv_bfloat16* row = a.catk + ((long long)w * B + b) * (LAY_SPLIT * d) + col;
-            // [c0 c0 c1 c0 c1 c2]
-            row[0] = c0; row[d] = c0; row[2 * d] = c1;
-            row[3 * d] = c0; row[4 * d] = c1; row[5 * d] = c2;
-          }
+      const long long idx = (long long)b * a.L + a.t;
+      float4 f = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (a.f32) {
+        f = ldg4(a.f32 + idx * d + gc);
+      } else if (a.fbf16) {
+        const uint2 u = __ldg(reinterpret_cast<const uint2*>(a.fbf16 + idx * d + gc));
+        f.x = __uint_as_float(u.x << 16); f.y = __uint_as_float(u.x & 0xffff0000u);
+        f.z = __uint_as_float(u.y << 16); f.w = __uint_as_float(u.y & 0xffff0000u);
+      } else {
+        const long long id = a.ids[idx];
+        if (id < 0 || id >= a.vocab) {
+          if (tx == 0) gfn_flag_error(kDevErrBadToken);
+        } else {
+          f = ldg4(a.table + id * d + gc);
         }
       }
+      if (a.mask) {
+        const float m = a.mask[idx];
+        f.x *= m; f.y *= m; f.z *= m; f.w *= m;
+      }
+      F[i][0] = f.x; F[i][1] = f.y; F[i][2] = f.z; F[i][3] = f.w;
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      xT[(c0 + j) * T::TRP + r0 + i] = xv[j];
+      vT[(c0 + j) * T::TRP + r0 + i] = vv[j];
     }
   }
+  __syncthreads();
+  // kick 1 at x
+  tile_gamma_p<RK, HD>(vT, U, ps);
+  __syncthreads();
+  float vn[RPT][4];
+  tile_kick<RK, HD>(xT, vT, ps, WfT, Wg, bfh, r0, c0, hh, F, vn);
+  float xn[RPT][4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    float xr[RPT];
+    lds_rows<RPT>(xT + (c0 + j) * T::TRP + r0, xr);
+#pragma unroll
+    for (int i = 0; i < RPT; ++i) xn[i][j] = xr[i] + eff * vn[i][j];
+  }
+  __syncthreads();
+  // drift done: x' and v_half replace the tiles
+#pragma unroll
+  for (int i = 0; i < RPT; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      xT[(c0 + j) * T::TRP + r0 + i] = xn[i][j];
+      vT[(c0 + j) * T::TRP + r0 + i] = vn[i][j];
+    }
+  __syncthreads();
+  // kick 2 at x'
+  tile_gamma_p<RK, HD>(vT, U, ps);
+  __syncthreads();
+  tile_kick<RK, HD>(xT, vT, ps, WfT, Wg, bfh, r0, c0, hh, F, vn);
+#pragma unroll
+  for (int i = 0; i < RPT; ++i) {
+    const int b = row0 + r0 + i;
+    if (b >= B) continue;
+    if (a.cat) {
+      *reinterpret_cast<float4*>(a.cat + (long long)b * d + gc) =
+          make_float4(xn[i][0], xn[i][1], xn[i][2], xn[i][3]);
+      *reinterpret_cast<float4*>(a.cat + ((long long)B + b) * d + gc) =
+          make_float4(vn[i][0], vn[i][1], vn[i][2], vn[i][3]);
+    }
+    if (a.catk) {
+      store_split6(a.catk + (long long)b * (LAY_SPLIT * d) + gc, d, xn[i]);
+      store_split6(a.catk + ((long long)B + b) * (LAY_SPLIT * d) + gc, d, vn[i]);
+    }
+  }
+}
+
+template <int RK, int HD>
+constexpr size_t layered_pre_smem(int hblock) {
+  return ((size_t)hblock + 2 * HD * LayTile<HD>::TRP + LayTile<HD>::TR * RK) * 4;
 }
 
 // Last layer's RMSNorm + saturation -> x_seq[:, t], v_seq[:, t] and the state.

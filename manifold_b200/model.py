@@ -17,9 +17,11 @@ from .embeddings import FunctionalEmbedding, ImplicitEmbedding
 from .layers import MLayer, ParallelMLayer
 from .packing import PackCache
 
-# batch * dim from which recurrence() takes the layer-by-layer path (the
-# mixing becomes a GEMM with enough rows to fill the tensor-less fp32 pipes)
-LAYERED_MIN_ELEMS = 1 << 20
+# batch * dim from which recurrence() takes the layer-by-layer path: from
+# there the per-layer mixing is a GEMM with enough rows for the tensor cores
+# (measured on B200: C3 at 256 x 512 and C4 at 4096 x 1024 are faster layered;
+# C2 at 64 x 256 is faster fused)
+LAYERED_MIN_ELEMS = 1 << 17
 
 
 class ImplicitReadout(nn.Module):
@@ -143,7 +145,8 @@ class Manifold(nn.Module):
             return False
         if path == "layered":
             return True
-        return batch * self.dim >= LAYERED_MIN_ELEMS
+        hd = self.dim // self.heads
+        return hd in (16, 32, 64, 128) and batch * self.dim >= LAYERED_MIN_ELEMS
 
     def recurrence(self, input_ids=None, attention_mask=None, state=None, force_manual=None,
                    want_v_seq=True):

@@ -330,3 +330,27 @@ def test_layered_matches_fused_c4_shape(mixing):
     torch.testing.assert_close(xs2, xl_seq[:, 2:], rtol=0, atol=0)
     torch.testing.assert_close(x2, xl, rtol=0, atol=0)
     torch.testing.assert_close(v2, vl, rtol=0, atol=0)
+
+
+@pytest.mark.parametrize("d,H,rank,B", [(256, 4, 32, 100), (256, 4, 64, 70), (256, 2, 8, 33),
+                                        (512, 16, 64, 129), (128, 8, 128, 65)])
+def test_layered_matches_fused_shapes(d, H, rank, B, mixing):
+    """Head dims 16-128 and per-head ranks 4-16 on ragged row tiles, bf16
+    forces: the layered path agrees with the fused kernel."""
+    import manifold_b200 as gfn
+    torch.manual_seed(1)
+    m = gfn.Manifold(vocab_size=50, dim=d, depth=2, rank=rank, heads=H,
+                     integrator_type="leapfrog").cuda().eval()
+    with torch.no_grad():
+        for layer in m.layers:
+            for ch in layer.christoffels:
+                ch.U.normal_(0, 0.1)
+                ch.W.normal_(0, 0.1)
+    F = (torch.randn(B, 3, d, device="cuda") * 0.5).to(torch.bfloat16)
+    with torch.no_grad():
+        m.recurrence_path = "fused"
+        xf, vf, _, _ = m.recurrence(force_manual=F)
+        m.recurrence_path = "layered"
+        xl, vl, _, _ = m.recurrence(force_manual=F)
+    rowwise_close(xl.cpu().numpy(), xf.cpu().numpy(), SEQ_RTOL, SEQ_ATOL, "x_seq")
+    rowwise_close(vl.cpu().numpy(), vf.cpu().numpy(), SEQ_RTOL, SEQ_ATOL, "v_seq")
