@@ -18,8 +18,8 @@ namespace gfn {
 
 constexpr int LAY_THREADS = 256;
 
-// Per-layer layered pack offsets (floats).  Per head: WfT [hd][hd], U, W
-// [hd][r], bf [hd] (each head block padded to 4); then softplus(dt) [H] (pad
+// Per-layer layered pack offsets (floats).  Per head: WfT [hd][hd], U
+// [hd][r], W^T [r][hd], bf [hd] (each head block padded to 4); then softplus(dt) [H] (pad
 // 4), bx, bv, gx, gv [d], then Wx, Wv [d][d] ([out][in], contiguous pair).
 // Then the split-bf16 copy of the mixing weights WK [2][d][6d] (bf16): each
 // fp32 weight w = w0 + w1 + w2 (three bf16 pieces, round to nearest), laid
@@ -74,7 +74,8 @@ __global__ void layered_pack_kernel(const LayPackArgs a) {
       } else if (q < hd * hd + hd * r) {
         v = a.U[lh * hd * r + (q - hd * hd)];
       } else if (q < hd * hd + 2 * hd * r) {
-        v = a.W[lh * hd * r + (q - hd * hd - hd * r)];
+        const int t = q - hd * hd - hd * r, qq = t / hd, j = t - qq * hd;
+        v = a.W[lh * hd * r + j * r + qq];  // transposed: [q][j]
       } else if (q < hd * hd + 2 * hd * r + hd) {
         v = a.bf[lh * hd + (q - hd * hd - 2 * hd * r)];
       }
@@ -116,19 +117,24 @@ __global__ void layered_pack_kernel(const LayPackArgs a) {
   }
 }
 
-// Per-row RMSNorm factor 1/sqrt(mean((z + b)^2) + eps) of zx and zv.
+// Per-row RMSNorm factor 1/sqrt(mean((z + b)^2) + eps) of zx and zv (one
+// warp per row, 128-bit loads; d % 4 == 0).
 __global__ void layered_rowstat_kernel(const float* __restrict__ z, const float* __restrict__ bx,
                                        const float* __restrict__ bv, float* __restrict__ stat,
                                        int B, int d) {
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   if (warp >= 2 * B) return;
   const int which = warp / B, b = warp - which * B;
-  const float* row = z + ((long long)which * B + b) * d;
-  const float* bias = which == 0 ? bx : bv;
+  const float4* row = reinterpret_cast<const float4*>(z + ((long long)which * B + b) * d);
+  const float4* bias = reinterpret_cast<const float4*>(which == 0 ? bx : bv);
   float s = 0.f;
-  for (int j = lane; j < d; j += 32) {
-    const float u = row[j] + bias[j];
-    s = fmaf(u, u, s);
+  for (int j = lane; j < d / 4; j += 32) {
+    const float4 u = row[j], c = __ldg(bias + j);
+    const float a0 = u.x + c.x, a1 = u.y + c.y, a2 = u.z + c.z, a3 = u.w + c.w;
+    s = fmaf(a0, a0, s);
+    s = fmaf(a1, a1, s);
+    s = fmaf(a2, a2, s);
+    s = fmaf(a3, a3, s);
   }
   s = warp_sum(s);
   if (lane == 0) stat[which * B + b] = 1.f / sqrtf(s * (1.f / (float)d) + 1.1920928955078125e-07f);
@@ -166,9 +172,18 @@ struct LayTile {
   static constexpr int CG = HD / 4;             // column groups of 4
   static constexpr int RG = LAY_THREADS / CG;   // row groups
   static constexpr int RPT = TR / RG;           // rows per thread
-  static constexpr int TRP = TR + 4;            // padded row count of the transposed tiles
-  static_assert(RPT >= 1 && RG * RPT == TR, "tile shape");
+  static_assert(RPT >= 1 && RG * RPT == TR && TR >= 32, "tile shape");
 };
+
+// Transposed tile [HD][TR] with the 16-byte units of each column XOR-swizzled
+// by the column's group of four: a thread's 4 consecutive columns land in
+// distinct units, so its float4 row-group stores/loads take the minimum
+// number of wavefronts, while the friction loop's reads (one column, a
+// broadcast row group per half warp) stay conflict-free.
+template <int TR>
+GFN_DEV int tsw(int k, int r) {
+  return k * TR + ((((r >> 2) ^ ((k >> 2) & 7)) << 2) | (r & 3));
+}
 
 template <int N>
 GFN_DEV void lds_rows(const float* p, float (&r)[N]) {
@@ -184,6 +199,18 @@ GFN_DEV void lds_rows(const float* p, float (&r)[N]) {
   }
 }
 
+template <int N>
+GFN_DEV void sts_rows(float* p, const float (&r)[N]) {
+  if constexpr (N == 4) {
+    *reinterpret_cast<float4*>(p) = make_float4(r[0], r[1], r[2], r[3]);
+  } else if constexpr (N == 2) {
+    *reinterpret_cast<float2*>(p) = make_float2(r[0], r[1]);
+  } else {
+#pragma unroll
+    for (int i = 0; i < N; ++i) p[i] = r[i];
+  }
+}
+
 GFN_DEV float4 ldg4(const float* p) { return __ldg(reinterpret_cast<const float4*>(p)); }
 
 // p = v . U for every (row, q) of the tile, then ps = p^2 / (1 + |p| + 1e-6)
@@ -195,7 +222,7 @@ GFN_DEV void tile_gamma_p(const float* vT, const float* U, float* ps) {
     const int r = o / RK, q = o - (o / RK) * RK;
     float p = 0.f;
 #pragma unroll 16
-    for (int j = 0; j < HD; ++j) p = fmaf(vT[j * T::TRP + r], U[j * RK + q], p);
+    for (int j = 0; j < HD; ++j) p = fmaf(vT[tsw<T::TR>(j, r)], U[j * RK + q], p);
     float ss = p * p;
 #pragma unroll
     for (int m = 1; m < RK; m <<= 1) ss += __shfl_xor_sync(0xffffffffu, ss, m);
@@ -210,7 +237,7 @@ GFN_DEV void tile_gamma_p(const float* vT, const float* U, float* ps) {
 // (gfn/integrators/symplectic/leapfrog.py:72-114).
 template <int RK, int HD>
 GFN_DEV void tile_kick(const float* xT, const float* vT, const float* ps, const float* WfT,
-                       const float* Wg, const float* bfh, int r0, int c0, float hh,
+                       const float* WgT, const float* bfh, int r0, int c0, float hh,
                        const float (&F)[LayTile<HD>::RPT][4], float (&vn)[LayTile<HD>::RPT][4]) {
   using T = LayTile<HD>;
   constexpr int RPT = T::RPT;
@@ -223,7 +250,7 @@ GFN_DEV void tile_kick(const float* xT, const float* vT, const float* ps, const 
   for (int k = 0; k < HD; ++k) {
     const float4 w = *reinterpret_cast<const float4*>(WfT + k * HD + c0);
     float xr[RPT];
-    lds_rows<RPT>(xT + k * T::TRP + r0, xr);
+    lds_rows<RPT>(xT + tsw<T::TR>(k, r0), xr);
 #pragma unroll
     for (int i = 0; i < RPT; ++i) {
       acc[i][0] = fmaf(xr[i], w.x, acc[i][0]);
@@ -232,19 +259,33 @@ GFN_DEV void tile_kick(const float* xT, const float* vT, const float* ps, const 
       acc[i][3] = fmaf(xr[i], w.w, acc[i][3]);
     }
   }
+  float gs[RPT][4];
 #pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const int c = c0 + j;
-    float vr[RPT];
-    lds_rows<RPT>(vT + c * T::TRP + r0, vr);
-    const float bj = bfh[c];
+  for (int i = 0; i < RPT; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) gs[i][j] = 0.f;
+#pragma unroll
+  for (int q = 0; q < RK; ++q) {
+    const float4 w = *reinterpret_cast<const float4*>(WgT + q * HD + c0);
 #pragma unroll
     for (int i = 0; i < RPT; ++i) {
-      const float mu = sigmoid_f(acc[i][j] + bj) * 5.f;
-      float gsum = 0.f;
+      const float pq = ps[(r0 + i) * RK + q];
+      gs[i][0] = fmaf(pq, w.x, gs[i][0]);
+      gs[i][1] = fmaf(pq, w.y, gs[i][1]);
+      gs[i][2] = fmaf(pq, w.z, gs[i][2]);
+      gs[i][3] = fmaf(pq, w.w, gs[i][3]);
+    }
+  }
+  const float4 b4 = *reinterpret_cast<const float4*>(bfh + c0);
+  const float bj[4] = {b4.x, b4.y, b4.z, b4.w};
 #pragma unroll
-      for (int q = 0; q < RK; ++q) gsum = fmaf(ps[(r0 + i) * RK + q], Wg[c * RK + q], gsum);
-      const float g = soft_clamp20(gsum);
+  for (int j = 0; j < 4; ++j) {
+    float vr[RPT];
+    lds_rows<RPT>(vT + tsw<T::TR>(c0 + j, r0), vr);
+#pragma unroll
+    for (int i = 0; i < RPT; ++i) {
+      const float mu = sigmoid_f(acc[i][j] + bj[j]) * 5.f;
+      const float g = soft_clamp20(gs[i][j]);
       vn[i][j] = (vr[i] + hh * (F[i][j] - g)) / (1.f + hh * mu);
     }
   }
@@ -293,11 +334,11 @@ __global__ void __launch_bounds__(LAY_THREADS, 2) layered_pre_kernel(const LayPr
   }
   const float* WfT = hsm;
   const float* U = hsm + HD * HD;
-  const float* Wg = U + HD * RK;
-  const float* bfh = Wg + HD * RK;
+  const float* WgT = U + HD * RK;
+  const float* bfh = WgT + HD * RK;
   float* xT = hsm + o.hblock;
-  float* vT = xT + HD * T::TRP;
-  float* ps = vT + HD * T::TRP;
+  float* vT = xT + HD * T::TR;
+  float* ps = vT + HD * T::TR;
   const int tx = threadIdx.x % T::CG, ty = threadIdx.x / T::CG;
   const int c0 = 4 * tx, r0 = ty * RPT;
   const int gc = h * HD + c0;
@@ -306,6 +347,7 @@ __global__ void __launch_bounds__(LAY_THREADS, 2) layered_pre_kernel(const LayPr
   const float hh = 0.5f * eff;
 
   float F[RPT][4];
+  float xc[4][RPT], vc[4][RPT];  // the thread's tile, column-major for the stores
 #pragma unroll
   for (int i = 0; i < RPT; ++i) {
     const int b = row0 + r0 + i;
@@ -354,38 +396,46 @@ __global__ void __launch_bounds__(LAY_THREADS, 2) layered_pre_kernel(const LayPr
     }
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      xT[(c0 + j) * T::TRP + r0 + i] = xv[j];
-      vT[(c0 + j) * T::TRP + r0 + i] = vv[j];
+      xc[j][i] = xv[j];
+      vc[j][i] = vv[j];
     }
+  }
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    sts_rows<RPT>(xT + tsw<T::TR>(c0 + j, r0), xc[j]);
+    sts_rows<RPT>(vT + tsw<T::TR>(c0 + j, r0), vc[j]);
   }
   __syncthreads();
   // kick 1 at x
   tile_gamma_p<RK, HD>(vT, U, ps);
   __syncthreads();
   float vn[RPT][4];
-  tile_kick<RK, HD>(xT, vT, ps, WfT, Wg, bfh, r0, c0, hh, F, vn);
+  tile_kick<RK, HD>(xT, vT, ps, WfT, WgT, bfh, r0, c0, hh, F, vn);
   float xn[RPT][4];
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
     float xr[RPT];
-    lds_rows<RPT>(xT + (c0 + j) * T::TRP + r0, xr);
+    lds_rows<RPT>(xT + tsw<T::TR>(c0 + j, r0), xr);
 #pragma unroll
     for (int i = 0; i < RPT; ++i) xn[i][j] = xr[i] + eff * vn[i][j];
   }
   __syncthreads();
   // drift done: x' and v_half replace the tiles
 #pragma unroll
-  for (int i = 0; i < RPT; ++i)
+  for (int j = 0; j < 4; ++j) {
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      xT[(c0 + j) * T::TRP + r0 + i] = xn[i][j];
-      vT[(c0 + j) * T::TRP + r0 + i] = vn[i][j];
+    for (int i = 0; i < RPT; ++i) {
+      xc[j][i] = xn[i][j];
+      vc[j][i] = vn[i][j];
     }
+    sts_rows<RPT>(xT + tsw<T::TR>(c0 + j, r0), xc[j]);
+    sts_rows<RPT>(vT + tsw<T::TR>(c0 + j, r0), vc[j]);
+  }
   __syncthreads();
   // kick 2 at x'
   tile_gamma_p<RK, HD>(vT, U, ps);
   __syncthreads();
-  tile_kick<RK, HD>(xT, vT, ps, WfT, Wg, bfh, r0, c0, hh, F, vn);
+  tile_kick<RK, HD>(xT, vT, ps, WfT, WgT, bfh, r0, c0, hh, F, vn);
 #pragma unroll
   for (int i = 0; i < RPT; ++i) {
     const int b = row0 + r0 + i;
@@ -405,7 +455,7 @@ __global__ void __launch_bounds__(LAY_THREADS, 2) layered_pre_kernel(const LayPr
 
 template <int RK, int HD>
 constexpr size_t layered_pre_smem(int hblock) {
-  return ((size_t)hblock + 2 * HD * LayTile<HD>::TRP + LayTile<HD>::TR * RK) * 4;
+  return ((size_t)hblock + 2 * HD * LayTile<HD>::TR + LayTile<HD>::TR * RK) * 4;
 }
 
 // Last layer's RMSNorm + saturation -> x_seq[:, t], v_seq[:, t] and the state.
