@@ -41,15 +41,28 @@ struct LayPreInst {
   size_t smem;
 };
 
-bool lay_pre_for(int r, int hd, int hblock, LayPreInst* out) {
-#define GFN_L(RK, HD)                                                              \
-  if (r == RK && hd == HD) {                                                       \
-    *out = {layered_pre_kernel<RK, HD>, LayTile<HD>::TR, layered_pre_smem<RK, HD>(hblock)}; \
-    return true;                                                                   \
+// Row tile: the largest of 64 / 32 / 16 rows (32 for head_dim 128) that still gives two blocks
+// per SM (small batches need short tiles to fill the GPU), never below the
+// tile's minimum row count (one row per thread row-group).
+int pick_tile_rows(int batch, int heads, int hd, int sms) {
+  const int min_tr = hd >= 64 ? 16 : hd == 32 ? 32 : 64;
+  const int max_tr = hd == 128 ? 32 : 64;  // 8 rows per thread would spill
+  for (int tr = max_tr; tr > min_tr; tr >>= 1)
+    if ((long long)((batch + tr - 1) / tr) * heads >= 2LL * sms) return tr;
+  return min_tr;
+}
+
+bool lay_pre_for(int r, int hd, int tr, int hblock, LayPreInst* out) {
+#define GFN_L(RK, HD, TR)                                                         \
+  if (r == RK && hd == HD && tr == TR) {                                          \
+    *out = {layered_pre_kernel<RK, HD, TR>, TR, layered_pre_smem<RK, HD, TR>(hblock)}; \
+    return true;                                                                  \
   }
-  GFN_L(4, 16) GFN_L(4, 32) GFN_L(4, 64) GFN_L(4, 128)
-  GFN_L(8, 16) GFN_L(8, 32) GFN_L(8, 64) GFN_L(8, 128)
-  GFN_L(16, 16) GFN_L(16, 32) GFN_L(16, 64) GFN_L(16, 128)
+#define GFN_LR(RK) \
+  GFN_L(RK, 16, 64) GFN_L(RK, 32, 64) GFN_L(RK, 32, 32) GFN_L(RK, 64, 64) GFN_L(RK, 64, 32) \
+  GFN_L(RK, 64, 16) GFN_L(RK, 128, 32) GFN_L(RK, 128, 16)
+  GFN_LR(4) GFN_LR(8) GFN_LR(16)
+#undef GFN_LR
 #undef GFN_L
   return false;
 }
@@ -126,8 +139,11 @@ int gfn_leapfrog_layered_forward(const float* x_init, const float* v_init,
   if (workspace_floats < gfn_leapfrog_layered_workspace_floats(batch, dim))
     return fail(GFN_ERR_INVALID, "layered: workspace too small");
   if (batch == 0 || seq_len == 0) return GFN_OK;
+  int sms = 148, dev = 0;
+  if (cudaGetDevice(&dev) == cudaSuccess)
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   LayPreInst inst;
-  if (!lay_pre_for(rank, L.hd, lo.hblock, &inst))
+  if (!lay_pre_for(rank, L.hd, pick_tile_rows(batch, heads, L.hd, sms), lo.hblock, &inst))
     return fail(GFN_ERR_UNSUPPORTED, "layered: head_dim %d must be 16, 32, 64 or 128", L.hd);
   LayPreKernel pre = inst.fn;
   cublasHandle_t hb;

@@ -166,13 +166,14 @@ struct LayPreArgs {
 
 // Tile of the head-step kernel: TR rows of one head; thread (ty, tx) owns
 // rows ty*RPT .. +RPT-1 and columns 4tx .. 4tx+3 of the head.
-template <int HD>
+template <int HD, int TR_>
 struct LayTile {
-  static constexpr int TR = HD <= 64 ? 64 : 32;
+  static constexpr int TR = TR_;
   static constexpr int CG = HD / 4;             // column groups of 4
   static constexpr int RG = LAY_THREADS / CG;   // row groups
   static constexpr int RPT = TR / RG;           // rows per thread
-  static_assert(RPT >= 1 && RG * RPT == TR && TR >= 32, "tile shape");
+  static_assert(RPT >= 1 && RG * RPT == TR && TR >= 16 && TR * 4 >= LAY_THREADS / 4,
+                "tile shape");
 };
 
 // Transposed tile [HD][TR] with the 16-byte units of each column XOR-swizzled
@@ -182,7 +183,8 @@ struct LayTile {
 // broadcast row group per half warp) stay conflict-free.
 template <int TR>
 GFN_DEV int tsw(int k, int r) {
-  return k * TR + ((((r >> 2) ^ ((k >> 2) & 7)) << 2) | (r & 3));
+  constexpr int UM = (TR / 4 < 8 ? TR / 4 : 8) - 1;
+  return k * TR + ((((r >> 2) ^ ((k >> 2) & UM)) << 2) | (r & 3));
 }
 
 template <int N>
@@ -215,9 +217,9 @@ GFN_DEV float4 ldg4(const float* p) { return __ldg(reinterpret_cast<const float4
 
 // p = v . U for every (row, q) of the tile, then ps = p^2 / (1 + |p| + 1e-6)
 // (gfn/geometry/lowrank.py:93-98 without the W contraction).
-template <int RK, int HD>
+template <int RK, int HD, int TR>
 GFN_DEV void tile_gamma_p(const float* vT, const float* U, float* ps) {
-  using T = LayTile<HD>;
+  using T = LayTile<HD, TR>;
   for (int o = threadIdx.x; o < T::TR * RK; o += LAY_THREADS) {
     const int r = o / RK, q = o - (o / RK) * RK;
     float p = 0.f;
@@ -235,11 +237,12 @@ GFN_DEV void tile_gamma_p(const float* vT, const float* U, float* ps) {
 // + b_f) from the transposed x tile (a TR x HD x HD product in registers),
 // Gamma from ps, then v_new = (v + h (F - Gamma)) / (1 + h mu)
 // (gfn/integrators/symplectic/leapfrog.py:72-114).
-template <int RK, int HD>
+template <int RK, int HD, int TR>
 GFN_DEV void tile_kick(const float* xT, const float* vT, const float* ps, const float* WfT,
                        const float* WgT, const float* bfh, int r0, int c0, float hh,
-                       const float (&F)[LayTile<HD>::RPT][4], float (&vn)[LayTile<HD>::RPT][4]) {
-  using T = LayTile<HD>;
+                       const float (&F)[LayTile<HD, TR>::RPT][4],
+                       float (&vn)[LayTile<HD, TR>::RPT][4]) {
+  using T = LayTile<HD, TR>;
   constexpr int RPT = T::RPT;
   float acc[RPT][4];
 #pragma unroll
@@ -320,9 +323,9 @@ GFN_DEV void store_split6(__nv_bfloat16* row, int d, const float (&c)[4]) {
 // Input: the carried state (first layer of a token) or the previous layer's
 // mixing output with its RMSNorm / saturation applied on load.  Output: the
 // concat (x', v') as fp32 (cat) or split bf16 (catk).
-template <int RK, int HD>
+template <int RK, int HD, int TR>
 __global__ void __launch_bounds__(LAY_THREADS, 2) layered_pre_kernel(const LayPreArgs a) {
-  using T = LayTile<HD>;
+  using T = LayTile<HD, TR>;
   constexpr int RPT = T::RPT;
   extern __shared__ __align__(16) float hsm[];
   const int d = a.d, B = a.B, h = blockIdx.y;
@@ -407,10 +410,10 @@ __global__ void __launch_bounds__(LAY_THREADS, 2) layered_pre_kernel(const LayPr
   }
   __syncthreads();
   // kick 1 at x
-  tile_gamma_p<RK, HD>(vT, U, ps);
+  tile_gamma_p<RK, HD, TR>(vT, U, ps);
   __syncthreads();
   float vn[RPT][4];
-  tile_kick<RK, HD>(xT, vT, ps, WfT, WgT, bfh, r0, c0, hh, F, vn);
+  tile_kick<RK, HD, TR>(xT, vT, ps, WfT, WgT, bfh, r0, c0, hh, F, vn);
   float xn[RPT][4];
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
@@ -433,9 +436,9 @@ __global__ void __launch_bounds__(LAY_THREADS, 2) layered_pre_kernel(const LayPr
   }
   __syncthreads();
   // kick 2 at x'
-  tile_gamma_p<RK, HD>(vT, U, ps);
+  tile_gamma_p<RK, HD, TR>(vT, U, ps);
   __syncthreads();
-  tile_kick<RK, HD>(xT, vT, ps, WfT, WgT, bfh, r0, c0, hh, F, vn);
+  tile_kick<RK, HD, TR>(xT, vT, ps, WfT, WgT, bfh, r0, c0, hh, F, vn);
 #pragma unroll
   for (int i = 0; i < RPT; ++i) {
     const int b = row0 + r0 + i;
@@ -453,9 +456,9 @@ __global__ void __launch_bounds__(LAY_THREADS, 2) layered_pre_kernel(const LayPr
   }
 }
 
-template <int RK, int HD>
+template <int RK, int HD, int TR>
 constexpr size_t layered_pre_smem(int hblock) {
-  return ((size_t)hblock + 2 * HD * LayTile<HD>::TR + LayTile<HD>::TR * RK) * 4;
+  return ((size_t)hblock + 2 * HD * TR + TR * RK) * 4;
 }
 
 // Last layer's RMSNorm + saturation -> x_seq[:, t], v_seq[:, t] and the state.
