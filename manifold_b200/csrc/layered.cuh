@@ -215,83 +215,120 @@ GFN_DEV void sts_rows(float* p, const float (&r)[N]) {
 
 GFN_DEV float4 ldg4(const float* p) { return __ldg(reinterpret_cast<const float4*>(p)); }
 
-// p = v . U for every (row, q) of the tile, then ps = p^2 / (1 + |p| + 1e-6)
-// (gfn/geometry/lowrank.py:93-98 without the W contraction).
+// Gamma(v) for the thread's micro-tile, all in registers
+// (gfn/geometry/lowrank.py:93-98,125-127): partial p = v . U over the
+// thread's 4 columns, completed by a butterfly over the CG lanes that share
+// the rows, then g = 20 tanh((p^2 / (1 + |p| + 1e-6)) . W^T / 20).
 template <int RK, int HD, int TR>
-GFN_DEV void tile_gamma_p(const float* vT, const float* U, float* ps) {
-  using T = LayTile<HD, TR>;
-  for (int o = threadIdx.x; o < T::TR * RK; o += LAY_THREADS) {
-    const int r = o / RK, q = o - (o / RK) * RK;
-    float p = 0.f;
-#pragma unroll 16
-    for (int j = 0; j < HD; ++j) p = fmaf(vT[tsw<T::TR>(j, r)], U[j * RK + q], p);
-    float ss = p * p;
-#pragma unroll
-    for (int m = 1; m < RK; m <<= 1) ss += __shfl_xor_sync(0xffffffffu, ss, m);
-    const float sc = 1.f / ((1.f + sqrtf(ss)) + 1e-6f);
-    ps[o] = (p * p) * sc;
-  }
-}
-
-// One implicit kick for the thread's micro-tile: friction mu = 5 sigma(x Wf^T
-// + b_f) from the transposed x tile (a TR x HD x HD product in registers),
-// Gamma from ps, then v_new = (v + h (F - Gamma)) / (1 + h mu)
-// (gfn/integrators/symplectic/leapfrog.py:72-114).
-template <int RK, int HD, int TR>
-GFN_DEV void tile_kick(const float* xT, const float* vT, const float* ps, const float* WfT,
-                       const float* WgT, const float* bfh, int r0, int c0, float hh,
-                       const float (&F)[LayTile<HD, TR>::RPT][4],
-                       float (&vn)[LayTile<HD, TR>::RPT][4]) {
+GFN_DEV void tile_gamma(const float (&v)[LayTile<HD, TR>::RPT][4], const float* U,
+                        const float* WgT, int c0, float (&g)[LayTile<HD, TR>::RPT][4]) {
   using T = LayTile<HD, TR>;
   constexpr int RPT = T::RPT;
-  float acc[RPT][4];
+  float p[RPT][RK];
 #pragma unroll
   for (int i = 0; i < RPT; ++i)
 #pragma unroll
-    for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
-#pragma unroll 8
-  for (int k = 0; k < HD; ++k) {
-    const float4 w = *reinterpret_cast<const float4*>(WfT + k * HD + c0);
-    float xr[RPT];
-    lds_rows<RPT>(xT + tsw<T::TR>(k, r0), xr);
+    for (int q = 0; q < RK; ++q) p[i][q] = 0.f;
 #pragma unroll
-    for (int i = 0; i < RPT; ++i) {
-      acc[i][0] = fmaf(xr[i], w.x, acc[i][0]);
-      acc[i][1] = fmaf(xr[i], w.y, acc[i][1]);
-      acc[i][2] = fmaf(xr[i], w.z, acc[i][2]);
-      acc[i][3] = fmaf(xr[i], w.w, acc[i][3]);
+  for (int j = 0; j < 4; ++j) {
+#pragma unroll
+    for (int q4 = 0; q4 < RK; q4 += 4) {
+      const float4 u = *reinterpret_cast<const float4*>(U + (c0 + j) * RK + q4);
+#pragma unroll
+      for (int i = 0; i < RPT; ++i) {
+        p[i][q4 + 0] = fmaf(v[i][j], u.x, p[i][q4 + 0]);
+        p[i][q4 + 1] = fmaf(v[i][j], u.y, p[i][q4 + 1]);
+        p[i][q4 + 2] = fmaf(v[i][j], u.z, p[i][q4 + 2]);
+        p[i][q4 + 3] = fmaf(v[i][j], u.w, p[i][q4 + 3]);
+      }
     }
   }
-  float gs[RPT][4];
+#pragma unroll
+  for (int m = 1; m < T::CG; m <<= 1)
+#pragma unroll
+    for (int i = 0; i < RPT; ++i)
+#pragma unroll
+      for (int q = 0; q < RK; ++q) p[i][q] += __shfl_xor_sync(0xffffffffu, p[i][q], m);
+#pragma unroll
+  for (int i = 0; i < RPT; ++i) {
+    float ss = 0.f;
+#pragma unroll
+    for (int q = 0; q < RK; ++q) ss = fmaf(p[i][q], p[i][q], ss);
+    const float sc = 1.f / ((1.f + sqrtf(ss)) + 1e-6f);
+#pragma unroll
+    for (int q = 0; q < RK; ++q) p[i][q] = (p[i][q] * p[i][q]) * sc;
+  }
 #pragma unroll
   for (int i = 0; i < RPT; ++i)
 #pragma unroll
-    for (int j = 0; j < 4; ++j) gs[i][j] = 0.f;
+    for (int j = 0; j < 4; ++j) g[i][j] = 0.f;
 #pragma unroll
   for (int q = 0; q < RK; ++q) {
     const float4 w = *reinterpret_cast<const float4*>(WgT + q * HD + c0);
 #pragma unroll
     for (int i = 0; i < RPT; ++i) {
-      const float pq = ps[(r0 + i) * RK + q];
-      gs[i][0] = fmaf(pq, w.x, gs[i][0]);
-      gs[i][1] = fmaf(pq, w.y, gs[i][1]);
-      gs[i][2] = fmaf(pq, w.z, gs[i][2]);
-      gs[i][3] = fmaf(pq, w.w, gs[i][3]);
+      g[i][0] = fmaf(p[i][q], w.x, g[i][0]);
+      g[i][1] = fmaf(p[i][q], w.y, g[i][1]);
+      g[i][2] = fmaf(p[i][q], w.z, g[i][2]);
+      g[i][3] = fmaf(p[i][q], w.w, g[i][3]);
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < RPT; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) g[i][j] = soft_clamp20(g[i][j]);
+}
+
+// One implicit kick for the thread's micro-tile: friction mu = 5 sigma(x Wf^T
+// + b_f) from the transposed x tile (a TR x HD x HD product in registers),
+// then v_new = (v + h (F - Gamma(v))) / (1 + h mu)
+// (gfn/integrators/symplectic/leapfrog.py:72-114).
+template <int RK, int HD, int TR>
+GFN_DEV void tile_kick(const float* xT, const float* WfT, const float* U, const float* WgT,
+                       const float* bfh, int r0, int c0, float hh,
+                       const float (&F)[LayTile<HD, TR>::RPT][4],
+                       const float (&v)[LayTile<HD, TR>::RPT][4],
+                       float (&vn)[LayTile<HD, TR>::RPT][4]) {
+  using T = LayTile<HD, TR>;
+  constexpr int RPT = T::RPT;
+  constexpr int UM = (TR / 4 < 8 ? TR / 4 : 8) - 1;
+  float g[RPT][4];
+  tile_gamma<RK, HD, TR>(v, U, WgT, c0, g);
+  int offs[UM + 1];  // swizzled offset of the thread's row group, per column group
+#pragma unroll
+  for (int u = 0; u <= UM; ++u) offs[u] = (((r0 >> 2) ^ u) << 2) | (r0 & 3);
+  float acc[RPT][4];
+#pragma unroll
+  for (int i = 0; i < RPT; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
+  constexpr int KG = 4 * (UM + 1) < HD ? 4 * (UM + 1) : HD;  // one swizzle period
+#pragma unroll 1
+  for (int kb = 0; kb < HD; kb += KG) {
+#pragma unroll
+    for (int u = 0; u < KG; ++u) {
+      const int k = kb + u;
+      const float4 w = *reinterpret_cast<const float4*>(WfT + k * HD + c0);
+      float xr[RPT];
+      lds_rows<RPT>(xT + k * TR + offs[(u >> 2) & UM], xr);
+#pragma unroll
+      for (int i = 0; i < RPT; ++i) {
+        acc[i][0] = fmaf(xr[i], w.x, acc[i][0]);
+        acc[i][1] = fmaf(xr[i], w.y, acc[i][1]);
+        acc[i][2] = fmaf(xr[i], w.z, acc[i][2]);
+        acc[i][3] = fmaf(xr[i], w.w, acc[i][3]);
+      }
     }
   }
   const float4 b4 = *reinterpret_cast<const float4*>(bfh + c0);
   const float bj[4] = {b4.x, b4.y, b4.z, b4.w};
 #pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    float vr[RPT];
-    lds_rows<RPT>(vT + tsw<T::TR>(c0 + j, r0), vr);
+  for (int i = 0; i < RPT; ++i)
 #pragma unroll
-    for (int i = 0; i < RPT; ++i) {
+    for (int j = 0; j < 4; ++j) {
       const float mu = sigmoid_f(acc[i][j] + bj[j]) * 5.f;
-      const float g = soft_clamp20(gs[i][j]);
-      vn[i][j] = (vr[i] + hh * (F[i][j] - g)) / (1.f + hh * mu);
+      vn[i][j] = (v[i][j] + hh * (F[i][j] - g[i][j])) / (1.f + hh * mu);
     }
-  }
 }
 
 GFN_DEV void store_split6(__nv_bfloat16* row, int d, const float (&c)[4]) {
@@ -340,8 +377,6 @@ __global__ void __launch_bounds__(LAY_THREADS, 2) layered_pre_kernel(const LayPr
   const float* WgT = U + HD * RK;
   const float* bfh = WgT + HD * RK;
   float* xT = hsm + o.hblock;
-  float* vT = xT + HD * T::TR;
-  float* ps = vT + HD * T::TR;
   const int tx = threadIdx.x % T::CG, ty = threadIdx.x / T::CG;
   const int c0 = 4 * tx, r0 = ty * RPT;
   const int gc = h * HD + c0;
@@ -349,8 +384,8 @@ __global__ void __launch_bounds__(LAY_THREADS, 2) layered_pre_kernel(const LayPr
   const float eff = a.base_dt * a.lay[o.sc + h];
   const float hh = 0.5f * eff;
 
-  float F[RPT][4];
-  float xc[4][RPT], vc[4][RPT];  // the thread's tile, column-major for the stores
+  float F[RPT][4], X[RPT][4], V[RPT][4];
+  float xc[4][RPT];  // the thread's x tile, column-major for the stores
 #pragma unroll
   for (int i = 0; i < RPT; ++i) {
     const int b = row0 + r0 + i;
@@ -399,66 +434,57 @@ __global__ void __launch_bounds__(LAY_THREADS, 2) layered_pre_kernel(const LayPr
     }
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      xc[j][i] = xv[j];
-      vc[j][i] = vv[j];
+      xc[j][i] = X[i][j] = xv[j];
+      V[i][j] = vv[j];
     }
   }
 #pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    sts_rows<RPT>(xT + tsw<T::TR>(c0 + j, r0), xc[j]);
-    sts_rows<RPT>(vT + tsw<T::TR>(c0 + j, r0), vc[j]);
-  }
+  for (int j = 0; j < 4; ++j) sts_rows<RPT>(xT + tsw<T::TR>(c0 + j, r0), xc[j]);
   __syncthreads();
-  // kick 1 at x
-  tile_gamma_p<RK, HD, TR>(vT, U, ps);
-  __syncthreads();
-  float vn[RPT][4];
-  tile_kick<RK, HD, TR>(xT, vT, ps, WfT, WgT, bfh, r0, c0, hh, F, vn);
-  float xn[RPT][4];
+  // kick 1 at x, drift, kick 2 at x' (one loop body: one copy of the kick code)
+#pragma unroll 1
+  for (int kick = 0; kick < 2; ++kick) {
+    float vn[RPT][4];
+    tile_kick<RK, HD, TR>(xT, WfT, U, WgT, bfh, r0, c0, hh, F, V, vn);
 #pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    float xr[RPT];
-    lds_rows<RPT>(xT + tsw<T::TR>(c0 + j, r0), xr);
+    for (int i = 0; i < RPT; ++i)
 #pragma unroll
-    for (int i = 0; i < RPT; ++i) xn[i][j] = xr[i] + eff * vn[i][j];
-  }
-  __syncthreads();
-  // drift done: x' and v_half replace the tiles
+      for (int j = 0; j < 4; ++j) V[i][j] = vn[i][j];
+    if (kick == 0) {
 #pragma unroll
-  for (int j = 0; j < 4; ++j) {
+      for (int i = 0; i < RPT; ++i)
 #pragma unroll
-    for (int i = 0; i < RPT; ++i) {
-      xc[j][i] = xn[i][j];
-      vc[j][i] = vn[i][j];
+        for (int j = 0; j < 4; ++j) X[i][j] = X[i][j] + eff * V[i][j];
+      __syncthreads();
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+#pragma unroll
+        for (int i = 0; i < RPT; ++i) xc[j][i] = X[i][j];
+        sts_rows<RPT>(xT + tsw<T::TR>(c0 + j, r0), xc[j]);
+      }
+      __syncthreads();
     }
-    sts_rows<RPT>(xT + tsw<T::TR>(c0 + j, r0), xc[j]);
-    sts_rows<RPT>(vT + tsw<T::TR>(c0 + j, r0), vc[j]);
   }
-  __syncthreads();
-  // kick 2 at x'
-  tile_gamma_p<RK, HD, TR>(vT, U, ps);
-  __syncthreads();
-  tile_kick<RK, HD, TR>(xT, vT, ps, WfT, WgT, bfh, r0, c0, hh, F, vn);
 #pragma unroll
   for (int i = 0; i < RPT; ++i) {
     const int b = row0 + r0 + i;
     if (b >= B) continue;
     if (a.cat) {
       *reinterpret_cast<float4*>(a.cat + (long long)b * d + gc) =
-          make_float4(xn[i][0], xn[i][1], xn[i][2], xn[i][3]);
+          make_float4(X[i][0], X[i][1], X[i][2], X[i][3]);
       *reinterpret_cast<float4*>(a.cat + ((long long)B + b) * d + gc) =
-          make_float4(vn[i][0], vn[i][1], vn[i][2], vn[i][3]);
+          make_float4(V[i][0], V[i][1], V[i][2], V[i][3]);
     }
     if (a.catk) {
-      store_split6(a.catk + (long long)b * (LAY_SPLIT * d) + gc, d, xn[i]);
-      store_split6(a.catk + ((long long)B + b) * (LAY_SPLIT * d) + gc, d, vn[i]);
+      store_split6(a.catk + (long long)b * (LAY_SPLIT * d) + gc, d, X[i]);
+      store_split6(a.catk + ((long long)B + b) * (LAY_SPLIT * d) + gc, d, V[i]);
     }
   }
 }
 
 template <int RK, int HD, int TR>
 constexpr size_t layered_pre_smem(int hblock) {
-  return ((size_t)hblock + 2 * HD * TR + TR * RK) * 4;
+  return ((size_t)hblock + HD * TR) * 4;
 }
 
 // Last layer's RMSNorm + saturation -> x_seq[:, t], v_seq[:, t] and the state.
