@@ -207,7 +207,10 @@ int gfn_leapfrog_sequence_backward(const float* traj, const float* forces_f32,
  * the d x d mixing runs at GEMM rate when batch * dim is large.
  * `packed` comes from gfn_leapfrog_layered_pack (same operands as
  * gfn_leapfrog_pack); `workspace` holds at least
- * gfn_leapfrog_layered_workspace_floats(batch, dim) floats.
+ * gfn_leapfrog_layered_workspace_floats(batch, dim) floats (16-byte aligned,
+ * 256-byte preferred) and includes the GEMM library's workspace, so calls
+ * allocate nothing; the first call on a device creates that device's cuBLAS
+ * handle (the one allocation, kept for the process lifetime).
  */
 long long gfn_leapfrog_layered_pack_floats(int dim, int heads, int rank, int num_layers);
 int gfn_leapfrog_layered_pack(const float* U_stack, const float* W_stack,

@@ -15,6 +15,9 @@ using namespace gfn_abi;
 namespace {
 
 std::atomic<int> g_lay_mode{GFN_MIX_SPLIT_BF16};
+// cuBLAS workspace carved from the caller's workspace (4 MiB, 256-byte
+// aligned): the GEMMs allocate nothing.
+constexpr long long kLayCublasWsFloats = 1LL << 20;
 std::mutex g_cublas_mu;
 cublasHandle_t g_cublas[64] = {};
 
@@ -108,7 +111,7 @@ int gfn_leapfrog_layered_set_mixing(int mode) {
 }
 
 long long gfn_leapfrog_layered_workspace_floats(int batch, int dim) {
-  return 12LL * batch * dim + 2LL * batch + 4;
+  return 12LL * batch * dim + 2LL * batch + 4 + kLayCublasWsFloats;
 }
 
 int gfn_leapfrog_layered_forward(const float* x_init, const float* v_init,
@@ -151,6 +154,13 @@ int gfn_leapfrog_layered_forward(const float* x_init, const float* v_init,
   if (st) return st;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   if (cublasSetStream(hb, s) != CUBLAS_STATUS_SUCCESS) return fail(GFN_ERR_CUDA, "cublasSetStream");
+  {
+    const long long base = 12LL * batch * dim + 2LL * batch + 4;
+    float* cws = workspace + ((base + 63) / 64) * 64;
+    const size_t bytes = (size_t)(workspace_floats - ((base + 63) / 64) * 64) * 4;
+    if (cublasSetWorkspace(hb, cws, bytes) != CUBLAS_STATUS_SUCCESS)
+      return fail(GFN_ERR_CUDA, "cublasSetWorkspace");
+  }
   const long long BD = (long long)batch * dim;
   const int mode = g_lay_mode.load();
   float* cat = workspace;
