@@ -1,6 +1,7 @@
 // gfn_b200: the C ABI (include/gfn_b200.h) over the sm_100a kernels.
 // One translation unit: every kernel header is included here.
 #include <cstdarg>
+#include <cstdlib>
 #include <cstdio>
 #include <cstring>
 #include <atomic>
@@ -221,6 +222,20 @@ int make_plan(int B, const Layout& L, const DevInfo& di, SeqPlan* p) {
   // Fewest rows per cluster (most clusters, shortest per-CTA chain) such
   // that every cluster is resident in one wave.
   int R = 1;
+  // Tuning override: GFN_SEQ_ROWS=<rows per cluster> (clamped to what fits)
+  if (const char* env = getenv("GFN_SEQ_ROWS")) {
+    const int want = atoi(env);
+    if (want >= 1) {
+      R = want < Rmax ? want : Rmax;
+      if (!fit(R)) return fail(GFN_ERR_RESOURCES, "sequence plan for %d rows does not fit", R);
+      int active = 0;
+      const int st = query_active_clusters(kern, *p, &active);
+      if (st) return st;
+      p->max_active = active;
+      p->nclusters = (B + p->R - 1) / p->R;
+      return GFN_OK;
+    }
+  }
   for (int it = 0; it < 8; ++it) {
     if (!fit(R)) return fail(GFN_ERR_RESOURCES, "sequence plan for %d rows does not fit", R);
     int active = 0;

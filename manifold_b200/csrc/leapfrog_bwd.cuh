@@ -117,10 +117,11 @@ GFN_DEV void bwd_gamma(const float (&p)[RK], float s, const float* __restrict__ 
 }
 
 // z = x Wf^T + bf with x broadcast by shuffles; WfT is [k][j].
-template <int EPL>
-GFN_DEV void bwd_friction_pre(const float (&xx)[EPL], const float* __restrict__ WfT,
-                              const float* __restrict__ bf, int hd, const int (&jj)[EPL],
+template <int EPL, int HDC>
+GFN_DEV void bwd_friction_pre_impl(const float (&xx)[EPL], const float* __restrict__ WfT,
+                              const float* __restrict__ bf, int hd_rt, const int (&jj)[EPL],
                               float (&z)[EPL]) {
+  const int hd = HDC ? HDC : hd_rt;
   float z0[EPL], z1[EPL];
 #pragma unroll
   for (int e = 0; e < EPL; ++e) z0[e] = z1[e] = 0.f;
@@ -143,10 +144,22 @@ GFN_DEV void bwd_friction_pre(const float (&xx)[EPL], const float* __restrict__ 
   for (int e = 0; e < EPL; ++e) z[e] = (z0[e] + z1[e]) + bf[jj[e]];
 }
 
-// out_k = sum_j dz_j Wf[j][k] (Wf untransposed [j][k]) for the lane's k.
 template <int EPL>
-GFN_DEV void bwd_friction_t(const float (&dz)[EPL], const float* __restrict__ Wf, int hd,
+GFN_DEV void bwd_friction_pre(const float (&xx)[EPL], const float* __restrict__ WfT,
+                              const float* __restrict__ bf, int hd, const int (&jj)[EPL],
+                              float (&z)[EPL]) {
+  // compile-time head_dim when it fills the lanes (no per-k bounds checks)
+  if (hd == 32 * EPL)
+    bwd_friction_pre_impl<EPL, 32 * EPL>(xx, WfT, bf, hd, jj, z);
+  else
+    bwd_friction_pre_impl<EPL, 0>(xx, WfT, bf, hd, jj, z);
+}
+
+// out_k = sum_j dz_j Wf[j][k] (Wf untransposed [j][k]) for the lane's k.
+template <int EPL, int HDC>
+GFN_DEV void bwd_friction_t_impl(const float (&dz)[EPL], const float* __restrict__ Wf, int hd_rt,
                             const int (&jj)[EPL], float (&out)[EPL]) {
+  const int hd = HDC ? HDC : hd_rt;
   float o0[EPL], o1[EPL];
 #pragma unroll
   for (int e = 0; e < EPL; ++e) o0[e] = o1[e] = 0.f;
@@ -167,6 +180,16 @@ GFN_DEV void bwd_friction_t(const float (&dz)[EPL], const float* __restrict__ Wf
     }
 #pragma unroll
   for (int e = 0; e < EPL; ++e) out[e] = o0[e] + o1[e];
+}
+
+template <int EPL>
+GFN_DEV void bwd_friction_t(const float (&dz)[EPL], const float* __restrict__ Wf, int hd,
+                            const int (&jj)[EPL], float (&out)[EPL]) {
+  // compile-time head_dim when it fills the lanes (no per-k bounds checks)
+  if (hd == 32 * EPL)
+    bwd_friction_t_impl<EPL, 32 * EPL>(dz, Wf, hd, jj, out);
+  else
+    bwd_friction_t_impl<EPL, 0>(dz, Wf, hd, jj, out);
 }
 
 // Backward of G = Gamma(v) given dG: returns dv (added to dv), writes the

@@ -300,10 +300,11 @@ GFN_DEV void unit_gamma(const float (&vv)[EPL], const float* __restrict__ U,
 
 // mu(x) = 5 sigmoid(x Wf^T + bf) for the lane's elements; x is broadcast
 // across the warp by shuffles, WfT is [k][j] in shared memory.
-template <int EPL>
-GFN_DEV void unit_friction(const float (&xx)[EPL], const float* __restrict__ WfT,
-                           const float* __restrict__ bf, int hd, const int (&jj)[EPL],
+template <int EPL, int HDC>
+GFN_DEV void unit_friction_impl(const float (&xx)[EPL], const float* __restrict__ WfT,
+                           const float* __restrict__ bf, int hd_rt, const int (&jj)[EPL],
                            float (&mu)[EPL]) {
+  const int hd = HDC ? HDC : hd_rt;
   float z0[EPL], z1[EPL];
 #pragma unroll
   for (int e = 0; e < EPL; ++e) z0[e] = z1[e] = 0.f;
@@ -325,6 +326,17 @@ GFN_DEV void unit_friction(const float (&xx)[EPL], const float* __restrict__ WfT
   }
 #pragma unroll
   for (int e = 0; e < EPL; ++e) mu[e] = sigmoid_f((z0[e] + z1[e]) + bf[jj[e]]) * 5.f;
+}
+
+template <int EPL>
+GFN_DEV void unit_friction(const float (&xx)[EPL], const float* __restrict__ WfT,
+                           const float* __restrict__ bf, int hd, const int (&jj)[EPL],
+                           float (&mu)[EPL]) {
+  // compile-time head_dim when it fills the lanes (no per-k bounds checks)
+  if (hd == 32 * EPL)
+    unit_friction_impl<EPL, 32 * EPL>(xx, WfT, bf, hd, jj, mu);
+  else
+    unit_friction_impl<EPL, 0>(xx, WfT, bf, hd, jj, mu);
 }
 
 template <int RK, int EPL, int NW>
