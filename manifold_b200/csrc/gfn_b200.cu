@@ -86,7 +86,12 @@ int make_layout(int d, int H, int r, int NL, Layout* L) {
   // kernel finds a concat element's column block by shifts, so a chunk may
   // span blocks; otherwise the chunk is a multiple of 4 dividing C.
   const bool c_pow2 = (L->C & (L->C - 1)) == 0;
-  int KC = 2048 / L->C;
+  int kc_target = 4096;  // weight floats per chunk row block (measured best on B200 for C1-C5)
+  if (const char* env = getenv("GFN_SEQ_CHUNK_FLOATS")) {  // tuning override
+    const int v = atoi(env);
+    if (v >= 256) kc_target = v;
+  }
+  int KC = kc_target / L->C;
   if (c_pow2) {
     int p = 4;
     while (p * 2 <= KC && d % (p * 2) == 0) p *= 2;
@@ -203,7 +208,11 @@ int make_plan(int B, const Layout& L, const DevInfo& di, SeqPlan* p) {
     // layer's weights are in flight a whole layer ahead, as shared memory allows.
     const int want = L.mix ? 2 * L.nchunk + 2 : 2;
     // two CTAs per SM for the 8-warp form: each gets a bit under half the SM
-    const size_t budget = p->NW == 8 ? (size_t)114 * 1024 : (size_t)di.max_smem;
+    size_t budget = p->NW == 8 ? (size_t)114 * 1024 : (size_t)di.max_smem;
+    if (const char* env = getenv("GFN_SEQ_SMEM_KB")) {  // tuning override
+      const int kb = atoi(env);
+      if (kb > 0 && (size_t)kb * 1024 <= (size_t)di.max_smem) budget = (size_t)kb * 1024;
+    }
     for (int NST = want < SEQ_MAX_NST ? want : SEQ_MAX_NST; NST >= 2; --NST) {
       const size_t smem = plan_smem(L, R, NST, p);
       if (smem + 256 <= budget) {  // 256 B: the kernels' static shared memory
