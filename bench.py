@@ -359,6 +359,9 @@ def run_ours(args, c):
         achieved = alg / (step_ms / 1e3) / 1e9
         fl = flops_per_token(c) * B * T / (step_ms / 1e3) / 1e12
         plan = ops.leapfrog_plan(B, c["d"], c["H"], max(4, c["rank"] // c["H"]), c["NL"])
+        layer_step_ns = step_ms * 1e6 / (T * c["NL"])
+        latency = None if layered else latency_floor(dev, max(4, c["rank"] // c["H"]),
+                                                     plan["clusters"], layer_step_ns)
         result = {
             "metric": "recurrent tokens/sec (prefill+decode)",
             "value": round(value, 1),
@@ -382,11 +385,8 @@ def run_ours(args, c):
             + (steps if c.get("functional") else 0),
             "recurrence_path": "layered (head-step kernel + fp32 cuBLAS mixing GEMM per layer)"
             if layered else "fused persistent cluster kernel",
-            "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": hbm, "unit": "GB/s",
-                         "frac": round(achieved / hbm, 5), "traffic": None,
-                         "peak_source": peak_kind,
-                         "note": "latency-bound dependent chain; fp32 SIMT FLOP rate in fp32_tflops",
-                         "fp32_tflops": round(fl, 3)},
+            "roofline": roofline_entry(c, layered, achieved, hbm, bf16, peak_kind, fl, step_ms, T,
+                                       latency),
             "clocks": clocks,
             "wall_s_timed": round(wall, 3),
         }
@@ -396,6 +396,52 @@ def run_ours(args, c):
         dist.barrier()
         dist.destroy_process_group()
     return result
+
+
+def latency_floor(dev, rank, clusters, layer_step_ns, steps=20000):
+    """Latency roof of the fused recurrence: ns per layer step of the
+    dependent chain alone (gfn_debug_latency_probe: the reductions, kick
+    arithmetic and the two cluster exchanges of a layer step, no weight
+    traffic), on the plan's cluster count, against the measured layer step."""
+    import ctypes
+    import torch
+    from manifold_b200 import _lib
+    buf = torch.zeros(1, dtype=torch.int64, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    _lib.call("gfn_debug_latency_probe", rank, clusters, 100, ctypes.c_void_p(buf.data_ptr()),
+              stream.cuda_stream)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    _lib.call("gfn_debug_latency_probe", rank, clusters, steps, ctypes.c_void_p(buf.data_ptr()),
+              stream.cuda_stream)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    floor_ns = e0.elapsed_time(e1) * 1e6 / steps
+    return {"floor_ns_per_layer_step": round(floor_ns, 1),
+            "achieved_ns_per_layer_step": round(layer_step_ns, 1),
+            "frac": round(floor_ns / layer_step_ns, 4),
+            "floor_cycles_per_layer_step": round(buf.item() / steps, 1),
+            "source": "gfn_debug_latency_probe (dependent chain of one layer step, no weight traffic)"}
+
+
+def roofline_entry(c, layered, achieved_gbs, hbm, bf16, peak_kind, fp32_tflops, step_ms, T, latency):
+    """Roofline of the recurrence.  Layered path: tensor-bound mixing GEMMs
+    (split-bf16, K = 6d: 2 * 2 * B * 6d * d FLOP per layer and token) over
+    the whole step against the measured bf16 peak.  Fused path: algorithmic
+    HBM bytes against the measured copy bandwidth (tiny by construction: the
+    chain is latency-bound) plus the latency roof from the probe kernel."""
+    if layered:
+        fl = 2.0 * 2 * c["B"] * 6 * c["d"] * c["d"] * c["NL"] * T
+        tf = fl / (step_ms / 1e3) / 1e12
+        return {"bound": "tensor", "achieved": round(tf, 1), "peak": bf16, "unit": "TFLOP/s",
+                "frac": round(tf / bf16, 4), "traffic": None, "peak_source": peak_kind,
+                "note": "mixing GEMM tensor FLOPs (split-bf16, K = 6d) over the whole step time "
+                        "(head-step kernels included); fp32-equivalent FLOP rate in fp32_tflops",
+                "fp32_tflops": round(fp32_tflops, 3)}
+    return {"bound": "hbm", "achieved": round(achieved_gbs, 2), "peak": hbm, "unit": "GB/s",
+            "frac": round(achieved_gbs / hbm, 5), "traffic": None, "peak_source": peak_kind,
+            "note": "dependent chain: HBM is not the binding roof; see latency",
+            "fp32_tflops": round(fp32_tflops, 3), "latency": latency}
 
 
 def phase_profile(step, i, state, dev):

@@ -240,6 +240,16 @@ int gfn_leapfrog_layered_forward(const float* x_init, const float* v_init,
                                  gfn_stream_t stream);
 
 /* ------------------------------------------------------------------------
+ * Measurement: cycles of `steps` iterations of the layer-step latency floor
+ * (the fused recurrence's dependent chain with no weight traffic: Gamma and
+ * friction reductions, the kick arithmetic, the concat and RMSNorm cluster
+ * exchanges, the mixing reduction; 8-CTA clusters, one warp per CTA) on
+ * `clusters` clusters; CTA 0's clock64 difference is written to the device
+ * pointer `cycles`.  Per-head rank 4, 8 or 16. */
+int gfn_debug_latency_probe(int rank, int clusters, int steps, long long* cycles,
+                            gfn_stream_t stream);
+
+/* ------------------------------------------------------------------------
  * y_t = a_t y_{t-1} + x_t along t of [batch, seq_len, dim] (a NULL: a == 1).
  * Replaces parallel_scan_fused (gfn/cuda/src/layers/parallel_scan_fused.cu:81,
  * called from gfn/scan.py:20); semantics gfn/scan.py:11-104.

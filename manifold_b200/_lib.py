@@ -33,6 +33,7 @@ _SIGS = {
     "gfn_leapfrog_pack": [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i, _i, _i, _i, _p, _ll, _p],
     "gfn_leapfrog_plan": [_i, _i, _i, _i, _i, _p],
     "gfn_debug_set_phase_profile": [_p],
+    "gfn_debug_latency_probe": [_i, _i, _i, _p, _p],
     "gfn_parallel_scan_workspace_floats": [_i, _i, _i],
     "gfn_leapfrog_pack_train_floats": [_i, _i, _i, _i],
     "gfn_leapfrog_pack_train": [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i, _i, _i, _i, _p, _ll,
