@@ -238,7 +238,7 @@ template <int CT>
 GFN_DEV void bwd_mix(const BwdArgs& a, const float* catx, const float* catv, float* ox, float* ov,
                      const float* bx, const float* bv, float* chunk_ring, uint64_t* chunk_full,
                      uint64_t* chunk_empty, int& cslot, uint32_t& cphase, int tid, int lane) {
-  const int C = a.C, R = a.R, S = a.S, CS = chunk_row_stride(C);
+  const int C = a.C, R = a.R, S = a.S, CS = chunk_row_stride(C), swz = chunk_swizzle_mask(C);
   const bool active = tid < a.tiles * S;
   const int ms = tid % S, mtile = tid / S;
   const int mng = mtile % a.NG, mrg = mtile / a.NG;
@@ -261,10 +261,11 @@ GFN_DEV void bwd_mix(const BwdArgs& a, const float* catx, const float* catv, flo
         const int kg = k0 + kk;
         const float* cblk = a.logC >= 0 ? mcat + ((kg >> a.logC) * R) * C + (kg & (C - 1))
                                         : mcat + ((kg / C) * R) * C + (kg % C);
-        const float4 w0 = *reinterpret_cast<const float4*>(wc + (kk + 0) * CS + mn0);
-        const float4 w1 = *reinterpret_cast<const float4*>(wc + (kk + 1) * CS + mn0);
-        const float4 w2 = *reinterpret_cast<const float4*>(wc + (kk + 2) * CS + mn0);
-        const float4 w3 = *reinterpret_cast<const float4*>(wc + (kk + 3) * CS + mn0);
+        const float* wq = wc + kk * CS + ((((mn0 >> 2) ^ ((kk >> 2) & swz))) << 2);
+        const float4 w0 = *reinterpret_cast<const float4*>(wq);
+        const float4 w1 = *reinterpret_cast<const float4*>(wq + CS);
+        const float4 w2 = *reinterpret_cast<const float4*>(wq + 2 * CS);
+        const float4 w3 = *reinterpret_cast<const float4*>(wq + 3 * CS);
 #pragma unroll
         for (int rr = 0; rr < 4; ++rr) {
           if (rr < a.TR && mr0 + rr < R) {

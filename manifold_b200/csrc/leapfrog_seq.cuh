@@ -82,6 +82,10 @@ __host__ __device__ inline HeadOffsets head_offsets(int hpc, int hd, int r, int 
 // Row stride (floats) of a mixing chunk [KC][2C + 4]: the 4-float pad
 // rotates consecutive k rows across bank groups for the k-split lanes.
 __host__ __device__ inline int chunk_row_stride(int C) { return 2 * C + 4; }
+// 16-byte units of weight-chunk row k are XOR-permuted by (k / 4) & 7 (when
+// a row's 2C/4 data units are a multiple of 8): the mixing loop's lanes read
+// rows 4 apart, which the 4-float pad alone would map onto two bank groups.
+__host__ __device__ inline int chunk_swizzle_mask(int C) { return ((2 * C / 4) % 8 == 0) ? 7 : 0; }
 
 struct SeqArgs {
   const float* x0;
@@ -485,6 +489,7 @@ __global__ void __launch_bounds__(SeqShape<NW>::THREADS, SeqShape<NW>::MINB) lea
   const int mn0 = mng * 4, mr0 = mrg * a.TR;
   const float* mcat = (mn0 < C) ? catx : catv;
   const int CS = chunk_row_stride(C);
+  const int swz = chunk_swizzle_mask(C);
   const float inv_d = 1.f / (float)d;
   const float rms_eps = 1.1920928955078125e-07f;  // float32 machine epsilon
 
@@ -604,10 +609,11 @@ __global__ void __launch_bounds__(SeqShape<NW>::THREADS, SeqShape<NW>::MINB) lea
               const float* cblk = a.logC >= 0
                   ? mcat + ((kg >> a.logC) * R) * C + (kg & (C - 1))
                   : mcat + ((kg / C) * R) * C + (kg % C);
-              const float4 w0 = *reinterpret_cast<const float4*>(wc + (kk + 0) * CS + mn0);
-              const float4 w1 = *reinterpret_cast<const float4*>(wc + (kk + 1) * CS + mn0);
-              const float4 w2 = *reinterpret_cast<const float4*>(wc + (kk + 2) * CS + mn0);
-              const float4 w3 = *reinterpret_cast<const float4*>(wc + (kk + 3) * CS + mn0);
+              const float* wq = wc + kk * CS + ((((mn0 >> 2) ^ ((kk >> 2) & swz))) << 2);
+              const float4 w0 = *reinterpret_cast<const float4*>(wq);
+              const float4 w1 = *reinterpret_cast<const float4*>(wq + CS);
+              const float4 w2 = *reinterpret_cast<const float4*>(wq + 2 * CS);
+              const float4 w3 = *reinterpret_cast<const float4*>(wq + 3 * CS);
 #pragma unroll
               for (int rr = 0; rr < 4; ++rr) {
                 if (rr < a.TR && mr0 + rr < R) {

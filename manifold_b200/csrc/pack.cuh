@@ -80,7 +80,9 @@ __global__ void pack_kernel(const PackArgs a) {
       if (transposed) i -= a.nchunk;
       const int e2 = (int)(o2 - (long long)(transposed ? i + a.nchunk : i) * a.CF);
       const int CS = chunk_row_stride(C);
-      const int kk = e2 / CS, n = e2 - kk * CS;
+      const int kk = e2 / CS, np = e2 - kk * CS;
+      // stored unit np/4 holds logical unit (np/4) ^ ((kk/4) & mask) (the pad unit is not permuted)
+      const int n = np < 2 * C ? ((((np >> 2) ^ ((kk >> 2) & chunk_swizzle_mask(C)))) << 2) + (np & 3) : np;
       const int k = i * a.KC + kk;
       if (k < d && n < 2 * C && transposed) {
         if (n < C)
