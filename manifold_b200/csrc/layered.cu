@@ -173,6 +173,10 @@ int gfn_leapfrog_layered_forward(const float* x_init, const float* v_init,
   cudaError_t ae = cudaFuncSetAttribute(pre, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pre_smem);
   if (ae != cudaSuccess) return cuda_status(ae, "layered: shared memory attribute");
   const dim3 pre_grid((batch + inst.tr - 1) / inst.tr, heads);
+  // Small problems: each head-step block computes its rows' RMSNorm factors
+  // itself (every head re-reads the rows: batch * heads * dim * 8 bytes per
+  // layer from L2) instead of a separate launch.
+  const bool fuse_stat = (long long)batch * heads * dim * 8 <= (32LL << 20);
   const unsigned stat_blocks = (unsigned)((2LL * batch * 32 + 255) / 256);
   const float one = 1.f, zero = 0.f;
   for (int t = 0; t < seq_len; ++t) {
@@ -185,9 +189,11 @@ int gfn_leapfrog_layered_forward(const float* x_init, const float* v_init,
         a.in_stride = t == 0 ? state_row_stride : dim;
       } else {
         const float* prev = packed + (long long)(l - 1) * lo.total;
-        layered_rowstat_kernel<<<stat_blocks, 256, 0, s>>>(z, prev + lo.bx, prev + lo.bv, stat, batch, dim);
+        if (!fuse_stat)
+          layered_rowstat_kernel<<<stat_blocks, 256, 0, s>>>(z, prev + lo.bx, prev + lo.bv, stat, batch,
+                                                             dim);
         a.z = z;
-        a.stat = stat;
+        a.stat = fuse_stat ? nullptr : stat;
         a.prev = prev;
       }
       a.f32 = forces_f32; a.fbf16 = reinterpret_cast<const __nv_bfloat16*>(forces_bf16);

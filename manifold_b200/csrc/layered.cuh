@@ -117,19 +117,15 @@ __global__ void layered_pack_kernel(const LayPackArgs a) {
   }
 }
 
-// Per-row RMSNorm factor 1/sqrt(mean((z + b)^2) + eps) of zx and zv (one
-// warp per row, 128-bit loads; d % 4 == 0).
-__global__ void layered_rowstat_kernel(const float* __restrict__ z, const float* __restrict__ bx,
-                                       const float* __restrict__ bv, float* __restrict__ stat,
-                                       int B, int d) {
-  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
-  if (warp >= 2 * B) return;
-  const int which = warp / B, b = warp - which * B;
-  const float4* row = reinterpret_cast<const float4*>(z + ((long long)which * B + b) * d);
-  const float4* bias = reinterpret_cast<const float4*>(which == 0 ? bx : bv);
+// 1/sqrt(mean((z + b)^2) + eps) of one d-long row, by one warp (128-bit
+// loads, d % 4 == 0); the same order of operations wherever it runs.
+GFN_DEV float row_rms_factor(const float* __restrict__ zrow, const float* __restrict__ bias, int d,
+                             int lane) {
+  const float4* row = reinterpret_cast<const float4*>(zrow);
+  const float4* bb = reinterpret_cast<const float4*>(bias);
   float s = 0.f;
   for (int j = lane; j < d / 4; j += 32) {
-    const float4 u = row[j], c = __ldg(bias + j);
+    const float4 u = row[j], c = __ldg(bb + j);
     const float a0 = u.x + c.x, a1 = u.y + c.y, a2 = u.z + c.z, a3 = u.w + c.w;
     s = fmaf(a0, a0, s);
     s = fmaf(a1, a1, s);
@@ -137,7 +133,18 @@ __global__ void layered_rowstat_kernel(const float* __restrict__ z, const float*
     s = fmaf(a3, a3, s);
   }
   s = warp_sum(s);
-  if (lane == 0) stat[which * B + b] = 1.f / sqrtf(s * (1.f / (float)d) + 1.1920928955078125e-07f);
+  return 1.f / sqrtf(s * (1.f / (float)d) + 1.1920928955078125e-07f);
+}
+
+// Per-row RMSNorm factors of zx and zv (one warp per row).
+__global__ void layered_rowstat_kernel(const float* __restrict__ z, const float* __restrict__ bx,
+                                       const float* __restrict__ bv, float* __restrict__ stat,
+                                       int B, int d) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (warp >= 2 * B) return;
+  const int which = warp / B, b = warp - which * B;
+  const float r = row_rms_factor(z + ((long long)which * B + b) * d, which == 0 ? bx : bv, d, lane);
+  if (lane == 0) stat[which * B + b] = r;
 }
 
 struct LayPreArgs {
@@ -147,7 +154,7 @@ struct LayPreArgs {
   long long in_stride;  // 0: one row broadcast
   // ... or the previous layer's mixing output z [2][B][d] with its params
   const float* z;
-  const float* stat;    // [2][B]
+  const float* stat;    // [2][B], or NULL: the block computes its rows' factors
   const float* prev;    // previous layer's pack run (bias / norm gains)
   // force of token t
   const float* f32;
@@ -377,6 +384,18 @@ __global__ void __launch_bounds__(LAY_THREADS, 2) layered_pre_kernel(const LayPr
   const float* WgT = U + HD * RK;
   const float* bfh = WgT + HD * RK;
   float* xT = hsm + o.hblock;
+  float* sstat = xT + HD * TR;  // [2][TR] RMSNorm factors when computed here
+  if (a.z && !a.stat) {
+    const int w = threadIdx.x >> 5, ln = threadIdx.x & 31;
+    for (int q = w; q < 2 * TR; q += LAY_THREADS / 32) {
+      const int which = q / TR, r = q - which * TR, b = blockIdx.x * TR + r;
+      float f = 0.f;
+      if (b < B)
+        f = row_rms_factor(a.z + ((long long)which * B + b) * d, a.prev + (which ? o.bv : o.bx), d, ln);
+      if (ln == 0) sstat[q] = f;
+    }
+    __syncthreads();
+  }
   const int tx = threadIdx.x % T::CG, ty = threadIdx.x / T::CG;
   const int c0 = 4 * tx, r0 = ty * RPT;
   const int gc = h * HD + c0;
@@ -393,7 +412,8 @@ __global__ void __launch_bounds__(LAY_THREADS, 2) layered_pre_kernel(const LayPr
     F[i][0] = F[i][1] = F[i][2] = F[i][3] = 0.f;
     if (b < B) {
       if (a.z) {
-        const float rx = a.stat[b], rv = a.stat[B + b];
+        const float rx = a.stat ? a.stat[b] : sstat[r0 + i];
+        const float rv = a.stat ? a.stat[B + b] : sstat[TR + r0 + i];
         const float4 zx = ldg4(a.z + (long long)b * d + gc);
         const float4 zv = ldg4(a.z + ((long long)B + b) * d + gc);
         const float4 bx = ldg4(a.prev + o.bx + gc), bv = ldg4(a.prev + o.bv + gc);
@@ -484,7 +504,7 @@ __global__ void __launch_bounds__(LAY_THREADS, 2) layered_pre_kernel(const LayPr
 
 template <int RK, int HD, int TR>
 constexpr size_t layered_pre_smem(int hblock) {
-  return ((size_t)hblock + HD * TR) * 4;
+  return ((size_t)hblock + HD * TR + 2 * TR) * 4;
 }
 
 // Last layer's RMSNorm + saturation -> x_seq[:, t], v_seq[:, t] and the state.
