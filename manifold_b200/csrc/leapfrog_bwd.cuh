@@ -374,12 +374,12 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) leapfrog_bwd_kernel(const BwdA
       const int nck = a.mix ? 2 * a.nchunk : 0;
       for (long long g = 0; g < total_steps; ++g) {
         const int hslot = (int)(g & 1);
-        if (g >= 2) mbar_wait(&head_empty[hslot], (uint32_t)(((g >> 1) - 1) & 1), 128);
+        if (g >= 2) mbar_wait(&head_empty[hslot], (uint32_t)(((g >> 1) - 1) & 1), kProducerSleepNs);
         mbar_arrive_expect_tx(&head_full[hslot], (uint32_t)a.HST * 4u);
         bulk_g2s(head_ring + hslot * a.HST, my_pack + l * layer_stride, (uint32_t)a.HST * 4u,
                  &head_full[hslot]);
         for (int i = 0; i < nck; ++i) {
-          if (!first_lap) mbar_wait(&chunk_empty[slot], empty_phase, 128);
+          if (!first_lap) mbar_wait(&chunk_empty[slot], empty_phase, kProducerSleepNs);
           mbar_arrive_expect_tx(&chunk_full[slot], (uint32_t)a.CF * 4u);
           bulk_g2s(chunk_ring + (long long)slot * a.CF,
                    my_pack + l * layer_stride + a.HST + (long long)i * a.CF, (uint32_t)a.CF * 4u,

@@ -53,6 +53,9 @@ struct SeqShape {
   static constexpr int MINB = NW == 8 ? 2 : 1;
 };
 constexpr int SEQ_NBAR = 48;                        // mbarrier slots reserved
+// Back-off of the weight-producer warp between barrier polls (the poll itself
+// suspends in hardware; a long sleep only delays the refill).
+constexpr uint32_t kProducerSleepNs = 128;
 constexpr int SEQ_BAR_BYTES = SEQ_NBAR * 8;
 constexpr int SEQ_MAX_NST = (SEQ_NBAR - 6) / 2;     // ring depth limit
 constexpr int SEQ_PROF_N = 12;
@@ -404,12 +407,12 @@ __global__ void __launch_bounds__(SeqShape<NW>::THREADS, SeqShape<NW>::MINB) lea
       bool first_lap = true;
       for (long long g = 0; g < total_steps; ++g) {
         const int hslot = (int)(g & 1);
-        if (g >= 2) mbar_wait(&head_empty[hslot], (uint32_t)(((g >> 1) - 1) & 1), 128);
+        if (g >= 2) mbar_wait(&head_empty[hslot], (uint32_t)(((g >> 1) - 1) & 1), kProducerSleepNs);
         mbar_arrive_expect_tx(&head_full[hslot], (uint32_t)a.HS * 4u);
         bulk_g2s(head_ring + hslot * a.HS, my_pack + l * layer_stride, (uint32_t)a.HS * 4u,
                  &head_full[hslot]);
         for (int i = 0; a.mix && i < a.nchunk; ++i) {
-          if (!first_lap) mbar_wait(&chunk_empty[slot], empty_phase, 128);
+          if (!first_lap) mbar_wait(&chunk_empty[slot], empty_phase, kProducerSleepNs);
           mbar_arrive_expect_tx(&chunk_full[slot], (uint32_t)a.CF * 4u);
           bulk_g2s(chunk_ring + (long long)slot * a.CF,
                    my_pack + l * layer_stride + a.chunk_base + (long long)i * a.CF, (uint32_t)a.CF * 4u,
