@@ -266,6 +266,9 @@ def run_ours(args, c):
     stream = torch.cuda.current_stream(dev)
     if args.path != "auto":
         m.recurrence_path = args.path
+    if args.mixing != "default":
+        ops.set_layered_mixing({"split_bf16": ops.MIX_SPLIT_BF16, "split_f16": ops.MIX_SPLIT_F16,
+                                "fp32": ops.MIX_FP32_SIMT}[args.mixing])
     layered = m._use_layered(B)
     packed, meta = m._pack.get(list(m.layers), layered=layered)
     seqfn = ops.leapfrog_layered_sequence if layered else ops.leapfrog_sequence
@@ -383,7 +386,7 @@ def run_ours(args, c):
                     "h2d_bytes_per_step": int(B * T * 8), "d2h_bytes_per_step": int(2 * B * c["d"] * 4)},
             "gpu_launches": steps * ((2 * c["NL"] + 1) * T if layered else 1)
             + (steps if c.get("functional") else 0),
-            "recurrence_path": "layered (head-step kernel + fp32 cuBLAS mixing GEMM per layer)"
+            "recurrence_path": "layered (head-step kernel + split-precision tensor-core mixing GEMM per layer)"
             if layered else "fused persistent cluster kernel",
             "roofline": roofline_entry(c, layered, achieved, hbm, bf16, peak_kind, fl, step_ms, T,
                                        latency),
@@ -431,12 +434,21 @@ def roofline_entry(c, layered, achieved_gbs, hbm, bf16, peak_kind, fp32_tflops, 
     HBM bytes against the measured copy bandwidth (tiny by construction: the
     chain is latency-bound) plus the latency roof from the probe kernel."""
     if layered:
-        fl = 2.0 * 2 * c["B"] * 6 * c["d"] * c["d"] * c["NL"] * T
+        from manifold_b200.cuda import ops
+        mode = ops.get_layered_mixing()
+        split = {ops.MIX_SPLIT_BF16: 6, ops.MIX_SPLIT_F16: 3}.get(mode)
+        if split is None:  # fp32 SGEMM: no tensor work
+            return {"bound": "hbm", "achieved": round(achieved_gbs, 2), "peak": hbm, "unit": "GB/s",
+                    "frac": round(achieved_gbs / hbm, 5), "traffic": None, "peak_source": peak_kind,
+                    "fp32_tflops": round(fp32_tflops, 3)}
+        fl = 2.0 * 2 * c["B"] * split * c["d"] * c["d"] * c["NL"] * T
         tf = fl / (step_ms / 1e3) / 1e12
+        kind = "split-fp16, K = 3d" if split == 3 else "split-bf16, K = 6d"
         return {"bound": "tensor", "achieved": round(tf, 1), "peak": bf16, "unit": "TFLOP/s",
                 "frac": round(tf / bf16, 4), "traffic": None, "peak_source": peak_kind,
-                "note": "mixing GEMM tensor FLOPs (split-bf16, K = 6d) over the whole step time "
-                        "(head-step kernels included); fp32-equivalent FLOP rate in fp32_tflops",
+                "note": f"mixing GEMM tensor FLOPs ({kind}) over the whole step time "
+                        "(head-step kernels included; fp16 and bf16 tensor rates are equal); "
+                        "fp32-equivalent FLOP rate in fp32_tflops",
                 "fp32_tflops": round(fp32_tflops, 3)}
     return {"bound": "hbm", "achieved": round(achieved_gbs, 2), "peak": hbm, "unit": "GB/s",
             "frac": round(achieved_gbs / hbm, 5), "traffic": None, "peak_source": peak_kind,
@@ -522,6 +534,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--path", default="auto", choices=["auto", "fused", "layered"],
                     help="recurrence path (auto: by batch size)")
+    ap.add_argument("--mixing", default="default", choices=["default", "split_bf16", "split_f16", "fp32"],
+                    help="layered path's mixing GEMM arithmetic (default: the library's)")
     ap.add_argument("--phase-profile", action="store_true",
                     help="print per-phase cycle counts of CTA 0 for one step instead")
     args = ap.parse_args()

@@ -39,6 +39,7 @@ enum {
 enum {
   GFN_DEVERR_MBAR_TIMEOUT = 1, /* a bounded wait for a bulk copy gave up */
   GFN_DEVERR_BAD_TOKEN = 2,    /* a token id outside [0, vocab) (force 0 used) */
+  GFN_DEVERR_F16_RANGE = 4,    /* layered GFN_MIX_SPLIT_F16: an activation |x| >= 2^15 */
 };
 
 const char* gfn_status_string(int status);
@@ -221,13 +222,20 @@ int gfn_leapfrog_layered_pack(const float* U_stack, const float* W_stack,
                               float* packed, long long packed_floats, gfn_stream_t stream);
 long long gfn_leapfrog_layered_workspace_floats(int batch, int dim);
 /* Arithmetic of the layered path's mixing GEMM (process-wide; returns the
- * previous mode, or a negative status for an unknown mode):
- *   GFN_MIX_SPLIT_BF16 (default) each fp32 operand split into three bf16
- *     pieces, the six cross products of order <= 2^-16 summed by one bf16
- *     tensor-core GEMM with fp32 accumulation (K = 6 * dim): fp32-level
- *     accuracy at tensor-core rate.
+ * previous mode, or a negative status for an unknown mode; mode -1 only
+ * returns the current one):
+ *   GFN_MIX_SPLIT_F16 (default) each operand split into two fp16 pieces
+ *     (weights scaled by a power of two per layer so their small pieces stay
+ *     normal); the three products of order >= 2^-11 summed by one fp16
+ *     tensor-core GEMM with fp32 accumulation (K = 3 * dim): error ~2^-22 per
+ *     product, the order of an fp32 SGEMM's own accumulation error.
+ *     Activations must stay below 2^15 in magnitude; larger ones set
+ *     GFN_DEVERR_F16_RANGE.
+ *   GFN_MIX_SPLIT_BF16 each fp32 operand split into three bf16 pieces, the
+ *     six cross products of order <= 2^-16 summed by one bf16 tensor-core
+ *     GEMM (K = 6 * dim): full fp32 range, twice the GEMM cost.
  *   GFN_MIX_FP32_SIMT  plain fp32 SGEMM on the CUDA cores. */
-enum { GFN_MIX_SPLIT_BF16 = 0, GFN_MIX_FP32_SIMT = 1 };
+enum { GFN_MIX_SPLIT_BF16 = 0, GFN_MIX_FP32_SIMT = 1, GFN_MIX_SPLIT_F16 = 2 };
 int gfn_leapfrog_layered_set_mixing(int mode);
 int gfn_leapfrog_layered_forward(const float* x_init, const float* v_init,
                                  long long state_row_stride, const float* forces_f32,

@@ -20,8 +20,23 @@ __device__ int gfn_device_err;
 //       2 = a token id outside [0, vocab).
 constexpr int kDevErrMbarTimeout = 1;
 constexpr int kDevErrBadToken = 2;
+constexpr int kDevErrF16Range = 4;
 
 GFN_DEV void gfn_flag_error(int bits) { atomicOr(&gfn_device_err, bits); }
+
+// Each translation unit of the library has its own copy of gfn_device_err
+// (no relocatable device code); this reads (and optionally clears) the copy
+// of the unit it is compiled into.
+static inline cudaError_t gfn_unit_error_word(int* v, int reset, cudaStream_t s) {
+  cudaError_t e = cudaMemcpyFromSymbolAsync(v, gfn_device_err, sizeof(int), 0, cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e == cudaSuccess && reset && *v) {
+    const int zero = 0;
+    e = cudaMemcpyToSymbolAsync(gfn_device_err, &zero, sizeof(int), 0, cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  }
+  return e;
+}
 
 GFN_DEV uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));

@@ -376,17 +376,12 @@ const char* gfn_build_info(void) {
 int gfn_get_device_error(int* bits, int reset, gfn_stream_t stream) {
   if (!bits) return fail(GFN_ERR_INVALID, "bits is NULL");
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  int v = 0;
-  cudaError_t e = cudaMemcpyFromSymbolAsync(&v, gfn_device_err, sizeof(int), 0, cudaMemcpyDeviceToHost, s);
-  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
-  if (e != cudaSuccess) return cuda_status(e, "read device error word");
-  *bits = v;
-  if (reset && v) {
-    const int zero = 0;
-    e = cudaMemcpyToSymbolAsync(gfn_device_err, &zero, sizeof(int), 0, cudaMemcpyHostToDevice, s);
-    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
-    if (e != cudaSuccess) return cuda_status(e, "reset device error word");
-  }
+  int v0 = 0, v1 = 0, v2 = 0;
+  cudaError_t e = gfn_unit_error_word(&v0, reset, s);
+  if (e == cudaSuccess) e = error_word_layered(&v1, reset, s);
+  if (e == cudaSuccess) e = error_word_probe(&v2, reset, s);
+  if (e != cudaSuccess) return cuda_status(e, "device error word");
+  *bits = v0 | v1 | v2;
   return GFN_OK;
 }
 

@@ -11,10 +11,14 @@
 using namespace gfn;
 using namespace gfn_abi;
 
+namespace gfn_abi {
+cudaError_t error_word_layered(int* v, int reset, cudaStream_t s) { return gfn_unit_error_word(v, reset, s); }
+}  // namespace gfn_abi
+
 
 namespace {
 
-std::atomic<int> g_lay_mode{GFN_MIX_SPLIT_BF16};
+std::atomic<int> g_lay_mode{GFN_MIX_SPLIT_F16};
 // cuBLAS workspace carved from the caller's workspace (4 MiB, 256-byte
 // aligned): the GEMMs allocate nothing.
 constexpr long long kLayCublasWsFloats = 1LL << 20;
@@ -100,12 +104,19 @@ int gfn_leapfrog_layered_pack(const float* U_stack, const float* W_stack,
   a.LF = lay_offsets(heads, L.hd, rank, dim).total;
   if (packed_floats < a.LF * num_layers) return fail(GFN_ERR_INVALID, "layered pack: buffer too small");
   if (!aligned16(packed)) return fail(GFN_ERR_ALIGN, "layered pack: output not 16-byte aligned");
-  layered_pack_kernel<<<148 * 8, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(a);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const LayOffsets lo = lay_offsets(heads, L.hd, rank, dim);
+  // per-layer max|W| slot: zeroed, then atomic max over both mixing matrices
+  cudaError_t e = cudaMemset2DAsync(packed + lo.wsc, (size_t)a.LF * 4, 0, 4, (size_t)num_layers, s);
+  if (e != cudaSuccess) return cuda_status(e, "layered pack: scale slots");
+  layered_absmax_kernel<<<148 * 4, 256, 0, s>>>(mix_x_w, mix_v_w, packed, num_layers, dim, a.LF, lo.wsc);
+  layered_pack_kernel<<<148 * 8, 256, 0, s>>>(a);
   return launch_status("layered_pack_kernel");
 }
 
 int gfn_leapfrog_layered_set_mixing(int mode) {
-  if (mode != GFN_MIX_SPLIT_BF16 && mode != GFN_MIX_FP32_SIMT)
+  if (mode == -1) return g_lay_mode.load();
+  if (mode != GFN_MIX_SPLIT_BF16 && mode != GFN_MIX_FP32_SIMT && mode != GFN_MIX_SPLIT_F16)
     return -fail(GFN_ERR_INVALID, "mixing mode %d", mode);
   return g_lay_mode.exchange(mode);
 }
@@ -199,7 +210,9 @@ int gfn_leapfrog_layered_forward(const float* x_init, const float* v_init,
       a.f32 = forces_f32; a.fbf16 = reinterpret_cast<const __nv_bfloat16*>(forces_bf16);
       a.ids = token_ids; a.table = embed_table; a.vocab = vocab; a.mask = mask;
       a.t = t; a.L = seq_len; a.lay = lay; a.B = batch;
-      if (mode == GFN_MIX_SPLIT_BF16) a.catk = catk; else a.cat = cat; a.d = dim; a.H = heads;
+      if (mode == GFN_MIX_SPLIT_BF16) a.catk = catk;
+      else if (mode == GFN_MIX_SPLIT_F16) a.catkh = reinterpret_cast<__half*>(catk);
+      else a.cat = cat; a.d = dim; a.H = heads;
       a.hd = L.hd; a.base_dt = base_dt;
       pre<<<pre_grid, LAY_THREADS, pre_smem, s>>>(a);
       // z[i] = cat[i] . W_i^T for i in {x, v}: column-major view z^T = W cat^T
@@ -210,6 +223,15 @@ int gfn_leapfrog_layered_forward(const float* x_init, const float* v_init,
             hb, CUBLAS_OP_T, CUBLAS_OP_N, dim, batch, K, &one, lay + lo.WK, CUDA_R_16BF, K,
             (long long)dim * K, catk, CUDA_R_16BF, K, (long long)batch * K, &zero, z, CUDA_R_32F,
             dim, BD, 2, CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT);
+      } else if (mode == GFN_MIX_SPLIT_F16) {
+        // alpha = 1/s and beta = 0 live in the pack (device pointer mode)
+        const int K = LAY_SPLIT_H * dim;
+        cublasSetPointerMode(hb, CUBLAS_POINTER_MODE_DEVICE);
+        cs = cublasGemmStridedBatchedEx(
+            hb, CUBLAS_OP_T, CUBLAS_OP_N, dim, batch, K, lay + lo.wsc + 2, lay + lo.WH, CUDA_R_16F, K,
+            (long long)dim * K, catk, CUDA_R_16F, K, (long long)batch * K, lay + lo.wsc + 3, z,
+            CUDA_R_32F, dim, BD, 2, CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT);
+        cublasSetPointerMode(hb, CUBLAS_POINTER_MODE_HOST);
       } else {
         cs = cublasSgemmStridedBatched(hb, CUBLAS_OP_T, CUBLAS_OP_N, dim, batch, dim, &one,
                                        lay + lo.Wx, dim, (long long)dim * dim, cat, dim, BD, &zero,

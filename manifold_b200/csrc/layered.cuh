@@ -12,6 +12,8 @@
 // and after the last layer `finalize` applies the last RMSNorm/saturation and
 // writes x_seq / v_seq and the carried state.
 #pragma once
+#include <cuda_fp16.h>
+
 #include "leapfrog_seq.cuh"
 
 namespace gfn {
@@ -26,12 +28,16 @@ constexpr int LAY_THREADS = 256;
 // along K as [w0 w1 w0 w2 w1 w0] against the activations' [c0 c0 c1 c0 c1 c2],
 // so one bf16 GEMM with K = 6d and fp32 accumulation sums the six products
 // c_i w_j with i + j <= 2.  The dropped terms are below 2^-26 of |c w|.
+// Then the split-fp16 copy WH [2][d][3d] (fp16): weights scaled by s (a power
+// of two per layer), w s = w0 + w1 laid along K as [w0 w1 w0] against the
+// activations' [c0 c0 c1]; then 4 floats: max|W|, s, 1/s, 0.
 struct LayOffsets {
   int head, hblock, sc, bx, bv, gx, gv;
-  long long Wx, Wv, WK;
+  long long Wx, Wv, WK, WH, wsc;
   long long total;
 };
 constexpr int LAY_SPLIT = 6;
+constexpr int LAY_SPLIT_H = 3;
 
 __host__ __device__ inline LayOffsets lay_offsets(int H, int hd, int r, int d) {
   LayOffsets o;
@@ -45,8 +51,36 @@ __host__ __device__ inline LayOffsets lay_offsets(int H, int hd, int r, int d) {
   o.Wx = o.gv + d;
   o.Wv = o.Wx + (long long)d * d;
   o.WK = o.Wv + (long long)d * d;
-  o.total = o.WK + (long long)LAY_SPLIT * d * d;  // 2 * d * 6d bf16
+  o.WH = o.WK + (long long)LAY_SPLIT * d * d;     // after 2 * d * 6d bf16
+  o.wsc = o.WH + (long long)LAY_SPLIT_H * d * d;  // after 2 * d * 3d fp16
+  o.total = o.wsc + 4;
   return o;
+}
+
+// Power-of-two weight scale putting max|W| s in [2^13, 2^14): the small fp16
+// pieces of the scaled weights stay normal; 1 for an all-zero layer.
+GFN_DEV float lay_weight_scale(float m) {
+  if (!(m > 0.f)) return 1.f;
+  int e;
+  frexpf(m, &e);  // m = f 2^e, f in [0.5, 1)
+  return ldexpf(1.f, 14 - e);
+}
+
+// max |Wx|, |Wv| of each layer into the pack's scale slot (non-negative
+// floats order like their bit patterns, so an integer atomic max works).
+// The slot is zeroed first.
+__global__ void layered_absmax_kernel(const float* __restrict__ Wx, const float* __restrict__ Wv,
+                                      float* out, int NL, int d, long long LF, long long wsc) {
+  const long long n = (long long)d * d;
+  for (long long e = blockIdx.x * (long long)blockDim.x + threadIdx.x; e < 2 * NL * n;
+       e += (long long)gridDim.x * blockDim.x) {
+    const int which = (int)(e / (NL * n));
+    const long long r = e - (long long)which * NL * n;
+    const int l = (int)(r / n);
+    const float w = fabsf((which == 0 ? Wx : Wv)[r]);
+    if (w > 0.f)
+      atomicMax(reinterpret_cast<unsigned*>(out + (long long)l * LF + wsc), __float_as_uint(w));
+  }
 }
 
 struct LayPackArgs {
@@ -90,6 +124,30 @@ __global__ void layered_pack_kernel(const LayPackArgs a) {
       v = a.Wx[(long long)l * d * d + (off - o.Wx)];
     } else if (off < o.WK) {
       v = a.Wv[(long long)l * d * d + (off - o.Wv)];
+    } else if (off >= o.wsc) {
+      const int q = (int)(off - o.wsc);
+      if (q == 0) continue;  // max|W|, written by layered_absmax_kernel
+      const float s = lay_weight_scale(a.out[(long long)l * a.LF + o.wsc]);
+      v = q == 1 ? s : q == 2 ? 1.f / s : 0.f;
+    } else if (off >= o.WH) {
+      // two fp16 of WH per float slot: [w0 w1 w0] of the scaled weight
+      const float s = lay_weight_scale(a.out[(long long)l * a.LF + o.wsc]);
+      const long long q = 2 * (off - o.WH);
+      __half pr[2];
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const long long qq = q + u;
+        const long long rowk = (long long)LAY_SPLIT_H * d;
+        const int which = (int)(qq / ((long long)d * rowk));
+        const long long rem = qq - (long long)which * d * rowk;
+        const int orow = (int)(rem / rowk), kk = (int)(rem - (long long)orow * rowk);
+        const int seg = kk / d, col = kk - seg * d;
+        const float w = (which == 0 ? a.Wx : a.Wv)[((long long)l * d + orow) * d + col] * s;
+        const __half w0 = __float2half_rn(w);
+        const __half w1 = __float2half_rn(w - __half2float(w0));
+        pr[u] = seg == 1 ? w1 : w0;
+      }
+      v = __uint_as_float((unsigned)__half_as_ushort(pr[0]) | ((unsigned)__half_as_ushort(pr[1]) << 16));
     } else {
       // two bf16 of WK per float slot
       const long long q = 2 * (off - o.WK);
@@ -167,6 +225,7 @@ struct LayPreArgs {
   const float* lay;     // this layer's pack run
   float* cat;           // [2][B][d] head-step outputs (x', v'), or NULL
   __nv_bfloat16* catk;  // [2][B][6d] split-bf16 head-step outputs, or NULL
+  __half* catkh;        // [2][B][3d] split-fp16 head-step outputs, or NULL
   int B, d, H, hd;
   float base_dt;
 };
@@ -363,6 +422,27 @@ GFN_DEV void store_split6(__nv_bfloat16* row, int d, const float (&c)[4]) {
   *reinterpret_cast<uint2*>(row + 5 * d) = u2;
 }
 
+GFN_DEV void store_split3h(__half* row, int d, const float (&c)[4]) {
+  // [c0 c0 c1] per column, 4 columns per 8-byte store; |c| >= 2^15 is flagged
+  __half p0[4], p1[4];
+  bool bad = false;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    bad |= !(fabsf(c[j]) < 32768.f);
+    p0[j] = __float2half_rn(c[j]);
+    p1[j] = __float2half_rn(c[j] - __half2float(p0[j]));
+  }
+  if (bad) gfn_flag_error(kDevErrF16Range);
+  uint2 u0, u1;
+  u0.x = (unsigned)__half_as_ushort(p0[0]) | ((unsigned)__half_as_ushort(p0[1]) << 16);
+  u0.y = (unsigned)__half_as_ushort(p0[2]) | ((unsigned)__half_as_ushort(p0[3]) << 16);
+  u1.x = (unsigned)__half_as_ushort(p1[0]) | ((unsigned)__half_as_ushort(p1[1]) << 16);
+  u1.y = (unsigned)__half_as_ushort(p1[2]) | ((unsigned)__half_as_ushort(p1[3]) << 16);
+  *reinterpret_cast<uint2*>(row) = u0;
+  *reinterpret_cast<uint2*>(row + d) = u0;
+  *reinterpret_cast<uint2*>(row + 2 * d) = u1;
+}
+
 // Head step of one layer for TR rows of one head (grid: row tiles x heads).
 // Input: the carried state (first layer of a token) or the previous layer's
 // mixing output with its RMSNorm / saturation applied on load.  Output: the
@@ -498,6 +578,10 @@ __global__ void __launch_bounds__(LAY_THREADS, 2) layered_pre_kernel(const LayPr
     if (a.catk) {
       store_split6(a.catk + (long long)b * (LAY_SPLIT * d) + gc, d, X[i]);
       store_split6(a.catk + ((long long)B + b) * (LAY_SPLIT * d) + gc, d, V[i]);
+    }
+    if (a.catkh) {
+      store_split3h(a.catkh + (long long)b * (LAY_SPLIT_H * d) + gc, d, X[i]);
+      store_split3h(a.catkh + ((long long)B + b) * (LAY_SPLIT_H * d) + gc, d, V[i]);
     }
   }
 }

@@ -5,6 +5,10 @@
 using namespace gfn;
 using namespace gfn_abi;
 
+namespace gfn_abi {
+cudaError_t error_word_probe(int* v, int reset, cudaStream_t s) { return gfn_unit_error_word(v, reset, s); }
+}  // namespace gfn_abi
+
 extern "C" int gfn_debug_latency_probe(int rank, int clusters, int steps, long long* cycles,
                                        gfn_stream_t stream) {
   if (clusters < 1 || steps < 1 || !cycles) return fail(GFN_ERR_INVALID, "latency probe: bad arguments");

@@ -281,10 +281,11 @@ def test_errors_are_loud():
     assert ops.device_error(reset=True) == 0
 
 
-@pytest.fixture(params=["split_bf16", "fp32_simt"])
+@pytest.fixture(params=["split_bf16", "fp32_simt", "split_f16"])
 def mixing(request):
     from manifold_b200.cuda import ops
-    mode = ops.MIX_SPLIT_BF16 if request.param == "split_bf16" else ops.MIX_FP32_SIMT
+    mode = {"split_bf16": ops.MIX_SPLIT_BF16, "fp32_simt": ops.MIX_FP32_SIMT,
+            "split_f16": ops.MIX_SPLIT_F16}[request.param]
     prev = ops.set_layered_mixing(mode)
     yield request.param
     ops.set_layered_mixing(prev)
@@ -354,3 +355,31 @@ def test_layered_matches_fused_shapes(d, H, rank, B, mixing):
         xl, vl, _, _ = m.recurrence(force_manual=F)
     rowwise_close(xl.cpu().numpy(), xf.cpu().numpy(), SEQ_RTOL, SEQ_ATOL, "x_seq")
     rowwise_close(vl.cpu().numpy(), vf.cpu().numpy(), SEQ_RTOL, SEQ_ATOL, "v_seq")
+
+
+def test_layered_f16_range_flag():
+    """Activations beyond the split-fp16 range are reported through the device
+    error word (no fault); the bf16 split handles the same input."""
+    import manifold_b200 as gfn
+    from manifold_b200 import _lib
+    from manifold_b200.cuda import ops
+    torch.manual_seed(2)
+    m = gfn.Manifold(vocab_size=10, dim=256, depth=1, rank=32, heads=4,
+                     integrator_type="leapfrog").cuda().eval()
+    m.recurrence_path = "layered"
+    F = torch.full((8, 1, 256), 2.0e6, device="cuda")
+    _lib.device_error(reset=True)
+    prev = ops.set_layered_mixing(ops.MIX_SPLIT_F16)
+    try:
+        with torch.no_grad():
+            m.recurrence(force_manual=F)
+        torch.cuda.synchronize()
+        assert _lib.device_error(reset=True) & 4
+        ops.set_layered_mixing(ops.MIX_SPLIT_BF16)
+        with torch.no_grad():
+            x, v, _, _ = m.recurrence(force_manual=F)
+        torch.cuda.synchronize()
+        assert _lib.device_error(reset=True) & 4 == 0
+        assert torch.isfinite(x).all() and torch.isfinite(v).all()
+    finally:
+        ops.set_layered_mixing(prev)
