@@ -258,6 +258,27 @@ int gfn_debug_latency_probe(int rank, int clusters, int steps, long long* cycles
                             gfn_stream_t stream);
 
 /* ------------------------------------------------------------------------
+ * Readout GEMMs at fp32-level accuracy on the tensor cores (the readout
+ * nn.Linear(d -> vocab) of gfn/model.py:393-397 and its backward, which the
+ * reference runs as fp32 torch matmuls).  gfn_split_f16 scales an fp32
+ * matrix x [rows][cols] by a power of two s (max|x| s in [2^13, 2^14); s is
+ * written to scale[1], scale[0] is scratch) and splits it into two fp16
+ * pieces along its K dimension: K = cols gives out [rows][3 cols], K = rows
+ * (k_along_rows) gives out [3 rows][cols]; segments [x0 x0 x1] for the A
+ * operand, [x0 x1 x0] for the B operand (role_b).  gfn_gemm_split_f16 then
+ * forms row-major C[M][N] = op(A) op(B) / (s_A s_B) + beta C with one fp16
+ * GEMM (K' = 3K, fp32 accumulation); op(A) is [M][K] (A split with K along
+ * its columns, or along its rows for a transposed A), op(B) is [K][N].
+ * K is laid out and multiplied in 512-wide blocks whose products are summed
+ * in fp32 (the tensor cores' accumulation error grows with K).
+ * alpha_beta: 3 device floats of scratch. */
+int gfn_split_f16(const float* x, long long rows, long long cols, int k_along_rows, int role_b, void* out,
+                  float* scale, gfn_stream_t stream);
+int gfn_gemm_split_f16(int M, int N, int K, const void* a2, int a_k_rows, const void* b2, int b_k_rows,
+                       const float* scale_a, const float* scale_b, float beta, float* c,
+                       float* alpha_beta, gfn_stream_t stream);
+
+/* ------------------------------------------------------------------------
  * y_t = a_t y_{t-1} + x_t along t of [batch, seq_len, dim] (a NULL: a == 1).
  * Replaces parallel_scan_fused (gfn/cuda/src/layers/parallel_scan_fused.cu:81,
  * called from gfn/scan.py:20); semantics gfn/scan.py:11-104.

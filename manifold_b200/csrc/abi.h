@@ -30,5 +30,6 @@ int make_layout(int d, int H, int r, int NL, Layout* L);
 // Device error words of the other translation units (see gfn_unit_error_word).
 cudaError_t error_word_layered(int* v, int reset, cudaStream_t s);
 cudaError_t error_word_probe(int* v, int reset, cudaStream_t s);
+cudaError_t error_word_readout(int* v, int reset, cudaStream_t s);
 
 }  // namespace gfn_abi

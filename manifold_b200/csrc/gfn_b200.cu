@@ -376,12 +376,13 @@ const char* gfn_build_info(void) {
 int gfn_get_device_error(int* bits, int reset, gfn_stream_t stream) {
   if (!bits) return fail(GFN_ERR_INVALID, "bits is NULL");
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  int v0 = 0, v1 = 0, v2 = 0;
+  int v0 = 0, v1 = 0, v2 = 0, v3 = 0;
   cudaError_t e = gfn_unit_error_word(&v0, reset, s);
   if (e == cudaSuccess) e = error_word_layered(&v1, reset, s);
   if (e == cudaSuccess) e = error_word_probe(&v2, reset, s);
+  if (e == cudaSuccess) e = error_word_readout(&v3, reset, s);
   if (e != cudaSuccess) return cuda_status(e, "device error word");
-  *bits = v0 | v1 | v2;
+  *bits = v0 | v1 | v2 | v3;
   return GFN_OK;
 }
 

@@ -150,5 +150,5 @@ def manifold_train_forward(model, input_ids, attention_mask, state, force_manual
     mask = None if attention_mask is None else attention_mask.to(torch.float32)
     x_seq, v_seq, xf, vf = leapfrog_sequence_train(list(model.layers), x, v, forces, mask)
     out = x_seq if model.holographic else model.readout_norm(x_seq)
-    logits = model.readout(out)
+    logits = model._apply_readout(out)
     return logits, (xf, vf), [], list(v_seq.unbind(1)), list(x_seq.unbind(1)), forces
