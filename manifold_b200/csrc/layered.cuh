@@ -448,7 +448,7 @@ GFN_DEV void store_split3h(__half* row, int d, const float (&c)[4]) {
 // mixing output with its RMSNorm / saturation applied on load.  Output: the
 // concat (x', v') as fp32 (cat) or split bf16 (catk).
 template <int RK, int HD, int TR>
-__global__ void __launch_bounds__(LAY_THREADS, 2) layered_pre_kernel(const LayPreArgs a) {
+__global__ void __launch_bounds__(LAY_THREADS, (TR * HD <= 2048 && RK <= 8) ? 3 : 2) layered_pre_kernel(const LayPreArgs a) {
   using T = LayTile<HD, TR>;
   constexpr int RPT = T::RPT;
   extern __shared__ __align__(16) float hsm[];
