@@ -224,7 +224,11 @@ long long gfn_leapfrog_layered_workspace_floats(int batch, int dim);
 /* Arithmetic of the layered path's mixing GEMM (process-wide; returns the
  * previous mode, or a negative status for an unknown mode; mode -1 only
  * returns the current one):
- *   GFN_MIX_SPLIT_F16 (default) each operand split into two fp16 pieces
+ *   GFN_MIX_UMMA_F16 (default) the split-fp16 products below computed by this
+ *     library's own tcgen05 kernel (TMA-fed, TMEM accumulator, three MMAs per
+ *     K step: c0 w0 + c0 w1 + c1 w0); needs dim % 64 == 0, otherwise the
+ *     call uses GFN_MIX_SPLIT_F16.
+ *   GFN_MIX_SPLIT_F16 each operand split into two fp16 pieces
  *     (weights scaled by a power of two per layer so their small pieces stay
  *     normal); the three products of order >= 2^-11 summed by one fp16
  *     tensor-core GEMM with fp32 accumulation (K = 3 * dim): error ~2^-22 per
@@ -235,7 +239,7 @@ long long gfn_leapfrog_layered_workspace_floats(int batch, int dim);
  *     six cross products of order <= 2^-16 summed by one bf16 tensor-core
  *     GEMM (K = 6 * dim): full fp32 range, twice the GEMM cost.
  *   GFN_MIX_FP32_SIMT  plain fp32 SGEMM on the CUDA cores. */
-enum { GFN_MIX_SPLIT_BF16 = 0, GFN_MIX_FP32_SIMT = 1, GFN_MIX_SPLIT_F16 = 2 };
+enum { GFN_MIX_SPLIT_BF16 = 0, GFN_MIX_FP32_SIMT = 1, GFN_MIX_SPLIT_F16 = 2, GFN_MIX_UMMA_F16 = 3 };
 int gfn_leapfrog_layered_set_mixing(int mode);
 int gfn_leapfrog_layered_forward(const float* x_init, const float* v_init,
                                  long long state_row_stride, const float* forces_f32,

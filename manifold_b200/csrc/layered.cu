@@ -5,9 +5,11 @@
 #include <mutex>
 
 #include <cublas_v2.h>
+#include <cudaTypedefs.h>
 
 #include "abi.h"
 #include "layered.cuh"
+#include "mix_umma.cuh"
 
 using namespace gfn;
 using namespace gfn_abi;
@@ -19,7 +21,7 @@ cudaError_t error_word_layered(int* v, int reset, cudaStream_t s) { return gfn_u
 
 namespace {
 
-std::atomic<int> g_lay_mode{GFN_MIX_SPLIT_F16};
+std::atomic<int> g_lay_mode{GFN_MIX_UMMA_F16};
 // cuBLAS workspace carved from the caller's workspace (4 MiB, 256-byte
 // aligned): the GEMMs allocate nothing.
 constexpr long long kLayCublasWsFloats = 1LL << 20;
@@ -40,6 +42,94 @@ int cublas_for_device(cublasHandle_t* out) {
   }
   *out = g_cublas[dev];
   return GFN_OK;
+}
+
+// ---------------------------------------------------------------- UMMA mixing
+// cuTensorMapEncodeTiled from the driver (no link-time libcuda dependency).
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// fp16 tensor map with a 64-element (128-byte) inner box and 128-byte swizzle.
+int encode_f16_map(CUtensorMap* m, const void* base, int rank, const cuuint64_t* dims,
+                   const cuuint64_t* strides_bytes, const cuuint32_t* box) {
+  PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
+  if (!enc) return fail(GFN_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, (cuuint32_t)rank, const_cast<void*>(base), dims,
+                   strides_bytes, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(GFN_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return GFN_OK;
+}
+
+// Column tile of the UMMA mixing GEMM: 256 when that gives at least one
+// tile per SM, else narrower tiles (small batches), never wider than d.
+int pick_mix_bn(int batch, int dim, int sms) {
+  if (const char* env = getenv("GFN_MIX_BN")) {  // tuning override
+    const int t = atoi(env);
+    if ((t == 64 || t == 128 || t == 256) && dim % t == 0) return t;
+  }
+  const long long mt = (batch + 127) / 128;
+  for (int bn = 256; bn > 64; bn >>= 1)
+    if (dim % bn == 0 && 2 * mt * (dim / bn) >= sms) return bn;
+  return 64;
+}
+
+struct MixUmmaPlan {
+  CUtensorMap ta, tb;
+  size_t smem;
+  int bn, grid;
+};
+
+template <int BN>
+int mix_plan_for(MixUmmaPlan* p, int sms, int mtiles, int d) {
+  p->smem = MixCfg<BN>::SMEM;
+  p->bn = BN;
+  const int tiles = 2 * mtiles * (d / BN);
+  p->grid = tiles < sms ? tiles : sms;
+  cudaError_t e = cudaFuncSetAttribute(mix_umma_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)p->smem);
+  return e == cudaSuccess ? GFN_OK : cuda_status(e, "mixing GEMM: shared memory attribute");
+}
+
+// Tensor maps of one forward call: activations catkh [2B][3d] and the packed
+// split weights WH of every layer, [NL][2d][3d] with the pack's layer stride.
+int make_mix_plan(MixUmmaPlan* p, const __half* catkh, const float* packed, const LayOffsets& lo,
+                  int batch, int dim, int num_layers, int sms) {
+  const int bn = pick_mix_bn(batch, dim, sms);
+  const int mtiles = (batch + 127) / 128;
+  int st = bn == 256 ? mix_plan_for<256>(p, sms, mtiles, dim)
+         : bn == 128 ? mix_plan_for<128>(p, sms, mtiles, dim)
+                     : mix_plan_for<64>(p, sms, mtiles, dim);
+  if (st) return st;
+  const cuuint64_t adims[2] = {(cuuint64_t)3 * dim, (cuuint64_t)2 * batch};
+  const cuuint64_t astr[1] = {(cuuint64_t)6 * dim};
+  const cuuint32_t abox[2] = {64, 128};
+  st = encode_f16_map(&p->ta, catkh, 2, adims, astr, abox);
+  if (st) return st;
+  const cuuint64_t bdims[3] = {(cuuint64_t)3 * dim, (cuuint64_t)2 * dim, (cuuint64_t)num_layers};
+  const cuuint64_t bstr[2] = {(cuuint64_t)6 * dim, (cuuint64_t)lo.total * 4};
+  const cuuint32_t bbox[3] = {64, (cuuint32_t)bn, 1};
+  return encode_f16_map(&p->tb, packed + lo.WH, 3, bdims, bstr, bbox);
+}
+
+void launch_mix(const MixUmmaPlan& p, const MixUmmaArgs& ma, cudaStream_t s) {
+  if (p.bn == 256)
+    mix_umma_kernel<256><<<p.grid, MixCfg<256>::THREADS, p.smem, s>>>(p.ta, p.tb, ma);
+  else if (p.bn == 128)
+    mix_umma_kernel<128><<<p.grid, MixCfg<128>::THREADS, p.smem, s>>>(p.ta, p.tb, ma);
+  else
+    mix_umma_kernel<64><<<p.grid, MixCfg<64>::THREADS, p.smem, s>>>(p.ta, p.tb, ma);
 }
 
 using LayPreKernel = void (*)(LayPreArgs);
@@ -124,7 +214,8 @@ int gfn_leapfrog_layered_pack(const float* U_stack, const float* W_stack,
 
 int gfn_leapfrog_layered_set_mixing(int mode) {
   if (mode == -1) return g_lay_mode.load();
-  if (mode != GFN_MIX_SPLIT_BF16 && mode != GFN_MIX_FP32_SIMT && mode != GFN_MIX_SPLIT_F16)
+  if (mode != GFN_MIX_SPLIT_BF16 && mode != GFN_MIX_FP32_SIMT && mode != GFN_MIX_SPLIT_F16 &&
+      mode != GFN_MIX_UMMA_F16)
     return -fail(GFN_ERR_INVALID, "mixing mode %d", mode);
   return g_lay_mode.exchange(mode);
 }
@@ -181,13 +272,21 @@ int gfn_leapfrog_layered_forward(const float* x_init, const float* v_init,
       return fail(GFN_ERR_CUDA, "cublasSetWorkspace");
   }
   const long long BD = (long long)batch * dim;
-  const int mode = g_lay_mode.load();
+  int mode = g_lay_mode.load();
+  // the tcgen05 kernel tiles K by 64 and N by at least 64 columns
+  if (mode == GFN_MIX_UMMA_F16 && (dim % 64 != 0 || 3LL * dim > (1LL << 31) / 4))
+    mode = GFN_MIX_SPLIT_F16;
   float* cat = workspace;
   __nv_bfloat16* catk = reinterpret_cast<__nv_bfloat16*>(workspace + 2 * BD);
   float* z = workspace + 8 * BD;
   float* xs = workspace + 10 * BD;
   float* vs = workspace + 11 * BD;
   float* stat = workspace + 12 * BD;
+  MixUmmaPlan mix;
+  if (mode == GFN_MIX_UMMA_F16) {
+    st = make_mix_plan(&mix, reinterpret_cast<const __half*>(catk), packed, lo, batch, dim, num_layers, sms);
+    if (st) return st;
+  }
   const size_t pre_smem = inst.smem;
   cudaError_t ae = cudaFuncSetAttribute(pre, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pre_smem);
   if (ae != cudaSuccess) return cuda_status(ae, "layered: shared memory attribute");
@@ -219,10 +318,17 @@ int gfn_leapfrog_layered_forward(const float* x_init, const float* v_init,
       a.ids = token_ids; a.table = embed_table; a.vocab = vocab; a.mask = mask;
       a.t = t; a.L = seq_len; a.lay = lay; a.B = batch;
       if (mode == GFN_MIX_SPLIT_BF16) a.catk = catk;
-      else if (mode == GFN_MIX_SPLIT_F16) a.catkh = reinterpret_cast<__half*>(catk);
+      else if (mode == GFN_MIX_SPLIT_F16 || mode == GFN_MIX_UMMA_F16) a.catkh = reinterpret_cast<__half*>(catk);
       else a.cat = cat; a.d = dim; a.H = heads;
       a.hd = L.hd; a.base_dt = base_dt;
       pre<<<pre_grid, LAY_THREADS, pre_smem, s>>>(a);
+      if (mode == GFN_MIX_UMMA_F16) {
+        MixUmmaArgs ma;
+        ma.z = z; ma.alpha = lay + lo.wsc + 2; ma.B = batch; ma.d = dim; ma.layer = l;
+        ma.mtiles = (batch + 127) / 128; ma.ntiles = dim / mix.bn;
+        launch_mix(mix, ma, s);
+        continue;
+      }
       // z[i] = cat[i] . W_i^T for i in {x, v}: column-major view z^T = W cat^T
       cublasStatus_t cs;
       if (mode == GFN_MIX_SPLIT_BF16) {

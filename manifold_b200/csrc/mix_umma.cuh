@@ -1,0 +1,211 @@
+// Head-mixing GEMM of the layered recurrence on the 5th-generation tensor
+// cores (tcgen05 + TMEM + TMA), with fp32-level accuracy by operand splitting.
+//
+// Per layer (gfn/layers/base.py:305-317, the out_proj_x / out_proj_v Linear
+// without its bias) the two products
+//     z_x = cat_x . W_x^T,   z_v = cat_v . W_v^T      ([B, d] x [d, d] each)
+// are computed from fp16 pieces: every activation c = c0 + c1 (written by the
+// head-step kernel as rows [c0 | c0 | c1] of width 3d) and every weight,
+// scaled by a power of two s per layer, w s = w0 + w1 (packed as rows
+// [w0 | w1 | w0]).  The three products of order >= 2^-11,
+//     c0 w0 + c0 w1 + c1 w0,
+// accumulate in one fp32 TMEM accumulator and the epilogue multiplies by
+// 1/s.  The dropped term c1 w1 is below 2^-22 of |c w|.
+//
+// Structure (one CTA per SM, persistent over output tiles):
+//   warp 0      TMA producer: per K-block of 64 the four operand tiles
+//               c0, c1 [128 x 64] and w0, w1 [BN x 64] (128-byte swizzle)
+//               into a STAGES-deep shared-memory ring;
+//   warp 1      allocates TMEM (two BN-column accumulators) and issues the
+//               tcgen05.mma instructions (M=128, N=BN, K=16) from one thread,
+//               releasing each ring slot with tcgen05.commit;
+//   warps 2..5  epilogue: tcgen05.ld of the accumulator (each warp its
+//               32-lane quarter of TMEM), scale, fp32 stores of z; the
+//               second accumulator lets the next tile's MMAs run meanwhile.
+// Tiles: (matrix, 128-row block, BN-column block), column blocks fastest so
+// that CTAs running together share their activation rows in L2.
+#pragma once
+#include <cuda.h>
+
+#include "umma.cuh"
+
+namespace gfn {
+
+struct MixUmmaArgs {
+  float* z;            // [2][B][d] fp32
+  const float* alpha;  // device scalar 1/s of this layer
+  int B, d, layer;
+  int mtiles, ntiles;  // 128-row blocks of B, BN-column blocks of d
+};
+
+template <int BN>
+struct MixCfg {
+  static constexpr int BM = 128, BK = 64;
+  static constexpr int A_BYTES = BM * BK * 2;
+  static constexpr int B_BYTES = BN * BK * 2;
+  static constexpr int STAGE = 2 * A_BYTES + 2 * B_BYTES;
+  static constexpr int STAGES_FIT = (200 * 1024) / STAGE;
+  static constexpr int STAGES = STAGES_FIT > 8 ? 8 : STAGES_FIT;
+  static constexpr int TMEM_COLS = 2 * BN;  // power of two for BN in {64, 128, 256}
+  static constexpr int THREADS = 192;
+  static constexpr size_t SMEM = (size_t)STAGES * STAGE + 1024 /* alignment slack */ + 256 /* barriers */;
+  static_assert(BN == 64 || BN == 128 || BN == 256, "N tile");
+  static_assert(STAGES >= 2, "ring depth");
+};
+
+template <int BN>
+__global__ void __launch_bounds__(192, 1)
+    mix_umma_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                    const MixUmmaArgs a) {
+  using C = MixCfg<BN>;
+  extern __shared__ __align__(1024) uint8_t mix_smem_raw[];
+  // operand tiles need 1024-byte alignment (128-byte swizzle atoms)
+  const uint32_t raw = smem_u32(mix_smem_raw);
+  uint8_t* sm = mix_smem_raw + ((1024u - (raw & 1023u)) & 1023u);
+  uint64_t* full = reinterpret_cast<uint64_t*>(sm + (size_t)C::STAGES * C::STAGE);
+  uint64_t* empty = full + C::STAGES;
+  uint64_t* tfull = empty + C::STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* done = tempty + 2;
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(done + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&tfull[i], 1);
+      mbar_init(&tempty[i], 4);  // one arrive per epilogue warp
+    }
+    mbar_init(done, 1);
+    fence_mbar_init();
+    umma::prefetch_tmap(&tmA);
+    umma::prefetch_tmap(&tmB);
+  }
+  if (warp == 1) umma::tmem_alloc(tslot, C::TMEM_COLS);
+  umma::tc_fence_before();
+  __syncthreads();
+  umma::tc_fence_after();
+  const uint32_t tbase = *tslot;
+
+  const int ntiles_total = 2 * a.mtiles * a.ntiles;
+  const int kblocks = a.d / C::BK;
+  auto decode = [&](int t, int& which, int& mt, int& nt) {
+    nt = t % a.ntiles;
+    const int rest = t / a.ntiles;
+    mt = rest % a.mtiles;
+    which = rest / a.mtiles;
+  };
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int s = 0;
+      uint32_t ph = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < ntiles_total && ok; t += gridDim.x) {
+        int which, mt, nt;
+        decode(t, which, mt, nt);
+        const int arow = which * a.B + mt * C::BM;
+        const int brow = which * a.d + nt * BN;
+        for (int kb = 0; kb < kblocks && ok; ++kb) {
+          ok = umma::mbar_wait_spin(&empty[s], ph ^ 1u);
+          if (!ok) break;
+          mbar_arrive_expect_tx(&full[s], C::STAGE);
+          uint8_t* st = sm + (size_t)s * C::STAGE;
+          const int k = kb * C::BK;
+          umma::tma_load_2d(st, &tmA, &full[s], k, arow);                           // c0
+          umma::tma_load_2d(st + C::A_BYTES, &tmA, &full[s], 2 * a.d + k, arow);     // c1
+          umma::tma_load_3d(st + 2 * C::A_BYTES, &tmB, &full[s], k, brow, a.layer);  // w0
+          umma::tma_load_3d(st + 2 * C::A_BYTES + C::B_BYTES, &tmB, &full[s], a.d + k, brow,
+                            a.layer);                                                // w1
+          if (++s == C::STAGES) {
+            s = 0;
+            ph ^= 1u;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = umma::idesc_f16_f32(C::BM, BN);
+      int s = 0;
+      uint32_t ph = 0;
+      int it = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < ntiles_total && ok; t += gridDim.x, ++it) {
+        const int buf = it & 1;
+        const uint32_t use = (uint32_t)(it >> 1);
+        ok = umma::mbar_wait_spin(&tempty[buf], (use & 1u) ^ 1u);
+        umma::tc_fence_after();
+        const uint32_t dt = tbase + (uint32_t)(buf * BN);
+        for (int kb = 0; kb < kblocks && ok; ++kb) {
+          ok = umma::mbar_wait_spin(&full[s], ph);
+          if (!ok) break;
+          umma::tc_fence_after();
+          const uint32_t st = smem_u32(sm + (size_t)s * C::STAGE);
+          const uint32_t a0 = st, a1 = st + C::A_BYTES;
+          const uint32_t b0 = st + 2 * C::A_BYTES, b1 = b0 + C::B_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < C::BK / 16; ++kk) {
+            const uint32_t off = (uint32_t)kk * 32u;  // 16 fp16 along K
+            umma::mma_f16(dt, umma::desc_sw128(a0 + off), umma::desc_sw128(b0 + off), idesc,
+                          (kb | kk) != 0);
+            umma::mma_f16(dt, umma::desc_sw128(a0 + off), umma::desc_sw128(b1 + off), idesc, 1u);
+            umma::mma_f16(dt, umma::desc_sw128(a1 + off), umma::desc_sw128(b0 + off), idesc, 1u);
+          }
+          umma::mma_commit(&empty[s]);
+          if (++s == C::STAGES) {
+            s = 0;
+            ph ^= 1u;
+          }
+        }
+        umma::mma_commit(&tfull[buf]);
+      }
+      // every MMA issued has completed before the accumulator columns are
+      // freed: one more commit, waited for (bounded)
+      umma::mma_commit(done);
+      umma::mbar_wait_spin(done, 0);
+    }
+  } else {
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const int r = 32 * q + lane;
+    const float alpha = *a.alpha;
+    int it = 0;
+    for (int t = blockIdx.x; t < ntiles_total; t += gridDim.x, ++it) {
+      int which, mt, nt;
+      decode(t, which, mt, nt);
+      const int buf = it & 1;
+      const uint32_t use = (uint32_t)(it >> 1);
+      // all lanes wait, so the warp leaves together if the wait gives up
+      if (!umma::mbar_wait_sleep(&tfull[buf], use & 1u)) break;
+      umma::tc_fence_after();
+      const int b = mt * C::BM + r;
+      float* zr = a.z + ((long long)which * a.B + b) * a.d + nt * BN;
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        float v[32];
+        umma::tmem_ld32(tbase + ((uint32_t)(32 * q) << 16) + (uint32_t)(buf * BN + c * 32), v);
+        if (b < a.B) {
+          float4* dst = reinterpret_cast<float4*>(zr + c * 32);
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            dst[j] = make_float4(v[4 * j] * alpha, v[4 * j + 1] * alpha, v[4 * j + 2] * alpha,
+                                 v[4 * j + 3] * alpha);
+        }
+      }
+      umma::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) umma::mbar_arrive(&tempty[buf]);
+    }
+  }
+  umma::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    umma::tc_fence_after();
+    umma::tmem_dealloc(tbase, C::TMEM_COLS);
+  }
+}
+
+}  // namespace gfn

@@ -201,13 +201,14 @@ def leapfrog_layered_sequence(x0, v0, packed, meta, base_dt, forces=None, ids=No
     return x_seq, v_seq, x_f, v_f
 
 
-MIX_SPLIT_BF16, MIX_FP32_SIMT, MIX_SPLIT_F16 = 0, 1, 2
+MIX_SPLIT_BF16, MIX_FP32_SIMT, MIX_SPLIT_F16, MIX_UMMA_F16 = 0, 1, 2, 3
 
 
 def set_layered_mixing(mode):
-    """Mixing-GEMM arithmetic of the layered path: MIX_SPLIT_F16 (default;
-    two-piece fp16 split on the tensor cores, K = 3 dim, activations below
-    2^15), MIX_SPLIT_BF16 (three-piece bf16 split, K = 6 dim, full fp32 range)
+    """Mixing-GEMM arithmetic of the layered path: MIX_UMMA_F16 (default; the
+    two-piece fp16 split computed by the library's own tcgen05 kernel, three
+    MMAs per K step), MIX_SPLIT_F16 (the same split as one cuBLAS GEMM,
+    K = 3 dim; both need activations below 2^15), MIX_SPLIT_BF16 (three-piece bf16 split, K = 6 dim, full fp32 range)
     or MIX_FP32_SIMT (fp32 SGEMM).  Returns the previous mode."""
     prev = _lib.load().gfn_leapfrog_layered_set_mixing(int(mode))
     if prev < 0:

@@ -281,11 +281,11 @@ def test_errors_are_loud():
     assert ops.device_error(reset=True) == 0
 
 
-@pytest.fixture(params=["split_bf16", "fp32_simt", "split_f16"])
+@pytest.fixture(params=["umma_f16", "split_bf16", "fp32_simt", "split_f16"])
 def mixing(request):
     from manifold_b200.cuda import ops
     mode = {"split_bf16": ops.MIX_SPLIT_BF16, "fp32_simt": ops.MIX_FP32_SIMT,
-            "split_f16": ops.MIX_SPLIT_F16}[request.param]
+            "split_f16": ops.MIX_SPLIT_F16, "umma_f16": ops.MIX_UMMA_F16}[request.param]
     prev = ops.set_layered_mixing(mode)
     yield request.param
     ops.set_layered_mixing(prev)
