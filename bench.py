@@ -1,15 +1,16 @@
-"""Recurrent tokens/sec of the fused leapfrog recurrence on B200.
+"""Recurrent tokens/sec of the leapfrog recurrence on B200.
 
-Default workload (N=1): the long-horizon configuration -- parity bit tokens,
-d=256, 6 layers, 8 heads, rank 32 (per-head 4), leapfrog dt=0.1, batch 64
-per GPU, the 100,000-token stream processed in chunks with the O(1) (x, v)
-state carried between chunks.  One step = one chunk of --chunk tokens for
-all 64 rows through all 6 layers (one kernel launch).  Weights are seeded
-random (U, W ~ N(0, 0.2^2) etc.); data is synthetic.
+Default workload (N=1): the batched-decode configuration C4 -- 4,096
+independent streams, d=1024, 24 layers, 16 heads, rank 64 (per-head 4),
+leapfrog dt=0.1, uniform token ids over 32,000, persistent (x, v) state; one
+step = one decode token for every stream through all 24 layers.  Weights are
+seeded random (U, W ~ N(0, 0.2^2) etc.); data is synthetic.
 
-Multi-GPU (torchrun): every rank runs its own 64 independent streams (weak
-scaling by batch sharding, no collective on the path); time is the max over
-ranks of the device time.
+Multi-GPU (torchrun): C4 shards its 4,096 streams over the ranks (strong
+scaling: 4096 / N per GPU); the other configs give every rank its own batch
+(weak scaling).  Rows are independent: no collective on the path, except the
+gradient all-reduce of the training config C5.  Time is the max over ranks
+of the device time.
 
 --impl reference times the CPU baseline: the numpy restatement of the
 reference's algorithm (oracle/), all host threads, on the same config.
@@ -33,8 +34,14 @@ CONFIGS = {
                workload="C2 long-horizon recurrence fp32: d=256, 6 layers, 8 heads, rank 32, "
                         "leapfrog, batch 64, 100k-token stream in chunks"),
     "c4": dict(V=32000, d=1024, NL=24, H=16, rank=64, B=4096, dt=0.1, chunk=1, parity=False,
-               workload="C4 batched decode fp32: 4096 streams, d=1024, 24 layers, 16 heads, "
-                        "rank 64, one token per step"),
+               strong=True,
+               workload="C4 batched decode fp32: 4096 streams sharded over the GPUs, d=1024, "
+                        "24 layers, 16 heads, rank 64, one token per step"),
+    "c3_scan": dict(V=50257, d=512, NL=12, H=8, rank=32, B=256, dt=0.1, chunk=2048, functional=True,
+                    scan=True,
+                    workload="C3 LM prefill through the parallel-scan path (use_scan=True: "
+                             "ParallelMLayer x 12, d=512, 8 heads), functional-embedding forces, "
+                             "batch 256, L=2048"),
     "c3": dict(V=50257, d=512, NL=12, H=8, rank=32, B=256, dt=0.1, chunk=64, functional=True,
                workload="C3 LM prefill: bf16 functional-embedding forces, fp32 state, d=512, "
                         "12 layers, 8 heads, batch 256"),
@@ -55,6 +62,16 @@ def flops_per_token(c):
     # + 2 Gamma evaluations (2 * 2*hd*r MAC per head) + ~30 elementwise flops per element
     mac = 2 * d * d + H * (2 * hd * hd + 4 * hd * r)
     return c["NL"] * (2 * mac + 30 * d)
+
+
+def rank_batch(c, world):
+    """Rows per rank: C4's streams are a fixed total sharded over the ranks
+    (strong scaling); every other config gives each rank its own batch."""
+    if c.get("strong"):
+        if c["B"] % world:
+            raise SystemExit(f"{c['B']} streams do not shard evenly over {world} GPUs")
+        return c["B"] // world
+    return c["B"]
 
 
 def dist_env():
@@ -257,7 +274,7 @@ def run_ours(args, c):
     dev = torch.device("cuda", local)
     from manifold_b200.cuda import ops
     m, P = make_model(c, dev)
-    B, T = c["B"], args.chunk or c["chunk"]
+    B, T = rank_batch(c, world), args.chunk or c["chunk"]
     steps, warm = args.steps, args.warmup
     ids_host = [torch.from_numpy(make_ids(c, B, T, 100 * rank + i)).pin_memory()
                 for i in range(steps + warm)]
@@ -268,7 +285,7 @@ def run_ours(args, c):
         m.recurrence_path = args.path
     if args.mixing != "default":
         ops.set_layered_mixing({"split_bf16": ops.MIX_SPLIT_BF16, "split_f16": ops.MIX_SPLIT_F16,
-                                "fp32": ops.MIX_FP32_SIMT}[args.mixing])
+                                "fp32": ops.MIX_FP32_SIMT, "umma_f16": ops.MIX_UMMA_F16}[args.mixing])
     layered = m._use_layered(B)
     packed, meta = m._pack.get(list(m.layers), layered=layered)
     seqfn = ops.leapfrog_layered_sequence if layered else ops.leapfrog_sequence
@@ -343,6 +360,9 @@ def run_ours(args, c):
     torch.cuda.synchronize(dev)
     e2e_ms = e0.elapsed_time(e1)
     clocks = sampler.stop() if sampler else None
+    # per-kernel CUDA-event timing of the layered path (a second timed pass with
+    # events recorded around every head-step and mixing launch on their stream)
+    ktime = layered_kernel_times(step, warm, state, steps, flush, dev) if layered else None
     if world > 1:
         t = torch.tensor([ms, e2e_ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -374,7 +394,7 @@ def run_ours(args, c):
             "warmup": warm,
             "ms_per_step": round(ms / steps, 4),
             "higher_is_better": True,
-            "scaling": "weak",
+            "scaling": "strong" if c.get("strong") else "weak",
             "vs_baseline": None,
             "dtype": "f32",
             "data": "synthetic (seeded parity bits / ids; seeded random weights)",
@@ -384,17 +404,143 @@ def run_ours(args, c):
                        "plan": plan},
             "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s",
                     "h2d_bytes_per_step": int(B * T * 8), "d2h_bytes_per_step": int(2 * B * c["d"] * 4)},
-            "gpu_launches": steps * ((2 * c["NL"] + 1) * T if layered else 1)
+            "gpu_launches": steps * ((2 * c["NL"] + 2) * T if layered else 1)
             + (steps if c.get("functional") else 0),
             "recurrence_path": "layered (head-step kernel + split-precision tensor-core mixing GEMM per layer)"
             if layered else "fused persistent cluster kernel",
             "roofline": roofline_entry(c, layered, achieved, hbm, bf16, peak_kind, fl, step_ms, T,
-                                       latency),
+                                       latency, ktime, B),
             "clocks": clocks,
             "wall_s_timed": round(wall, 3),
         }
         if not args.no_cpu_baseline and world == 1:
             result["cpu_baseline"] = cpu_baseline(c, args.cpu_tokens)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return result
+
+
+def run_scan(args, c):
+    """C3 through the parallel-scan path (use_scan=True): one step = the 12
+    ParallelMLayers over one [B, L] batch of functional-embedding forces
+    (LayerNorm + the three d x d projections as one GEMM + the fused
+    sigmoid/softplus/two-scan kernel per layer)."""
+    import torch
+    import torch.distributed as dist
+    import manifold_b200 as gfn
+    from manifold_b200.cuda import ops
+    from tests.golden import cases as C
+    world, rank, local = dist_env()
+    if world > 1:
+        dist.init_process_group("nccl")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    torch.manual_seed(0)
+    kw = dict(C.model_kwargs(dict(c, seed=1234)), use_scan=True)
+    m = gfn.Manifold(**kw).to(dev).eval()
+    B, T, d = c["B"], args.chunk or c["chunk"], c["d"]
+    steps, warm = args.steps, args.warmup
+    ids_host = [torch.from_numpy(make_ids(c, B, T, 100 * rank + i)).pin_memory() for i in range(steps + warm)]
+    ids_dev = [t.to(dev) for t in ids_host]
+    flush = torch.empty(256 * 1024 * 1024 // 4, device=dev, dtype=torch.float32)
+    stream = torch.cuda.current_stream(dev)
+
+    def layers(forces):
+        cur = forces
+        for layer in m.layers:
+            cur, _, _, _ = layer(None, None, force=cur)
+        return cur
+
+    def step(i):
+        with torch.no_grad():
+            return layers(m.embedding(ids_dev[i]))
+
+    for i in range(warm):
+        step(i)
+    torch.cuda.synchronize(dev)
+    sampler = ClockSampler(local) if rank == 0 else None
+    if sampler:
+        sampler.start()
+        time.sleep(0.3)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    for i in range(steps):
+        flush.zero_()
+        ev[i][0].record(stream)
+        step(warm + i)
+        ev[i][1].record(stream)
+    torch.cuda.synchronize(dev)
+    ms = sum(a.elapsed_time(b) for a, b in ev)
+    # end to end: ids from pinned host memory, the layers, the last position's
+    # state read back to the host
+    hx = torch.empty(B, d, dtype=torch.float32).pin_memory()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(steps):
+        with torch.no_grad():
+            out = layers(m.embedding(ids_host[warm + i].to(dev, non_blocking=True)))
+        hx.copy_(out[:, -1], non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    e2e_ms = e0.elapsed_time(e1)
+    # the fused layer-scan kernel alone, per launch (CUDA events on its stream)
+    layer = m.layers[0]
+    with torch.no_grad():
+        f = layer.norm_x(m.embedding(ids_dev[0]))
+        Wcat = torch.cat([layer.to_A[0].weight, layer.to_dt[0].weight, layer.to_B.weight], 0)
+        bcat = torch.cat([layer.to_A[0].bias, layer.to_dt[0].bias, layer.to_B.bias], 0)
+        z = torch.nn.functional.linear(f, Wcat, bcat)
+        ks = []
+        for i in range(max(3, steps)):
+            flush.zero_()
+            k0, k1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            k0.record(stream)
+            ops.parallel_layer_scan(z, layer.heads, layer.base_dt)
+            k1.record(stream)
+            ks.append((k0, k1))
+        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        g0.record(stream)
+        for i in range(steps):
+            torch.nn.functional.linear(layer.norm_x(f), Wcat, bcat)
+        g1.record(stream)
+    torch.cuda.synchronize(dev)
+    scan_us = sum(a.elapsed_time(b) for a, b in ks) * 1e3 / len(ks)
+    proj_us = g0.elapsed_time(g1) * 1e3 / steps
+    clocks = sampler.stop() if sampler else None
+    if world > 1:
+        t = torch.tensor([ms, e2e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, e2e_ms = t.tolist()
+    result = None
+    if rank == 0:
+        hbm, bf16, peak_kind = measured_peaks()
+        tokens = world * B * T * steps
+        scan_bytes = 20.0 * B * T * d  # read z [B, L, 3d], write x_seq, v_seq
+        scan_gbs = scan_bytes / (scan_us * 1e-6) / 1e9
+        proj_tf = 2.0 * B * T * d * 3 * d / (proj_us * 1e-6) / 1e12
+        result = {
+            "metric": "recurrent tokens/sec (prefill+decode)", "value": round(tokens / (ms / 1e3), 1),
+            "unit": "tokens/s", "n_gpus": world, "steps": steps, "warmup": warm,
+            "ms_per_step": round(ms / steps, 3), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded Zipf ids; seeded random weights)",
+            "config": {"workload": c["workload"], "batch_per_gpu": B, "tokens_per_step": T, "dim": d,
+                       "layers": c["NL"], "heads": c["H"], "l2": "flushed (256 MB write) between timed steps"},
+            "e2e": {"value": round(tokens / (e2e_ms / 1e3), 1), "unit": "tokens/s",
+                    "h2d_bytes_per_step": int(B * T * 8), "d2h_bytes_per_step": int(B * d * 4)},
+            "gpu_launches": steps * (1 + c["NL"]),
+            "recurrence_path": "parallel scan (ParallelMLayer: LayerNorm + projection GEMM + fused scan kernel)",
+            "roofline": {"bound": "hbm", "kernel": "parallel_layer_scan_kernel", "achieved": round(scan_gbs, 1),
+                         "peak": hbm, "unit": "GB/s", "frac": round(scan_gbs / hbm, 4),
+                         "traffic": TRAFFIC.get((c.get("name"), "scan")), "peak_source": peak_kind,
+                         "launch_us": round(scan_us, 2),
+                         "algorithmic_bytes_per_launch": scan_bytes,
+                         "projections": {"launch_us": round(proj_us, 2), "tflops": round(proj_tf, 1),
+                                         "note": "LayerNorm + [B*L, d] x [d, 3d] fp32 GEMM (torch)"}},
+            "clocks": clocks,
+        }
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -427,31 +573,82 @@ def latency_floor(dev, rank, clusters, layer_step_ns, steps=20000):
             "source": "gfn_debug_latency_probe (dependent chain of one layer step, no weight traffic)"}
 
 
-def roofline_entry(c, layered, achieved_gbs, hbm, bf16, peak_kind, fp32_tflops, step_ms, T, latency):
-    """Roofline of the recurrence.  Layered path: tensor-bound mixing GEMMs
-    (split-bf16, K = 6d: 2 * 2 * B * 6d * d FLOP per layer and token) over
-    the whole step against the measured bf16 peak.  Fused path: algorithmic
-    HBM bytes against the measured copy bandwidth (tiny by construction: the
-    chain is latency-bound) plus the latency roof from the probe kernel."""
-    if layered:
-        from manifold_b200.cuda import ops
-        mode = ops.get_layered_mixing()
-        split = {ops.MIX_SPLIT_BF16: 6, ops.MIX_SPLIT_F16: 3}.get(mode)
-        if split is None:  # fp32 SGEMM: no tensor work
-            return {"bound": "hbm", "achieved": round(achieved_gbs, 2), "peak": hbm, "unit": "GB/s",
-                    "frac": round(achieved_gbs / hbm, 5), "traffic": None, "peak_source": peak_kind,
-                    "fp32_tflops": round(fp32_tflops, 3)}
-        fl = 2.0 * 2 * c["B"] * split * c["d"] * c["d"] * c["NL"] * T
-        tf = fl / (step_ms / 1e3) / 1e12
-        kind = "split-fp16, K = 3d" if split == 3 else "split-bf16, K = 6d"
-        return {"bound": "tensor", "achieved": round(tf, 1), "peak": bf16, "unit": "TFLOP/s",
-                "frac": round(tf / bf16, 4), "traffic": None, "peak_source": peak_kind,
-                "note": f"mixing GEMM tensor FLOPs ({kind}) over the whole step time "
-                        "(head-step kernels included; fp16 and bf16 tensor rates are equal); "
-                        "fp32-equivalent FLOP rate in fp32_tflops",
-                "fp32_tflops": round(fp32_tflops, 3)}
+def layered_kernel_times(step, i0, state, steps, flush, dev):
+    """Average device time per launch of the layered path's head-step and
+    mixing kernels: CUDA events recorded by the library around each launch,
+    on the launching stream, over `steps` steps (L2 flushed between steps)."""
+    import ctypes
+    import torch
+    from manifold_b200 import _lib
+    _lib.call("gfn_debug_layered_timing", 1)
+    try:
+        for i in range(steps):
+            flush.zero_()
+            state = step(i0 + i, state)
+        torch.cuda.synchronize(dev)
+        hm, mm, n = ctypes.c_double(), ctypes.c_double(), ctypes.c_int()
+        _lib.call("gfn_debug_layered_timing_read", ctypes.addressof(hm), ctypes.addressof(mm),
+                  ctypes.addressof(n))
+    finally:
+        _lib.call("gfn_debug_layered_timing", 0)
+    n = max(1, n.value)
+    return dict(head_us=hm.value * 1e3 / n, mix_us=mm.value * 1e3 / n, launches=n)
+
+
+# DRAM bytes (read + write) per launch of the dominant kernels, from one ncu
+# capture each (dram__bytes_read.sum + dram__bytes_write.sum; the commands and
+# figures are in profiles/*.md).  Keyed by (config, kernel).
+TRAFFIC = {}
+
+
+def roofline_entry(c, layered, achieved_gbs, hbm, bf16, peak_kind, fp32_tflops, step_ms, T, latency,
+                   ktime=None, B=None):
+    """Roofline of the recurrence.
+
+    Layered path: the dominant kernel of the step, timed per launch with CUDA
+    events.  Mixing GEMM: algorithmic FLOPs = the fp32 product 2 * 2 * B * d^2
+    per launch (x and v; the split-fp16 scheme issues three times this on the
+    tensor pipe) against the measured bf16 peak.  Head step: algorithmic
+    bytes = read x, v, force + write x', v' (20 B per element of [B, d]) against
+    the measured copy bandwidth.  Fused path: algorithmic HBM bytes of the
+    launch against the copy bandwidth (tiny by construction: the chain is
+    latency-bound) plus the latency roof from the probe kernel."""
+    if layered and ktime:
+        d = c["d"]
+        mix_fl = 2.0 * 2 * B * d * d
+        head_bytes = 20.0 * B * d
+        mix_tf = mix_fl / (ktime["mix_us"] * 1e-6) / 1e12
+        head_gbs = head_bytes / (ktime["head_us"] * 1e-6) / 1e9
+        step_tf = flops_per_token(c) * B * T / (step_ms / 1e3) / 1e12
+        kernels = {
+            "mixing_gemm": {"kernel": "mix_umma_kernel (tcgen05, split-fp16)", "launch_us": round(ktime["mix_us"], 2),
+                            "algorithmic_flop_per_launch": mix_fl, "achieved_tflops": round(mix_tf, 1),
+                            "frac_of_bf16_peak": round(mix_tf / bf16, 4),
+                            "tensor_pipe_tflops": round(3 * mix_tf, 1),
+                            "traffic": TRAFFIC.get((c.get("name"), "mix"))},
+            "head_step": {"kernel": "layered_head_umma_kernel / layered_pre_kernel",
+                          "launch_us": round(ktime["head_us"], 2),
+                          "algorithmic_bytes_per_launch": head_bytes, "achieved_gbs": round(head_gbs, 1),
+                          "frac_of_hbm": round(head_gbs / hbm, 4),
+                          "traffic": TRAFFIC.get((c.get("name"), "head"))},
+        }
+        if ktime["mix_us"] >= ktime["head_us"]:
+            k = kernels["mixing_gemm"]
+            top = {"bound": "tensor", "kernel": "mixing_gemm", "achieved": k["achieved_tflops"], "peak": bf16,
+                   "unit": "TFLOP/s", "frac": k["frac_of_bf16_peak"], "traffic": k["traffic"]}
+        else:
+            k = kernels["head_step"]
+            top = {"bound": "hbm", "kernel": "head_step", "achieved": k["achieved_gbs"], "peak": hbm,
+                   "unit": "GB/s", "frac": k["frac_of_hbm"], "traffic": k["traffic"]}
+        top.update({"peak_source": peak_kind, "kernels": kernels, "layer_steps_timed": ktime["launches"],
+                    "step": {"algorithmic_fp32_tflops": round(step_tf, 2),
+                             "frac_of_bf16_peak": round(step_tf / bf16, 4),
+                             "note": "all algorithmic fp32 FLOPs of the step (mixing, friction, Gamma, "
+                                     "elementwise) over the whole step time"}})
+        return top
     return {"bound": "hbm", "achieved": round(achieved_gbs, 2), "peak": hbm, "unit": "GB/s",
-            "frac": round(achieved_gbs / hbm, 5), "traffic": None, "peak_source": peak_kind,
+            "frac": round(achieved_gbs / hbm, 5), "traffic": TRAFFIC.get((c.get("name"), "seq")),
+            "peak_source": peak_kind,
             "note": "dependent chain: HBM is not the binding roof; see latency",
             "fp32_tflops": round(fp32_tflops, 3), "latency": latency}
 
@@ -528,22 +725,23 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--config", default="c2", choices=sorted(CONFIGS))
+    ap.add_argument("--config", default="c4", choices=sorted(CONFIGS))
     ap.add_argument("--chunk", type=int, default=0, help="tokens per step (default per config)")
     ap.add_argument("--cpu-tokens", type=int, default=0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--path", default="auto", choices=["auto", "fused", "layered"],
                     help="recurrence path (auto: by batch size)")
-    ap.add_argument("--mixing", default="default", choices=["default", "split_bf16", "split_f16", "fp32"],
+    ap.add_argument("--mixing", default="default", choices=["default", "umma_f16", "split_bf16", "split_f16", "fp32"],
                     help="layered path's mixing GEMM arithmetic (default: the library's)")
     ap.add_argument("--phase-profile", action="store_true",
                     help="print per-phase cycle counts of CTA 0 for one step instead")
     args = ap.parse_args()
-    c = CONFIGS[args.config]
+    c = dict(CONFIGS[args.config], name=args.config)
     if args.impl == "reference":
         out = run_reference(args, c)
     else:
-        out = run_train(args, c) if c.get("train") else run_ours(args, c)
+        out = run_train(args, c) if c.get("train") else run_scan(args, c) if c.get("scan") \
+            else run_ours(args, c)
     if out is not None:
         print(json.dumps(out), flush=True)
 

@@ -252,6 +252,21 @@ int gfn_leapfrog_layered_forward(const float* x_init, const float* v_init,
                                  gfn_stream_t stream);
 
 /* ------------------------------------------------------------------------
+ * Measurement: per-kernel timing of the layered path.  While enabled (enable
+ * = 1 also clears earlier records), every layer step of
+ * gfn_leapfrog_layered_forward brackets its head-step and mixing-GEMM
+ * launches with CUDA events on the launch stream; _read synchronises them
+ * and returns the summed milliseconds of each kernel and the number of
+ * layer steps recorded.  Not for production calls (events cost launches). */
+int gfn_debug_layered_timing(int enable);
+/* Measurement: while `device_stamps` is non-NULL, every launch of the
+ * tensor-core head-step kernel writes global-timer stamps of its phases to
+ * device_stamps[cta * 8 + phase] (cta = head * row_tiles + row_tile), each
+ * launch overwriting the last. */
+int gfn_debug_head_profile(long long* device_stamps);
+int gfn_debug_layered_timing_read(double* head_ms, double* mix_ms, int* layer_steps);
+
+/* ------------------------------------------------------------------------
  * Measurement: cycles of `steps` iterations of the layer-step latency floor
  * (the fused recurrence's dependent chain with no weight traffic: Gamma and
  * friction reductions, the kick arithmetic, the concat and RMSNorm cluster

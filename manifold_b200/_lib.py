@@ -48,6 +48,9 @@ _SIGS = {
                                   _p],
     "gfn_leapfrog_layered_workspace_floats": [_i, _i],
     "gfn_leapfrog_layered_set_mixing": [_i],
+    "gfn_debug_layered_timing": [_i],
+    "gfn_debug_head_profile": [_p],
+    "gfn_debug_layered_timing_read": [_p, _p, _p],
     "gfn_leapfrog_layered_forward": [_p, _p, _ll, _p, _p, _p, _p, _ll, _p, _p, _ll, _i, _i, _i, _i,
                                      _i, _i, _f, _p, _p, _p, _p, _p, _ll, _p],
     "gfn_split_f16": [_p, _ll, _ll, _i, _i, _p, _p, _p],

@@ -1,6 +1,8 @@
 // Layered recurrence (large batches): the C ABI of the head-step kernels
 // (layered.cuh) around a batched cuBLAS mixing GEMM per layer.
 #include <atomic>
+#include <vector>
+#include <cstdio>
 #include <cstdlib>
 #include <mutex>
 
@@ -9,6 +11,7 @@
 
 #include "abi.h"
 #include "layered.cuh"
+#include "head_umma.cuh"
 #include "mix_umma.cuh"
 
 using namespace gfn;
@@ -59,77 +62,173 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
   return fn;
 }
 
-// fp16 tensor map with a 64-element (128-byte) inner box and 128-byte swizzle.
-int encode_f16_map(CUtensorMap* m, const void* base, int rank, const cuuint64_t* dims,
-                   const cuuint64_t* strides_bytes, const cuuint32_t* box) {
+// fp16 tensor map whose inner box (box[0] elements, 64 or 128 bytes) is the
+// swizzle span.
+int encode_map(CUtensorMap* m, CUtensorMapDataType dt, int esize, const void* base, int rank,
+               const cuuint64_t* dims, const cuuint64_t* strides_bytes, const cuuint32_t* box) {
   PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
   if (!enc) return fail(GFN_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
   cuuint32_t estr[3] = {1, 1, 1};
-  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, (cuuint32_t)rank, const_cast<void*>(base), dims,
-                   strides_bytes, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+  CUresult r = enc(m, dt, (cuuint32_t)rank, const_cast<void*>(base), dims,
+                   strides_bytes, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   box[0] * esize == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(GFN_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
   return GFN_OK;
 }
 
-// Column tile of the UMMA mixing GEMM: 256 when that gives at least one
-// tile per SM, else narrower tiles (small batches), never wider than d.
-int pick_mix_bn(int batch, int dim, int sms) {
-  if (const char* env = getenv("GFN_MIX_BN")) {  // tuning override
-    const int t = atoi(env);
-    if ((t == 64 || t == 128 || t == 256) && dim % t == 0) return t;
+int encode_f16_map(CUtensorMap* m, const void* base, int rank, const cuuint64_t* dims,
+                   const cuuint64_t* strides_bytes, const cuuint32_t* box) {
+  return encode_map(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, base, rank, dims, strides_bytes, box);
+}
+
+// Tile of the UMMA mixing GEMM.  256 x 256 tiles (K blocks of 32, three ring
+// stages) read the fewest operand bytes per FLOP: used when they still give
+// most SMs a tile.  Smaller problems use 128-row tiles and the widest column
+// tile that gives every SM work (K blocks of 64).
+struct MixShape { int bn, bk, mh; };
+
+MixShape pick_mix_shape(int batch, int dim, int sms) {
+  MixShape m{64, 64, 1};
+  const long long mt1 = (batch + 127) / 128, mt2 = (batch + 255) / 256;
+  if (dim % 256 == 0 && 2 * mt2 * (dim / 256) >= (sms * 3) / 4) m = {256, 32, 2};
+  else if (dim % 256 == 0 && 2 * mt1 * (dim / 256) >= sms) m = {256, 64, 1};
+  else if (dim % 128 == 0 && 2 * mt1 * (dim / 128) >= sms) m = {128, 64, 1};
+  if (const char* env = getenv("GFN_MIX_TILE")) {  // tuning override "BN,BK,MH"
+    int bn, bk, mh;
+    if (sscanf(env, "%d,%d,%d", &bn, &bk, &mh) == 3 && (bn == 64 || bn == 128 || bn == 256) &&
+        (bk == 32 || bk == 64) && (mh == 1 || mh == 2) && dim % bn == 0)
+      m = {bn, bk, mh};
   }
-  const long long mt = (batch + 127) / 128;
-  for (int bn = 256; bn > 64; bn >>= 1)
-    if (dim % bn == 0 && 2 * mt * (dim / bn) >= sms) return bn;
-  return 64;
+  return m;
 }
 
 struct MixUmmaPlan {
   CUtensorMap ta, tb;
   size_t smem;
-  int bn, grid;
+  int bn, bk, mh, grid, threads;
 };
 
-template <int BN>
-int mix_plan_for(MixUmmaPlan* p, int sms, int mtiles, int d) {
-  p->smem = MixCfg<BN>::SMEM;
-  p->bn = BN;
-  const int tiles = 2 * mtiles * (d / BN);
+template <int BN, int BK, int MH>
+int mix_plan_for(MixUmmaPlan* p, int sms, int batch, int d) {
+  using C = MixCfg<BN, BK, MH>;
+  p->smem = C::SMEM;
+  p->threads = C::THREADS;
+  const int tiles = 2 * ((batch + C::BM - 1) / C::BM) * (d / BN);
   p->grid = tiles < sms ? tiles : sms;
-  cudaError_t e = cudaFuncSetAttribute(mix_umma_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)p->smem);
+  cudaError_t e = cudaFuncSetAttribute(mix_umma_kernel<BN, BK, MH>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p->smem);
   return e == cudaSuccess ? GFN_OK : cuda_status(e, "mixing GEMM: shared memory attribute");
 }
+
+#define GFN_MIX_SHAPES(X) X(256, 32, 2) X(256, 32, 1) X(256, 64, 1) X(128, 32, 1) X(128, 64, 1) \
+  X(128, 32, 2) X(64, 32, 1) X(64, 64, 1) X(64, 32, 2) X(64, 64, 2)
 
 // Tensor maps of one forward call: activations catkh [2B][3d] and the packed
 // split weights WH of every layer, [NL][2d][3d] with the pack's layer stride.
 int make_mix_plan(MixUmmaPlan* p, const __half* catkh, const float* packed, const LayOffsets& lo,
                   int batch, int dim, int num_layers, int sms) {
-  const int bn = pick_mix_bn(batch, dim, sms);
-  const int mtiles = (batch + 127) / 128;
-  int st = bn == 256 ? mix_plan_for<256>(p, sms, mtiles, dim)
-         : bn == 128 ? mix_plan_for<128>(p, sms, mtiles, dim)
-                     : mix_plan_for<64>(p, sms, mtiles, dim);
-  if (st) return st;
+  const MixShape sh = pick_mix_shape(batch, dim, sms);
+  p->bn = sh.bn;
+  p->bk = sh.bk;
+  p->mh = sh.mh;
+  int st = GFN_ERR_UNSUPPORTED;
+#define GFN_MIX_PLAN(BN, BK, MH) \
+  if (sh.bn == BN && sh.bk == BK && sh.mh == MH) st = mix_plan_for<BN, BK, MH>(p, sms, batch, dim);
+  GFN_MIX_SHAPES(GFN_MIX_PLAN)
+#undef GFN_MIX_PLAN
+  if (st) return st == GFN_ERR_UNSUPPORTED ? fail(st, "mixing GEMM: no kernel for the tile") : st;
   const cuuint64_t adims[2] = {(cuuint64_t)3 * dim, (cuuint64_t)2 * batch};
   const cuuint64_t astr[1] = {(cuuint64_t)6 * dim};
-  const cuuint32_t abox[2] = {64, 128};
+  const cuuint32_t abox[2] = {(cuuint32_t)sh.bk, (cuuint32_t)(128 * sh.mh)};
   st = encode_f16_map(&p->ta, catkh, 2, adims, astr, abox);
   if (st) return st;
   const cuuint64_t bdims[3] = {(cuuint64_t)3 * dim, (cuuint64_t)2 * dim, (cuuint64_t)num_layers};
   const cuuint64_t bstr[2] = {(cuuint64_t)6 * dim, (cuuint64_t)lo.total * 4};
-  const cuuint32_t bbox[3] = {64, (cuuint32_t)bn, 1};
+  const cuuint32_t bbox[3] = {(cuuint32_t)sh.bk, (cuuint32_t)sh.bn, 1};
   return encode_f16_map(&p->tb, packed + lo.WH, 3, bdims, bstr, bbox);
 }
 
 void launch_mix(const MixUmmaPlan& p, const MixUmmaArgs& ma, cudaStream_t s) {
-  if (p.bn == 256)
-    mix_umma_kernel<256><<<p.grid, MixCfg<256>::THREADS, p.smem, s>>>(p.ta, p.tb, ma);
-  else if (p.bn == 128)
-    mix_umma_kernel<128><<<p.grid, MixCfg<128>::THREADS, p.smem, s>>>(p.ta, p.tb, ma);
+#define GFN_MIX_LAUNCH(BN, BK, MH)                                                       \
+  if (p.bn == BN && p.bk == BK && p.mh == MH) {                                          \
+    mix_umma_kernel<BN, BK, MH><<<p.grid, p.threads, p.smem, s>>>(p.ta, p.tb, ma);      \
+    return;                                                                              \
+  }
+  GFN_MIX_SHAPES(GFN_MIX_LAUNCH)
+#undef GFN_MIX_LAUNCH
+}
+
+// Tensor-core head step (head_dim 64, UMMA mixing): used when it gives every
+// SM at least one 128-row tile; GFN_LAY_HEAD=0/1 forces it off/on.
+bool use_head_umma(int batch, int heads, int hd, int rank, int mode, int sms) {
+  if (hd != 64 || mode != GFN_MIX_UMMA_F16 || (rank != 4 && rank != 8 && rank != 16)) return false;
+  if (const char* env = getenv("GFN_LAY_HEAD")) return atoi(env) != 0;
+  return (long long)((batch + 127) / 128) * heads >= sms;
+}
+
+void launch_head_umma(int rank, const CUtensorMap& tmz, const CUtensorMap& tmo, const LayPreArgs& a,
+                      dim3 grid, cudaStream_t s) {
+  constexpr int T = HeadUmmaCfg<64>::THREADS;
+  if (rank == 4)
+    layered_head_umma_kernel<4, 64><<<grid, T, head_umma_smem<4, 64>(), s>>>(tmz, tmo, a);
+  else if (rank == 8)
+    layered_head_umma_kernel<8, 64><<<grid, T, head_umma_smem<8, 64>(), s>>>(tmz, tmo, a);
   else
-    mix_umma_kernel<64><<<p.grid, MixCfg<64>::THREADS, p.smem, s>>>(p.ta, p.tb, ma);
+    layered_head_umma_kernel<16, 64><<<grid, T, head_umma_smem<16, 64>(), s>>>(tmz, tmo, a);
+}
+
+// The split head-step output catkh as [2][B][3d] fp16 in [1][128][64] boxes.
+int make_out_map(CUtensorMap* m, const __half* catkh, int batch, int dim) {
+  const cuuint64_t dims[3] = {(cuuint64_t)3 * dim, (cuuint64_t)batch, 2};
+  const cuuint64_t str[2] = {(cuuint64_t)6 * dim, (cuuint64_t)6 * dim * batch};
+  const cuuint32_t box[3] = {64, 128, 1};
+  return encode_f16_map(m, catkh, 3, dims, str, box);
+}
+
+// z [2B][d] fp32 in [128 x 32] boxes with the 128-byte swizzle.
+int make_z_map(CUtensorMap* m, const float* z, int batch, int dim) {
+  const cuuint64_t dims[2] = {(cuuint64_t)dim, (cuuint64_t)2 * batch};
+  const cuuint64_t str[1] = {(cuuint64_t)dim * 4};
+  const cuuint32_t box[2] = {32, 128};
+  return encode_map(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, z, 2, dims, str, box);
+}
+
+int set_head_umma_smem() {
+  cudaError_t e = cudaFuncSetAttribute(layered_head_umma_kernel<4, 64>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)head_umma_smem<4, 64>());
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(layered_head_umma_kernel<8, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)head_umma_smem<8, 64>());
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(layered_head_umma_kernel<16, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)head_umma_smem<16, 64>());
+  return e == cudaSuccess ? GFN_OK : cuda_status(e, "head step: shared memory attribute");
+}
+
+// ---------------------------------------------------------------- timing
+// Optional per-kernel CUDA-event timing of the layered path (measurement
+// only): while enabled, each layer's head-step and mixing launches are
+// bracketed by events recorded on the launch stream.
+std::mutex g_time_mu;
+bool g_time_on = false;
+long long* g_head_prof = nullptr;  // gfn_debug_head_profile
+std::vector<cudaEvent_t> g_time_ev;  // triplets: head start, mix start, mix end
+size_t g_time_used = 0;
+
+cudaEvent_t time_event() {
+  if (g_time_used == g_time_ev.size()) {
+    cudaEvent_t e;
+    if (cudaEventCreate(&e) != cudaSuccess) return nullptr;
+    g_time_ev.push_back(e);
+  }
+  return g_time_ev[g_time_used++];
+}
+
+void time_mark(cudaStream_t s) {
+  if (!g_time_on) return;
+  std::lock_guard<std::mutex> lock(g_time_mu);
+  if (cudaEvent_t e = time_event()) cudaEventRecord(e, s);
 }
 
 using LayPreKernel = void (*)(LayPreArgs);
@@ -176,6 +275,38 @@ bool lay_pre_for(int r, int hd, int tr, int hblock, LayPreInst* out) {
 
 extern "C" {
 
+int gfn_debug_head_profile(long long* device_stamps) {
+  g_head_prof = device_stamps;
+  return GFN_OK;
+}
+
+int gfn_debug_layered_timing(int enable) {
+  std::lock_guard<std::mutex> lock(g_time_mu);
+  g_time_on = enable != 0;
+  if (g_time_on) g_time_used = 0;
+  return GFN_OK;
+}
+
+int gfn_debug_layered_timing_read(double* head_ms, double* mix_ms, int* layer_steps) {
+  if (!head_ms || !mix_ms || !layer_steps) return fail(GFN_ERR_INVALID, "timing read: NULL output");
+  std::lock_guard<std::mutex> lock(g_time_mu);
+  double hs = 0.0, ms = 0.0;
+  const size_t n = g_time_used / 3;
+  for (size_t i = 0; i < n; ++i) {
+    float a = 0.f, b = 0.f;
+    cudaError_t e = cudaEventSynchronize(g_time_ev[3 * i + 2]);
+    if (e == cudaSuccess) e = cudaEventElapsedTime(&a, g_time_ev[3 * i], g_time_ev[3 * i + 1]);
+    if (e == cudaSuccess) e = cudaEventElapsedTime(&b, g_time_ev[3 * i + 1], g_time_ev[3 * i + 2]);
+    if (e != cudaSuccess) return cuda_status(e, "timing read");
+    hs += a;
+    ms += b;
+  }
+  *head_ms = hs;
+  *mix_ms = ms;
+  *layer_steps = (int)n;
+  return GFN_OK;
+}
+
 long long gfn_leapfrog_layered_pack_floats(int dim, int heads, int rank, int num_layers) {
   Layout L;
   if (make_layout(dim, heads, rank, num_layers, &L) != GFN_OK || heads < 2) return -1;
@@ -208,6 +339,10 @@ int gfn_leapfrog_layered_pack(const float* U_stack, const float* W_stack,
   cudaError_t e = cudaMemset2DAsync(packed + lo.wsc, (size_t)a.LF * 4, 0, 4, (size_t)num_layers, s);
   if (e != cudaSuccess) return cuda_status(e, "layered pack: scale slots");
   layered_absmax_kernel<<<148 * 4, 256, 0, s>>>(mix_x_w, mix_v_w, packed, num_layers, dim, a.LF, lo.wsc);
+  e = cudaMemset2DAsync(packed + lo.HUs, (size_t)a.LF * 4, 0, (size_t)(2 * heads) * 4, (size_t)num_layers, s);
+  if (e != cudaSuccess) return cuda_status(e, "layered pack: head scale slots");
+  layered_head_absmax_kernel<<<num_layers * heads, 256, 0, s>>>(W_forget_stack, packed, num_layers, heads,
+                                                                L.hd, a.LF, lo.HUs);
   layered_pack_kernel<<<148 * 8, 256, 0, s>>>(a);
   return launch_status("layered_pack_kernel");
 }
@@ -220,8 +355,15 @@ int gfn_leapfrog_layered_set_mixing(int mode) {
   return g_lay_mode.exchange(mode);
 }
 
+// Workspace: cat / split activations / z / state (12 B d), row statistics
+// (2 B + 4), the mixing GEMM's partial row sums (2 B ceil(d / 64)), then the
+// cuBLAS workspace (rounded up to a 256-byte boundary inside the slack).
+static long long lay_ws_base(int batch, int dim) {
+  return 12LL * batch * dim + 2LL * batch + 4 + 2LL * batch * ((dim + 63) / 64);
+}
+
 long long gfn_leapfrog_layered_workspace_floats(int batch, int dim) {
-  return 12LL * batch * dim + 2LL * batch + 4 + kLayCublasWsFloats;
+  return lay_ws_base(batch, dim) + 64 + kLayCublasWsFloats;
 }
 
 int gfn_leapfrog_layered_forward(const float* x_init, const float* v_init,
@@ -265,9 +407,11 @@ int gfn_leapfrog_layered_forward(const float* x_init, const float* v_init,
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   if (cublasSetStream(hb, s) != CUBLAS_STATUS_SUCCESS) return fail(GFN_ERR_CUDA, "cublasSetStream");
   {
-    const long long base = 12LL * batch * dim + 2LL * batch + 4;
-    float* cws = workspace + ((base + 63) / 64) * 64;
-    const size_t bytes = (size_t)(workspace_floats - ((base + 63) / 64) * 64) * 4;
+    // cuBLAS wants a 256-byte aligned workspace: round the absolute address up
+    const uintptr_t p0 = reinterpret_cast<uintptr_t>(workspace + lay_ws_base(batch, dim));
+    const uintptr_t p1 = (p0 + 255) & ~(uintptr_t)255;
+    float* cws = reinterpret_cast<float*>(p1);
+    const size_t bytes = (size_t)(workspace_floats * 4) - (size_t)(p1 - reinterpret_cast<uintptr_t>(workspace));
     if (cublasSetWorkspace(hb, cws, bytes) != CUBLAS_STATUS_SUCCESS)
       return fail(GFN_ERR_CUDA, "cublasSetWorkspace");
   }
@@ -282,11 +426,21 @@ int gfn_leapfrog_layered_forward(const float* x_init, const float* v_init,
   float* xs = workspace + 10 * BD;
   float* vs = workspace + 11 * BD;
   float* stat = workspace + 12 * BD;
+  float* spart = stat + 2LL * batch + 4;
   MixUmmaPlan mix;
   if (mode == GFN_MIX_UMMA_F16) {
     st = make_mix_plan(&mix, reinterpret_cast<const __half*>(catk), packed, lo, batch, dim, num_layers, sms);
     if (st) return st;
   }
+  const bool head_tc = use_head_umma(batch, heads, L.hd, rank, mode, sms);
+  CUtensorMap zmap, omap;
+  if (head_tc) {
+    st = set_head_umma_smem();
+    if (!st) st = make_z_map(&zmap, z, batch, dim);
+    if (!st) st = make_out_map(&omap, reinterpret_cast<const __half*>(catk), batch, dim);
+    if (st) return st;
+  }
+  const dim3 head_grid((batch + 127) / 128, heads);
   const size_t pre_smem = inst.smem;
   cudaError_t ae = cudaFuncSetAttribute(pre, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pre_smem);
   if (ae != cudaSuccess) return cuda_status(ae, "layered: shared memory attribute");
@@ -307,12 +461,17 @@ int gfn_leapfrog_layered_forward(const float* x_init, const float* v_init,
         a.in_stride = t == 0 ? state_row_stride : dim;
       } else {
         const float* prev = packed + (long long)(l - 1) * lo.total;
-        if (!fuse_stat)
-          layered_rowstat_kernel<<<stat_blocks, 256, 0, s>>>(z, prev + lo.bx, prev + lo.bv, stat, batch,
-                                                             dim);
         a.z = z;
-        a.stat = fuse_stat ? nullptr : stat;
         a.prev = prev;
+        if (mode == GFN_MIX_UMMA_F16) {  // the GEMM epilogue left partial row sums
+          a.spart = spart;
+          a.nparts = dim / mix.bn;
+        } else {
+          if (!fuse_stat)
+            layered_rowstat_kernel<<<stat_blocks, 256, 0, s>>>(z, prev + lo.bx, prev + lo.bv, stat,
+                                                               batch, dim);
+          a.stat = fuse_stat ? nullptr : stat;
+        }
       }
       a.f32 = forces_f32; a.fbf16 = reinterpret_cast<const __nv_bfloat16*>(forces_bf16);
       a.ids = token_ids; a.table = embed_table; a.vocab = vocab; a.mask = mask;
@@ -321,12 +480,19 @@ int gfn_leapfrog_layered_forward(const float* x_init, const float* v_init,
       else if (mode == GFN_MIX_SPLIT_F16 || mode == GFN_MIX_UMMA_F16) a.catkh = reinterpret_cast<__half*>(catk);
       else a.cat = cat; a.d = dim; a.H = heads;
       a.hd = L.hd; a.base_dt = base_dt;
-      pre<<<pre_grid, LAY_THREADS, pre_smem, s>>>(a);
+      a.prof = g_head_prof;
+      time_mark(s);
+      if (head_tc)
+        launch_head_umma(rank, zmap, omap, a, head_grid, s);
+      else
+        pre<<<pre_grid, LAY_THREADS, pre_smem, s>>>(a);
+      time_mark(s);
       if (mode == GFN_MIX_UMMA_F16) {
         MixUmmaArgs ma;
-        ma.z = z; ma.alpha = lay + lo.wsc + 2; ma.B = batch; ma.d = dim; ma.layer = l;
-        ma.mtiles = (batch + 127) / 128; ma.ntiles = dim / mix.bn;
+        ma.z = z; ma.alpha = lay + lo.wsc + 2; ma.spart = spart; ma.bias = lay + lo.bx; ma.B = batch; ma.d = dim; ma.layer = l;
+        ma.mtiles = (batch + 128 * mix.mh - 1) / (128 * mix.mh); ma.ntiles = dim / mix.bn;
         launch_mix(mix, ma, s);
+        time_mark(s);
         continue;
       }
       // z[i] = cat[i] . W_i^T for i in {x, v}: column-major view z^T = W cat^T
@@ -351,6 +517,7 @@ int gfn_leapfrog_layered_forward(const float* x_init, const float* v_init,
                                        lay + lo.Wx, dim, (long long)dim * dim, cat, dim, BD, &zero,
                                        z, dim, BD, 2);
       }
+      time_mark(s);
       if (cs != CUBLAS_STATUS_SUCCESS) return fail(GFN_ERR_CUDA, "mixing GEMM failed (%d)", (int)cs);
     }
     const float* last = packed + (long long)(num_layers - 1) * lo.total;

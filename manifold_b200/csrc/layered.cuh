@@ -31,9 +31,14 @@ constexpr int LAY_THREADS = 256;
 // Then the split-fp16 copy WH [2][d][3d] (fp16): weights scaled by s (a power
 // of two per layer), w s = w0 + w1 laid along K as [w0 w1 w0] against the
 // activations' [c0 c0 c1]; then 4 floats: max|W|, s, 1/s, 0.
+// Then, for the tensor-core head step, per head the friction weight W_f
+// scaled by a power of two s_h and split into two fp16 pieces, each stored
+// as the shared-memory image of a K-major [hd][hd] UMMA operand tile
+// (hd * 2-byte rows, 16-byte units XOR-swizzled by row & 7): HU [H][2][hd][hd]
+// fp16; then per head 2 floats (max|W_f|, 1/s_h), padded to 4.
 struct LayOffsets {
   int head, hblock, sc, bx, bv, gx, gv;
-  long long Wx, Wv, WK, WH, wsc;
+  long long Wx, Wv, WK, WH, wsc, HU, HUs;
   long long total;
 };
 constexpr int LAY_SPLIT = 6;
@@ -53,7 +58,9 @@ __host__ __device__ inline LayOffsets lay_offsets(int H, int hd, int r, int d) {
   o.WK = o.Wv + (long long)d * d;
   o.WH = o.WK + (long long)LAY_SPLIT * d * d;     // after 2 * d * 6d bf16
   o.wsc = o.WH + (long long)LAY_SPLIT_H * d * d;  // after 2 * d * 3d fp16
-  o.total = o.wsc + 4;
+  o.HU = o.wsc + 4;
+  o.HUs = o.HU + (long long)H * hd * hd;          // after H * 2 * hd * hd fp16
+  o.total = o.HUs + ((2 * H + 3) / 4) * 4;
   return o;
 }
 
@@ -81,6 +88,36 @@ __global__ void layered_absmax_kernel(const float* __restrict__ Wx, const float*
     if (w > 0.f)
       atomicMax(reinterpret_cast<unsigned*>(out + (long long)l * LF + wsc), __float_as_uint(w));
   }
+}
+
+// Byte offset of element (n, k) in the shared-memory image of a K-major
+// fp16 operand tile whose rows are `rowbytes` (64 or 128) long, with the
+// matching swizzle (the pattern the TMA engine writes and the UMMA
+// descriptor reads): address bits [4, 7) are XORed with bits [7, 10), i.e.
+// the 16-byte unit u of row n is stored at unit u ^ ((n * rowbytes / 128) mod units).
+__host__ __device__ inline int umma_kmajor_xor(int n, int rowbytes) {
+  return ((n * rowbytes) >> 7) & ((rowbytes >> 4) - 1);
+}
+__host__ __device__ inline int umma_kmajor_off(int n, int k, int rowbytes) {
+  const int u = (k * 2) >> 4;  // 16-byte unit within the row
+  return n * rowbytes + ((u ^ umma_kmajor_xor(n, rowbytes)) << 4) + ((k * 2) & 15);
+}
+
+// max |W_f| of every (layer, head) into the pack's HUs slots (zeroed first).
+__global__ void layered_head_absmax_kernel(const float* __restrict__ Wf, float* out, int NL, int H,
+                                           int hd, long long LF, long long HUs) {
+  const int lh = blockIdx.x;  // layer * H + head
+  if (lh >= NL * H) return;
+  const int l = lh / H, h = lh - l * H;
+  float m = 0.f;
+  for (int i = threadIdx.x; i < hd * hd; i += blockDim.x) m = fmaxf(m, fabsf(Wf[(long long)lh * hd * hd + i]));
+  m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 16));
+  m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 8));
+  m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 4));
+  m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
+  m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
+  if ((threadIdx.x & 31) == 0 && m > 0.f)
+    atomicMax(reinterpret_cast<unsigned*>(out + (long long)l * LF + HUs + 2 * h), __float_as_uint(m));
 }
 
 struct LayPackArgs {
@@ -124,6 +161,36 @@ __global__ void layered_pack_kernel(const LayPackArgs a) {
       v = a.Wx[(long long)l * d * d + (off - o.Wx)];
     } else if (off < o.WK) {
       v = a.Wv[(long long)l * d * d + (off - o.Wv)];
+    } else if (off >= o.HUs) {
+      const int q = (int)(off - o.HUs);
+      if (q >= 2 * a.H || (q & 1) == 0) {
+        if (q >= 2 * a.H) a.out[e] = 0.f;
+        continue;  // max|W_f| slots are written by layered_head_absmax_kernel
+      }
+      v = 1.f / lay_weight_scale(a.out[(long long)l * a.LF + o.HUs + (q - 1)]);
+    } else if (off >= o.HU) {
+      // two fp16 of HU per float slot; slot pair -> (head, piece, byte offset)
+      const long long q = 2 * (off - o.HU);  // fp16 index within the section
+      const int per_piece = hd * hd, per_head = 2 * per_piece;
+      const int h = (int)(q / per_head);
+      const int rem = (int)(q - (long long)h * per_head);
+      const int piece = rem / per_piece;
+      const int boff = (rem - piece * per_piece) * 2;  // byte offset inside the tile image
+      const int rowbytes = hd * 2;
+      const float s = lay_weight_scale(a.out[(long long)l * a.LF + o.HUs + 2 * h]);
+      __half pr[2];
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        // invert umma_kmajor_off: row n, swizzled unit, element within unit
+        const int bo = boff + 2 * u;
+        const int n = bo / rowbytes;
+        const int wi = bo - n * rowbytes;
+        const int k = (((wi >> 4) ^ umma_kmajor_xor(n, rowbytes)) << 3) + ((wi & 15) >> 1);
+        const float w = a.Wf[(((long long)l * a.H + h) * hd + n) * hd + k] * s;  // W_f[n][k]
+        const __half w0 = __float2half_rn(w);
+        pr[u] = piece == 0 ? w0 : __float2half_rn(w - __half2float(w0));
+      }
+      v = __uint_as_float((unsigned)__half_as_ushort(pr[0]) | ((unsigned)__half_as_ushort(pr[1]) << 16));
     } else if (off >= o.wsc) {
       const int q = (int)(off - o.wsc);
       if (q == 0) continue;  // max|W|, written by layered_absmax_kernel
@@ -213,6 +280,8 @@ struct LayPreArgs {
   // ... or the previous layer's mixing output z [2][B][d] with its params
   const float* z;
   const float* stat;    // [2][B], or NULL: the block computes its rows' factors
+  const float* spart;   // or [2][nparts][B] partial sums of squares from the mixing GEMM
+  int nparts;
   const float* prev;    // previous layer's pack run (bias / norm gains)
   // force of token t
   const float* f32;
@@ -228,6 +297,7 @@ struct LayPreArgs {
   __half* catkh;        // [2][B][3d] split-fp16 head-step outputs, or NULL
   int B, d, H, hd;
   float base_dt;
+  long long* prof;  // measurement only: per-CTA phase timestamps, or NULL
 };
 
 // Tile of the head-step kernel: TR rows of one head; thread (ty, tx) owns
@@ -465,7 +535,19 @@ __global__ void __launch_bounds__(LAY_THREADS, (TR * HD <= 2048 && RK <= 8) ? 3 
   const float* bfh = WgT + HD * RK;
   float* xT = hsm + o.hblock;
   float* sstat = xT + HD * TR;  // [2][TR] RMSNorm factors when computed here
-  if (a.z && !a.stat) {
+  if (a.z && !a.stat && a.spart) {
+    for (int q = threadIdx.x; q < 2 * TR; q += LAY_THREADS) {
+      const int which = q / TR, r = q - which * TR, b = blockIdx.x * TR + r;
+      float f = 0.f;
+      if (b < B) {
+        float s = 0.f;
+        for (int p = 0; p < a.nparts; ++p) s += a.spart[((long long)which * a.nparts + p) * B + b];
+        f = 1.f / sqrtf(s * (1.f / (float)d) + 1.1920928955078125e-07f);
+      }
+      sstat[q] = f;
+    }
+    __syncthreads();
+  } else if (a.z && !a.stat) {
     const int w = threadIdx.x >> 5, ln = threadIdx.x & 31;
     for (int q = w; q < 2 * TR; q += LAY_THREADS / 32) {
       const int which = q / TR, r = q - which * TR, b = blockIdx.x * TR + r;

@@ -114,6 +114,20 @@ GFN_DEV uint64_t desc_sw128(uint32_t saddr) {
   return d;
 }
 
+// K-major tile with a `swz`-byte swizzle (64 or 128): rows of `swz` bytes,
+// 8-row atoms of 8 * swz bytes.
+template <int SWZ>
+GFN_DEV uint64_t desc_kmajor(uint32_t saddr) {
+  static_assert(SWZ == 64 || SWZ == 128, "swizzle");
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+  d |= (uint64_t)1 << 16;
+  d |= (uint64_t)((8u * SWZ) >> 4) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)(SWZ == 128 ? 2 : 4) << 61;
+  return d;
+}
+
 // Instruction descriptor of kind::f16 with fp16 A and B (both K-major), fp32
 // accumulator, shape M x N.
 constexpr uint32_t idesc_f16_f32(int M, int N) {
@@ -160,6 +174,42 @@ GFN_DEV void tmem_ld32(uint32_t taddr, float (&v)[32]) {
       : "memory");
 #pragma unroll
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// 16 consecutive fp32 accumulator columns (see tmem_ld32).
+GFN_DEV void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr)
+      : "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// 8 consecutive fp32 accumulator columns (see tmem_ld32).
+GFN_DEV void tmem_ld8(uint32_t taddr, float (&v)[8]) {
+  uint32_t r[8];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+      : "r"(taddr)
+      : "memory");
+#pragma unroll
+  for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+template <int N>
+GFN_DEV void tmem_ld(uint32_t taddr, float (&v)[N]) {
+  if constexpr (N == 8) tmem_ld8(taddr, v);
+  else if constexpr (N == 16) tmem_ld16(taddr, v);
+  else tmem_ld32(taddr, v);
 }
 
 GFN_DEV uint32_t elect_one_lane() { return (threadIdx.x & 31) == 0; }

@@ -56,6 +56,23 @@ def _check_config(physics_config, integrator_type):
         raise GfnError("isomeric head groups are not implemented on this build")
 
 
+# batch * dim from which the layer-by-layer path is faster than the fused
+# persistent kernel (measured on B200: C3 256 x 512 and C4 4096 x 1024 are
+# faster layered, C1 / C2 fused)
+LAYERED_MIN_ELEMS = 1 << 17
+
+
+def use_layered_path(path, heads, dim, batch):
+    """True when the layer-by-layer (head-step kernel + tensor-core mixing
+    GEMM) path computes the recurrence: `path` "layered", or "auto" with
+    head mixing, a supported head dim and batch * dim >= LAYERED_MIN_ELEMS."""
+    if heads == 1 or path == "fused":
+        return False
+    if path == "layered":
+        return True
+    return dim // heads in (16, 32, 64, 128) and batch * dim >= LAYERED_MIN_ELEMS
+
+
 class MLayer(nn.Module):
     """One M-Layer: per-head leapfrog, head mixing, RMSNorm, saturation.
 
@@ -106,6 +123,9 @@ class MLayer(nn.Module):
             nn.init.zeros_(self.out_proj_v.bias)
         self.use_recursive = False
         self._pack = PackCache()
+        # "auto" (by batch size), "fused" or "layered": which recurrence kernel
+        # computes an inference step (the same choice as Manifold.recurrence)
+        self.recurrence_path = "auto"
 
     def forward(self, x, v, force=None, context=None, collect_christ=False):
         """One layer step for every row: returns (x_next, v_next, context, [])."""
@@ -113,7 +133,6 @@ class MLayer(nn.Module):
         if collect_christ:
             raise GfnError("collect_christ is not supported by the fused kernels")
         B = x.shape[0]
-        packed, meta = self._pack.get([self])
         if force is None:
             force = torch.zeros_like(x)
         if torch.is_grad_enabled() and any(t.requires_grad for t in
@@ -121,9 +140,11 @@ class MLayer(nn.Module):
             from .training import leapfrog_sequence_train
             _, _, xn, vn = leapfrog_sequence_train([self], x, v, force.reshape(B, 1, self.dim))
             return xn, vn, torch.ones(B, self.heads, device=x.device, dtype=x.dtype), []
-        _, _, xn, vn = ops.leapfrog_sequence(x, v, packed, meta, self.base_dt,
-                                             forces=force.reshape(B, 1, self.dim),
-                                             want_x_seq=False, want_v_seq=False)
+        layered = use_layered_path(self.recurrence_path, self.heads, self.dim, B)
+        packed, meta = self._pack.get([self], layered=layered)
+        seq = ops.leapfrog_layered_sequence if layered else ops.leapfrog_sequence
+        _, _, xn, vn = seq(x, v, packed, meta, self.base_dt, forces=force.reshape(B, 1, self.dim),
+                           want_x_seq=False, want_v_seq=False)
         context_next = torch.ones(B, self.heads, device=x.device, dtype=x.dtype)
         return xn, vn, context_next, []
 

@@ -14,14 +14,8 @@ import torch.nn as nn
 from ._lib import GfnError, require_cuda
 from .cuda import ops
 from .embeddings import FunctionalEmbedding, ImplicitEmbedding
-from .layers import MLayer, ParallelMLayer
+from .layers import LAYERED_MIN_ELEMS, MLayer, ParallelMLayer, use_layered_path  # noqa: F401
 from .packing import PackCache
-
-# batch * dim from which recurrence() takes the layer-by-layer path: from
-# there the per-layer mixing is a GEMM with enough rows for the tensor cores
-# (measured on B200: C3 at 256 x 512 and C4 at 4096 x 1024 are faster layered;
-# C2 at 64 x 256 is faster fused)
-LAYERED_MIN_ELEMS = 1 << 17
 
 
 class ImplicitReadout(nn.Module):
@@ -149,13 +143,7 @@ class Manifold(nn.Module):
         """Layer-by-layer path (head-step kernel + fp32 GEMM mixing) for
         large batches, the fused persistent kernel otherwise.  `recurrence_path`
         ("auto", "fused", "layered") overrides the choice."""
-        path = getattr(self, "recurrence_path", "auto")
-        if self.heads == 1 or path == "fused":
-            return False
-        if path == "layered":
-            return True
-        hd = self.dim // self.heads
-        return hd in (16, 32, 64, 128) and batch * self.dim >= LAYERED_MIN_ELEMS
+        return use_layered_path(getattr(self, "recurrence_path", "auto"), self.heads, self.dim, batch)
 
     def recurrence(self, input_ids=None, attention_mask=None, state=None, force_manual=None,
                    want_v_seq=True):

@@ -32,3 +32,18 @@ def max_rel(a, b):
     a = np.asarray(a, np.float64)
     b = np.asarray(b, np.float64)
     return float(np.max(np.max(np.abs(a - b), -1) / np.maximum(np.max(np.abs(b), -1), 1e-30)))
+
+
+def elementwise_rel(a, b, floor_frac=1e-2):
+    """max over elements of |a - b| / max(|b|, floor_frac * max|b_row|): the
+    element-relative error, with elements far below their row's magnitude
+    (where only absolute error is meaningful) measured against that floor."""
+    a = np.asarray(a, np.float64)
+    b = np.asarray(b, np.float64)
+    den = np.maximum(np.abs(b), floor_frac * np.max(np.abs(b), axis=-1, keepdims=True))
+    return float(np.max(np.abs(a - b) / np.maximum(den, 1e-300)))
+
+
+def report(a, b, what):
+    """Prints the row-relative and element-relative errors of a vs b."""
+    print(f"{what}: row-relative {max_rel(a, b):.2e}, element-relative {elementwise_rel(a, b):.2e}")

@@ -109,6 +109,37 @@ def test_backward_c5_shapes_vs_oracle_and_deterministic():
         gclose(layer.dt_params.grad.cpu(), lg["dt_params"], f"l{l} dt")
 
 
+def test_backward_c5_full_length_vs_float64_oracle():
+    """C5 layer shapes over the full 1024 tokens (8 layers, 8192 reverse layer
+    steps) on 2 rows: gradients vs the float64 oracle backward."""
+    cfg = dict(C.CASES["c5s"], B=2, L=1024, seed=43, V=500)
+    P = C.make_params(cfg)
+    rng = np.random.default_rng(5)
+    B, L, d = 2, 1024, cfg["d"]
+    ids = rng.integers(0, cfg["V"], (B, L))
+    Gx = (rng.standard_normal((B, L, d)) * 0.05).astype(np.float32)
+    Gv = (rng.standard_normal((B, L, d)) * 0.05).astype(np.float32)
+    z = np.zeros((B, d), np.float32)
+    m, F = run_grad(cfg, P, ids, Gx, Gv, z, z)
+    x0 = np.broadcast_to(P["x0"], (B, d)).astype(np.float64)
+    v0 = np.broadcast_to(P["v0"], (B, d)).astype(np.float64)
+    lay = [{k: a.astype(np.float64) for k, a in lp.items()} for lp in P["layers"]]
+    res = O.manifold_backward(x0, v0, P["emb"][ids].astype(np.float64), lay, cfg["H"], cfg["dt"],
+                              Gx.astype(np.float64), Gv.astype(np.float64))
+    gclose(F.grad.cpu(), res["forces"], "forces")
+    gclose(m.x0.grad.cpu()[0], res["x0"].sum(0), "x0")
+    gclose(m.v0.grad.cpu()[0], res["v0"].sum(0), "v0")
+    for l in (0, 4, 7):
+        lg, layer = res["layers"][l], m.layers[l]
+        gclose(layer.out_proj_x.weight.grad.cpu(), lg["Wx"], f"l{l} Wx")
+        gclose(layer.out_proj_v.weight.grad.cpu(), lg["Wv"], f"l{l} Wv")
+        gclose(torch.stack([c.forget_gate.weight.grad for c in layer.christoffels]).cpu(), lg["Wf"],
+               f"l{l} Wf")
+        gclose(torch.stack([c.U.grad for c in layer.christoffels]).cpu(), lg["U"], f"l{l} U")
+        gclose(torch.stack([c.W.grad for c in layer.christoffels]).cpu(), lg["W"], f"l{l} W")
+        gclose(layer.dt_params.grad.cpu(), lg["dt_params"], f"l{l} dt")
+
+
 def test_mlayer_step_gradients_flow():
     """MLayer.forward under autograd runs the fused single-step kernels."""
     import manifold_b200 as gfn

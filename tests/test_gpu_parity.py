@@ -17,7 +17,7 @@ import torch
 
 from oracle import gfn_oracle as O
 from tests.golden import cases as C
-from tests.parity import max_rel, rowwise_close
+from tests.parity import max_rel, report, rowwise_close
 
 pytestmark = pytest.mark.gpu
 
@@ -76,11 +76,59 @@ def test_layer_step_matches_reference(name):
     g = load(name)
     m = build(cfg)
     layer = m.layers[int(g["step_layer"])]
+    layer.recurrence_path = "fused"
     with torch.no_grad():
         xo, vo, ctx, _ = layer(cu(g["step_x"]), cu(g["step_v"]), cu(g["step_F"]))
+    report(xo.cpu().numpy(), g["step_xo"], f"{name} fused step x")
+    report(vo.cpu().numpy(), g["step_vo"], f"{name} fused step v")
     rowwise_close(xo.cpu().numpy(), g["step_xo"], what="x")
     rowwise_close(vo.cpu().numpy(), g["step_vo"], what="v")
     assert ctx.shape == (5, cfg["H"])
+
+
+@pytest.mark.parametrize("name", ["c3s", "c4s"])
+def test_layer_step_layered_matches_reference(name, mixing):
+    """Teacher-forced single MLayer step through the layered (large batch)
+    path, in every mixing arithmetic, at the per-step bar."""
+    cfg = C.CASES[name]
+    g = load(name)
+    m = build(cfg)
+    layer = m.layers[int(g["step_layer"])]
+    layer.recurrence_path = "layered"
+    with torch.no_grad():
+        xo, vo, _, _ = layer(cu(g["step_x"]), cu(g["step_v"]), cu(g["step_F"]))
+    report(xo.cpu().numpy(), g["step_xo"], f"{name} layered/{mixing} step x")
+    report(vo.cpu().numpy(), g["step_vo"], f"{name} layered/{mixing} step v")
+    rowwise_close(xo.cpu().numpy(), g["step_xo"], what="x")
+    rowwise_close(vo.cpu().numpy(), g["step_vo"], what="v")
+
+
+def test_c4_layer_step_full_batch_layered(mixing):
+    """C4 layer shape at the full decode batch (4096 rows), teacher forced:
+    one layered layer step from random states vs the float64 oracle on 48
+    sampled rows, at the per-step bar."""
+    cfg = dict(C.CASES["c4s"], B=4096, L=1, seed=9)
+    P = C.make_params(cfg)
+    m = build(cfg, P)
+    li = 5
+    layer = m.layers[li]
+    layer.recurrence_path = "layered"
+    d = cfg["d"]
+    rng = np.random.default_rng(11)
+    x = rng.standard_normal((4096, d)).astype(np.float32)
+    v = (rng.standard_normal((4096, d)) * 2).astype(np.float32)
+    F = P["emb"][rng.integers(0, cfg["V"], 4096)]
+    with torch.no_grad():
+        xo, vo, _, _ = layer(cu(x), cu(v), cu(F))
+    rows = np.r_[0:16, 2040:2056, 4080:4096]
+    lp = {k: a.astype(np.float64) for k, a in P["layers"][li].items()}
+    ox, ov = O.mlayer_step(x[rows].astype(np.float64), v[rows].astype(np.float64),
+                           F[rows].astype(np.float64), lp, cfg["H"], cfg["dt"])
+    xo, vo = xo.cpu().numpy()[rows], vo.cpu().numpy()[rows]
+    report(xo, ox, f"C4 full-batch layered/{mixing} step x vs float64")
+    report(vo, ov, f"C4 full-batch layered/{mixing} step v vs float64")
+    rowwise_close(xo, ox, what="x")
+    rowwise_close(vo, ov, what="v")
 
 
 def test_decode_streaming_state_c4s():
@@ -228,6 +276,28 @@ def test_c3_shapes_full_batch_slice_vs_oracle():
     rowwise_close(xs.cpu().numpy()[rows], oxs, SEQ_RTOL, SEQ_ATOL, "x_seq")
 
 
+def test_c3_full_batch_64_tokens_vs_oracle():
+    """C3 shapes at the full batch 256 over 64 tokens (layered path, bf16
+    functional forces as in the LM-prefill config): 6 sampled rows against
+    the oracle fed the same bf16-rounded forces, free-running bar."""
+    cfg = dict(C.CASES["c3s"], B=256, L=64, seed=23)
+    P = C.make_params(cfg)
+    ids = C.zipf_ids(np.random.default_rng(4), cfg["V"], (256, 64))
+    m = build(cfg, P)
+    m.force_dtype = torch.bfloat16
+    assert m._use_layered(256)
+    with torch.no_grad():
+        xs, vs, (x, v), forces = m.recurrence(cu(ids))
+    rows = np.r_[0:3, 253:256]
+    F = forces.float().cpu().numpy()[rows]
+    x0 = np.broadcast_to(P["x0"], (len(rows), cfg["d"])).copy()
+    v0 = np.broadcast_to(P["v0"], (len(rows), cfg["d"])).copy()
+    oxs, ovs, _, _ = O.manifold_forward(x0, v0, F, P["layers"], cfg["H"], cfg["dt"])
+    report(xs.cpu().numpy()[rows], oxs, "C3 64 tokens x_seq")
+    rowwise_close(xs.cpu().numpy()[rows], oxs, SEQ_RTOL, SEQ_ATOL, "x_seq")
+    rowwise_close(vs.cpu().numpy()[rows], ovs, SEQ_RTOL, SEQ_ATOL, "v_seq")
+
+
 def test_scan_long_and_chunked_paths():
     from manifold_b200.cuda import ops
     rng = np.random.default_rng(1)
@@ -281,14 +351,23 @@ def test_errors_are_loud():
     assert ops.device_error(reset=True) == 0
 
 
-@pytest.fixture(params=["umma_f16", "split_bf16", "fp32_simt", "split_f16"])
+@pytest.fixture(params=["umma_f16", "umma_f16+tc_head", "split_bf16", "fp32_simt", "split_f16"])
 def mixing(request):
+    """Mixing arithmetic of the layered path; "+tc_head" also forces the
+    tensor-core head-step kernel (head_dim 64) at any batch size."""
     from manifold_b200.cuda import ops
+    name = request.param.split("+")[0]
     mode = {"split_bf16": ops.MIX_SPLIT_BF16, "fp32_simt": ops.MIX_FP32_SIMT,
-            "split_f16": ops.MIX_SPLIT_F16, "umma_f16": ops.MIX_UMMA_F16}[request.param]
+            "split_f16": ops.MIX_SPLIT_F16, "umma_f16": ops.MIX_UMMA_F16}[name]
     prev = ops.set_layered_mixing(mode)
+    old = os.environ.get("GFN_LAY_HEAD")
+    os.environ["GFN_LAY_HEAD"] = "1" if "tc_head" in request.param else "0"
     yield request.param
     ops.set_layered_mixing(prev)
+    if old is None:
+        del os.environ["GFN_LAY_HEAD"]
+    else:
+        os.environ["GFN_LAY_HEAD"] = old
 
 
 @pytest.mark.parametrize("name", ["tiny", "mask", "c1", "c2s", "c3s", "c4s", "c5s"])
