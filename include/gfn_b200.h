@@ -13,6 +13,10 @@
  *    a device error word (gfn_get_device_error) and finish their launch.
  *  - `rank` is the per-head Christoffel rank (U.size(-1)), as in the
  *    reference's launchers; `heads * head_dim == dim`.
+ *  - Thread safety: entry points may be called from several host threads.
+ *    The library's per-device cuBLAS handles (used only by the library-GEMM
+ *    mixing modes and the readout GEMMs) are locked for the whole call that
+ *    uses them; the default tensor-core paths use no library handle.
  *
  * Each function names the reference entry point it replaces
  * (gfn/cuda/cuda_kernels.cpp is the reference's pybind/C boundary).
@@ -321,7 +325,8 @@ int gfn_parallel_scan(const float* a, const float* x, float* y, float* workspace
  *    (use gfn_parallel_scan with a workspace instead).
  *  - The first call on a device looks up that array's device address
  *    (cudaGetSymbolAddress) with the device current; make that first call
- *    before any stream capture on the device.
+ *    before any stream capture on the device.  The lookup is repeated when
+ *    the device's context has been re-created (after cudaDeviceReset).
  *  - All calls share the one array and it keeps the last call's contents
  *    (nothing in it is read before the same call writes it).  Calls whose
  *    executions overlap on the GPU, e.g. on two streams at once, race on

@@ -7,6 +7,8 @@
 #include <atomic>
 #include <mutex>
 
+#include <cuda.h>
+
 #include "../../include/gfn_b200.h"
 #include "embed.cuh"
 #include "leapfrog_seq.cuh"
@@ -633,21 +635,53 @@ constexpr long long GFN_SCAN_STATIC_MAX_COLUMNS = GFN_SCAN_STATIC_FLOATS / 4;  /
 
 static __device__ __align__(256) float g_scan_static_scratch[GFN_SCAN_STATIC_FLOATS];
 
-// Device address of g_scan_static_scratch, looked up once per device.  In
-// host code the symbol name is only a host-side stand-in, so the address has
-// to come from cudaGetSymbolAddress with that device current.
+// Device address of g_scan_static_scratch, looked up once per (device,
+// context).  In host code the symbol name is only a host-side stand-in, so
+// the address has to come from cudaGetSymbolAddress with that device
+// current.  The cache is keyed by the context's unique id as well: after a
+// cudaDeviceReset the primary context (and the module holding the array) is
+// created anew, and the lookup is repeated.
 constexpr int GFN_MAX_DEVICES = 64;
 float* g_scan_static_ptr[GFN_MAX_DEVICES] = {};
+unsigned long long g_scan_static_ctx[GFN_MAX_DEVICES] = {};
 std::mutex g_scan_static_mu;
+
+// Unique id of the calling thread's current context (0 if unavailable).
+unsigned long long current_context_id() {
+  using GetCurrent = CUresult (*)(CUcontext*);
+  using GetId = CUresult (*)(CUcontext, unsigned long long*);
+  static GetCurrent get_current = nullptr;
+  static GetId get_id = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_current = reinterpret_cast<GetCurrent>(p);
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_id = reinterpret_cast<GetId>(p);
+  });
+  CUcontext ctx = nullptr;
+  unsigned long long id = 0;
+  if (get_current && get_id && get_current(&ctx) == CUDA_SUCCESS && ctx) get_id(ctx, &id);
+  return id;
+}
 
 int scan_static_scratch(int dev, float** out) {
   if (dev < 0 || dev >= GFN_MAX_DEVICES) return fail(GFN_ERR_UNSUPPORTED, "device %d", dev);
+  // cudaFree(0) makes the device's primary context current if it is not yet
+  cudaError_t e = cudaFree(nullptr);
+  if (e != cudaSuccess) return cuda_status(e, "context init");
+  const unsigned long long ctx = current_context_id();
   std::lock_guard<std::mutex> lock(g_scan_static_mu);
-  if (!g_scan_static_ptr[dev]) {
+  if (!g_scan_static_ptr[dev] || g_scan_static_ctx[dev] != ctx || ctx == 0) {
     void* p = nullptr;
-    cudaError_t e = cudaGetSymbolAddress(&p, g_scan_static_scratch);
+    e = cudaGetSymbolAddress(&p, g_scan_static_scratch);
     if (e != cudaSuccess) return cuda_status(e, "cudaGetSymbolAddress(scan scratch)");
     g_scan_static_ptr[dev] = static_cast<float*>(p);
+    g_scan_static_ctx[dev] = ctx;
   }
   *out = g_scan_static_ptr[dev];
   return GFN_OK;

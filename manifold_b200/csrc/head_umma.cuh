@@ -31,10 +31,14 @@
 
 namespace gfn {
 
-template <int HD>
+template <int HD, int P>
 struct HeadUmmaCfg {
-  // PARTS threads per row (one warp per TMEM lane quarter and column part)
-  static constexpr int ROWS = 128, PARTS = 8, THREADS = 128 * PARTS, CPT = HD / PARTS;
+  // PARTS threads per row (one warp per TMEM lane quarter and column part).
+  // PARTS 8: 1024 threads, the force staged in shared memory, one CTA per SM;
+  // PARTS 4: 512 threads, the force in registers, two CTAs per SM.
+  static constexpr int ROWS = 128, PARTS = P, THREADS = 128 * PARTS, CPT = HD / PARTS;
+  static constexpr bool F_SMEM = P == 8;
+  static constexpr int MIN_BLOCKS = P == 8 ? 1 : 2;
   static constexpr int TL = CPT < 16 ? CPT : 16;  // TMEM columns per load
   static constexpr int ROWB = HD * 2;             // bytes per fp16 operand row
   static constexpr int A_BYTES = ROWS * ROWB;     // one fp16 piece of x (or v)
@@ -48,16 +52,16 @@ struct HeadUmmaCfg {
   //   U [HD][RK]; W^T [RK][HD]; b_f [HD]; p parts [PARTS][128][RK]; barriers
   static constexpr int STAGE = 4 * ZBOX;
   static constexpr int OFF_F = STAGE;
-  static constexpr int OFF_W = OFF_F + 2 * ZBOX;
+  static constexpr int OFF_W = OFF_F + (F_SMEM ? 2 * ZBOX : 0);
   static constexpr int OFF_F32 = OFF_W + 2 * W_BYTES;
   static_assert(HD == 64, "head dim (one 128-byte swizzle row per operand row)");
   static_assert(4 * A_BYTES <= STAGE, "x and v pieces reuse the staging area");
-  static_assert(CPT == 8, "one 16-byte unit of fp16 pieces per thread");
+  static_assert(CPT % 8 == 0, "whole 16-byte units of fp16 pieces per thread");
 };
 
-template <int RK, int HD>
+template <int RK, int HD, int P>
 constexpr size_t head_umma_smem() {
-  using C = HeadUmmaCfg<HD>;
+  using C = HeadUmmaCfg<HD, P>;
   return 1024 /* alignment */ + C::OFF_F32 +
          (size_t)(4 * HD + HD * RK + RK * HD + HD + C::PARTS * C::ROWS * RK) * 4 + 64;
 }
@@ -118,11 +122,11 @@ GFN_DEV void tma_store_3d(const void* tmap, const void* src, int x, int y, int z
 // (128-byte swizzle; unused for a layer that starts from the carried state).
 // tmo: the split output rows catkh viewed as [2][B][3d] fp16 in [1][128][64]
 // boxes (128-byte swizzle); rows past B are clipped by the map.
-template <int RK, int HD>
-__global__ void __launch_bounds__(HeadUmmaCfg<HD>::THREADS, 1)
+template <int RK, int HD, int P>
+__global__ void __launch_bounds__(HeadUmmaCfg<HD, P>::THREADS, HeadUmmaCfg<HD, P>::MIN_BLOCKS)
     layered_head_umma_kernel(const __grid_constant__ CUtensorMap tmz, const __grid_constant__ CUtensorMap tmo,
                              const LayPreArgs a) {
-  using C = HeadUmmaCfg<HD>;
+  using C = HeadUmmaCfg<HD, P>;
   static_assert(RK % 4 == 0, "rank");
   constexpr int CPT = C::CPT;
   extern __shared__ __align__(1024) uint8_t hu_smem_raw[];
@@ -158,8 +162,10 @@ __global__ void __launch_bounds__(HeadUmmaCfg<HD>::THREADS, 1)
     for (int i = 0; i < 3; ++i) mbar_init(&bars[i], 1);
     fence_mbar_init();
     const bool zin = a.z != nullptr;
-    mbar_arrive_expect_tx(&bars[0], 2 * C::W_BYTES + (zin ? 4 * HD * 4 : 0));
+    constexpr int UWB = (2 * HD * RK + HD) * 4;  // U | W^T | b_f bytes
+    mbar_arrive_expect_tx(&bars[0], 2 * C::W_BYTES + UWB + (zin ? 4 * HD * 4 : 0));
     bulk_g2s(sW, lay + o.HU + (long long)h * (HD * HD), 2 * C::W_BYTES, &bars[0]);
+    bulk_g2s(sU, lay + (long long)h * o.hblock + HD * HD, UWB, &bars[0]);
     if (zin) {
       const int offs[4] = {o.bx, o.bv, o.gx, o.gv};
 #pragma unroll
@@ -170,11 +176,29 @@ __global__ void __launch_bounds__(HeadUmmaCfg<HD>::THREADS, 1)
         umma::tma_load_2d(sZ + i * C::ZBOX, &tmz, &bars[1], h * HD + (i & 1) * 32, (i >> 1) * B + b0);
     }
   }
+  // RMSNorm factors of this row from the mixing GEMM's partial sums (issued
+  // first: their latency overlaps the copies below)
+  float rx = 0.f, rv = 0.f;
+  if (a.z && live) {
+    if (a.spart) {
+      float sx = 0.f, sv = 0.f;
+      for (int p = 0; p < a.nparts; ++p) {
+        sx += a.spart[(long long)p * B + b];
+        sv += a.spart[((long long)a.nparts + p) * B + b];
+      }
+      rx = 1.f / sqrtf(sx * (1.f / (float)d) + 1.1920928955078125e-07f);
+      rv = 1.f / sqrtf(sv * (1.f / (float)d) + 1.1920928955078125e-07f);
+    } else {
+      rx = a.stat[b];
+      rv = a.stat[B + b];
+    }
+  }
   // the token's force for this thread's columns, fetched now (it is used in
   // both kicks): fp32 into two swizzled [128][32] boxes, bf16 into one
   // swizzled [128][64] tile
   const bool fbf = a.fbf16 != nullptr;
   float fm = 0.f;
+  float F[CPT];
   {
     const void* src = nullptr;
     if (live) {
@@ -193,28 +217,43 @@ __global__ void __launch_bounds__(HeadUmmaCfg<HD>::THREADS, 1)
         }
       }
     }
-    const uint32_t nb = src ? 16u : 0u;
-    const void* s0 = src ? src : static_cast<const void*>(lay);  // any valid address when zero-filling
-    if (fbf) {
-      cp_async16(sF + r * 128 + (((c0 >> 3) ^ (r & 7)) << 4), s0, nb);
-    } else {
-      uint8_t* fb = sF + (c0 >> 5) * C::ZBOX + r * 128;
+    if constexpr (C::F_SMEM) {
+      const uint32_t nb = src ? 16u : 0u;
+      const void* s0 = src ? src : static_cast<const void*>(lay);  // any valid address when zero-filling
+      if (fbf) {
+        cp_async16(sF + r * 128 + (((c0 >> 3) ^ (r & 7)) << 4), s0, nb);
+      } else {
+        uint8_t* fb = sF + (c0 >> 5) * C::ZBOX + r * 128;
 #pragma unroll
-      for (int u = 0; u < 2; ++u)
-        cp_async16(fb + (((((c0 & 31) >> 2) + u) ^ (r & 7)) << 4),
-                   static_cast<const float*>(s0) + (src ? 4 * u : 0), nb);
+        for (int u = 0; u < 2; ++u)
+          cp_async16(fb + (((((c0 & 31) >> 2) + u) ^ (r & 7)) << 4),
+                     static_cast<const float*>(s0) + (src ? 4 * u : 0), nb);
+      }
+      asm volatile("cp.async.commit_group;" ::: "memory");
+    } else {
+#pragma unroll
+      for (int j = 0; j < CPT; ++j) F[j] = 0.f;
+      if (src && fbf) {
+#pragma unroll
+        for (int u = 0; u < CPT / 8; ++u) {
+          const uint4 w4 = __ldg(reinterpret_cast<const uint4*>(src) + u);
+          const unsigned w[4] = {w4.x, w4.y, w4.z, w4.w};
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            F[8 * u + 2 * i] = __uint_as_float(w[i] << 16);
+            F[8 * u + 2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+          }
+        }
+      } else if (src) {
+#pragma unroll
+        for (int j = 0; j < CPT; j += 4) {
+          const float4 f = ldg4(static_cast<const float*>(src) + j);
+          F[j] = f.x; F[j + 1] = f.y; F[j + 2] = f.z; F[j + 3] = f.w;
+        }
+      }
     }
-    asm volatile("cp.async.commit_group;" ::: "memory");
   }
   if (warp == 0) umma::tmem_alloc(tslot, 2 * HD);
-  {
-    const float* hs = lay + (long long)h * o.hblock;  // [WfT | U | W^T | bf]
-    for (int i = threadIdx.x; i < HD * RK; i += C::THREADS) {
-      sU[i] = hs[HD * HD + i];
-      sWg[i] = hs[HD * HD + HD * RK + i];
-    }
-    for (int i = threadIdx.x; i < HD; i += C::THREADS) sbf[i] = hs[HD * HD + 2 * HD * RK + i];
-  }
   const float eff = a.base_dt * lay[o.sc + h];
   const float hh = 0.5f * eff;
   const float inv_s = lay[o.HUs + 2 * h + 1];
@@ -226,23 +265,8 @@ __global__ void __launch_bounds__(HeadUmmaCfg<HD>::THREADS, 1)
   for (int j = 0; j < CPT; ++j) X[j] = V[j] = 0.f;
   bool ok = true;
   if (a.z) {
-    float rx = 0.f, rv = 0.f;
-    if (live) {
-      if (a.spart) {
-        float sx = 0.f, sv = 0.f;
-        for (int p = 0; p < a.nparts; ++p) {
-          sx += a.spart[(long long)p * B + b];
-          sv += a.spart[((long long)a.nparts + p) * B + b];
-        }
-        rx = 1.f / sqrtf(sx * (1.f / (float)d) + 1.1920928955078125e-07f);
-        rv = 1.f / sqrtf(sv * (1.f / (float)d) + 1.1920928955078125e-07f);
-      } else {
-        rx = a.stat[b];
-        rv = a.stat[B + b];
-      }
-    }
     GFN_HEAD_STAMP(1);
-    ok = umma::mbar_wait_sleep(&bars[1], 0) && umma::mbar_wait_sleep(&bars[0], 0);
+    ok = umma::mbar_wait_sleep(&bars[1], 0);
     GFN_HEAD_STAMP(2);
     const uint8_t* zxb = sZ + (c0 >> 5) * C::ZBOX + r * 128;
     const uint8_t* zvb = sZ + (2 + (c0 >> 5)) * C::ZBOX + r * 128;
@@ -279,38 +303,43 @@ __global__ void __launch_bounds__(HeadUmmaCfg<HD>::THREADS, 1)
 #pragma unroll
     for (int j = 0; j < CPT; ++j) X[j] = V[j] = 0.f;
   }
-  asm volatile("cp.async.wait_all;" ::: "memory");  // this thread's force copies landed
-  float F[CPT];
-  if (fbf) {
-    const uint4 u = *reinterpret_cast<const uint4*>(sF + r * 128 + (((c0 >> 3) ^ (r & 7)) << 4));
-    const unsigned w[4] = {u.x, u.y, u.z, u.w};
+  if constexpr (C::F_SMEM) {
+    asm volatile("cp.async.wait_all;" ::: "memory");  // this thread's force copies landed
+    if (fbf) {
+      const uint4 u = *reinterpret_cast<const uint4*>(sF + r * 128 + (((c0 >> 3) ^ (r & 7)) << 4));
+      const unsigned w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      F[2 * i] = __uint_as_float(w[i] << 16) * fm;
-      F[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u) * fm;
-    }
-  } else {
-    const uint8_t* fb = sF + (c0 >> 5) * C::ZBOX + r * 128;
+      for (int i = 0; i < 4; ++i) {
+        F[2 * i] = __uint_as_float(w[i] << 16);
+        F[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+      }
+    } else {
+      const uint8_t* fb = sF + (c0 >> 5) * C::ZBOX + r * 128;
 #pragma unroll
-    for (int u = 0; u < 2; ++u) {
-      const float4 f = *reinterpret_cast<const float4*>(fb + (((((c0 & 31) >> 2) + u) ^ (r & 7)) << 4));
-      F[4 * u] = f.x * fm; F[4 * u + 1] = f.y * fm; F[4 * u + 2] = f.z * fm; F[4 * u + 3] = f.w * fm;
+      for (int u = 0; u < 2; ++u) {
+        const float4 f = *reinterpret_cast<const float4*>(fb + (((((c0 & 31) >> 2) + u) ^ (r & 7)) << 4));
+        F[4 * u] = f.x; F[4 * u + 1] = f.y; F[4 * u + 2] = f.z; F[4 * u + 3] = f.w;
+      }
     }
   }
-  __syncthreads();  // z boxes consumed (the pieces overwrite them); U, W^T, b_f staged
+#pragma unroll
+  for (int j = 0; j < CPT; ++j) F[j] *= fm;
+  if (ok) ok = umma::mbar_wait_sleep(&bars[0], 0);  // W_f pieces, U, W^T, b_f landed
+  __syncthreads();  // z boxes consumed (the pieces overwrite them)
   umma::tc_fence_after();
   const uint32_t tbase = *tslot;
-  if (!a.z && threadIdx.x == 0) ok = umma::mbar_wait_spin(&bars[0], 0);  // W_f pieces landed
   const uint32_t idesc = umma::idesc_f16_f32(128, HD);
-  const int aoff = umma_kmajor_off(r, c0, C::ROWB);  // this thread's unit in a piece tile
+
 
   // ---- kick 1 at x (then the drift), kick 2 at x' (one copy of the code)
 #pragma unroll 1
   for (int kick = 0; kick < 2; ++kick) {
     const uint32_t tacc = tbase + (uint32_t)(kick * HD);
-    {  // A operand: fp16 pieces of x for the gate product
+#pragma unroll
+    for (int u8 = 0; u8 < CPT / 8; ++u8) {  // A operand: fp16 pieces of x for the gate product
       uint4 p0, p1;
-      split8(X, p0, p1);
+      split8(X + 8 * u8, p0, p1);
+      const int aoff = umma_kmajor_off(r, c0 + 8 * u8, C::ROWB);
       *reinterpret_cast<uint4*>(sA + aoff) = p0;
       *reinterpret_cast<uint4*>(sA + C::A_BYTES + aoff) = p1;
     }
@@ -374,7 +403,7 @@ __global__ void __launch_bounds__(HeadUmmaCfg<HD>::THREADS, 1)
     umma::tc_fence_after();
     GFN_HEAD_STAMP(4 + 2 * kick);
     float g[CPT];
-    umma::tmem_ld<CPT>(tacc + ((uint32_t)(32 * q) << 16) + (uint32_t)c0, g);
+    umma::tmem_ld<CPT>(tacc + ((uint32_t)(32 * q) << 16) + (uint32_t)c0, g);  // CPT = 8 or 16
 #pragma unroll
     for (int j4 = 0; j4 < CPT; j4 += 4) {
       float gm[4] = {0.f, 0.f, 0.f, 0.f};
@@ -392,8 +421,12 @@ __global__ void __launch_bounds__(HeadUmmaCfg<HD>::THREADS, 1)
       for (int i = 0; i < 4; ++i) {
         const int j = j4 + i;
         const float gam = soft_clamp20(gm[i]);
-        const float mu = sigmoid_f(g[j] * inv_s + bj[i]) * 5.f;
-        V[j] = (V[j] + hh * (F[j] - gam)) / (1.f + hh * mu);
+        // (v + h (F - Gamma)) / (1 + h * 5 sigmoid(gate)) with one division:
+        // 1 + 5h sigmoid = (1 + e + 5h) / (1 + e), e = exp(-gate); an
+        // overflowing e means sigmoid = 0 (no friction)
+        const float ope = 1.f + expf(-(g[j] * inv_s + bj[i]));
+        const float num = V[j] + hh * (F[j] - gam);
+        V[j] = isinf(ope) ? num : (num * ope) / (ope + 5.f * hh);
       }
     }
     if (kick == 0) {
@@ -406,13 +439,15 @@ __global__ void __launch_bounds__(HeadUmmaCfg<HD>::THREADS, 1)
 
   // ---- output: x' pieces are the last gate operand (still in sA); v' pieces
   // next to them; TMA stores write [c0 | c0 | c1] of x' and v'
-  {
+#pragma unroll
+  for (int u8 = 0; u8 < CPT / 8; ++u8) {
     uint4 p0, p1;
-    split8(V, p0, p1);
+    split8(V + 8 * u8, p0, p1);
+    const int aoff = umma_kmajor_off(r, c0 + 8 * u8, C::ROWB);
     *reinterpret_cast<uint4*>(sVo + aoff) = p0;
     *reinterpret_cast<uint4*>(sVo + C::A_BYTES + aoff) = p1;
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
   }
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
   __syncthreads();
   if (threadIdx.x == 0) {
     const int col = h * HD;

@@ -30,6 +30,10 @@ std::atomic<int> g_lay_mode{GFN_MIX_UMMA_F16};
 constexpr long long kLayCublasWsFloats = 1LL << 20;
 std::mutex g_cublas_mu;
 cublasHandle_t g_cublas[64] = {};
+// One lock per device handle, held for a whole forward call that uses cuBLAS
+// (stream, workspace and pointer-mode changes plus the GEMMs), so two host
+// threads never interleave them on the shared handle.
+std::mutex g_cublas_use_mu[64];
 
 int cublas_for_device(cublasHandle_t* out) {
   int dev;
@@ -167,15 +171,31 @@ bool use_head_umma(int batch, int heads, int hd, int rank, int mode, int sms) {
   return (long long)((batch + 127) / 128) * heads >= sms;
 }
 
+// Threads per row of the tensor-core head step: 4 (two 512-thread CTAs per
+// SM, measured faster at C4) or 8 (GFN_LAY_HEAD_PARTS=8).
+int head_parts() {
+  if (const char* env = getenv("GFN_LAY_HEAD_PARTS")) return atoi(env) == 8 ? 8 : 4;
+  return 4;
+}
+
+template <int P>
+void launch_head_umma_p(int rank, const CUtensorMap& tmz, const CUtensorMap& tmo, const LayPreArgs& a,
+                        dim3 grid, cudaStream_t s) {
+  constexpr int T = HeadUmmaCfg<64, P>::THREADS;
+  if (rank == 4)
+    layered_head_umma_kernel<4, 64, P><<<grid, T, head_umma_smem<4, 64, P>(), s>>>(tmz, tmo, a);
+  else if (rank == 8)
+    layered_head_umma_kernel<8, 64, P><<<grid, T, head_umma_smem<8, 64, P>(), s>>>(tmz, tmo, a);
+  else
+    layered_head_umma_kernel<16, 64, P><<<grid, T, head_umma_smem<16, 64, P>(), s>>>(tmz, tmo, a);
+}
+
 void launch_head_umma(int rank, const CUtensorMap& tmz, const CUtensorMap& tmo, const LayPreArgs& a,
                       dim3 grid, cudaStream_t s) {
-  constexpr int T = HeadUmmaCfg<64>::THREADS;
-  if (rank == 4)
-    layered_head_umma_kernel<4, 64><<<grid, T, head_umma_smem<4, 64>(), s>>>(tmz, tmo, a);
-  else if (rank == 8)
-    layered_head_umma_kernel<8, 64><<<grid, T, head_umma_smem<8, 64>(), s>>>(tmz, tmo, a);
+  if (head_parts() == 4)
+    launch_head_umma_p<4>(rank, tmz, tmo, a, grid, s);
   else
-    layered_head_umma_kernel<16, 64><<<grid, T, head_umma_smem<16, 64>(), s>>>(tmz, tmo, a);
+    launch_head_umma_p<8>(rank, tmz, tmo, a, grid, s);
 }
 
 // The split head-step output catkh as [2][B][3d] fp16 in [1][128][64] boxes.
@@ -194,15 +214,23 @@ int make_z_map(CUtensorMap* m, const float* z, int batch, int dim) {
   return encode_map(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, z, 2, dims, str, box);
 }
 
+template <int P>
+cudaError_t set_head_umma_smem_p() {
+  cudaError_t e = cudaFuncSetAttribute(layered_head_umma_kernel<4, 64, P>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)head_umma_smem<4, 64, P>());
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(layered_head_umma_kernel<8, 64, P>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)head_umma_smem<8, 64, P>());
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(layered_head_umma_kernel<16, 64, P>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)head_umma_smem<16, 64, P>());
+  return e;
+}
+
 int set_head_umma_smem() {
-  cudaError_t e = cudaFuncSetAttribute(layered_head_umma_kernel<4, 64>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)head_umma_smem<4, 64>());
-  if (e == cudaSuccess)
-    e = cudaFuncSetAttribute(layered_head_umma_kernel<8, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)head_umma_smem<8, 64>());
-  if (e == cudaSuccess)
-    e = cudaFuncSetAttribute(layered_head_umma_kernel<16, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)head_umma_smem<16, 64>());
+  cudaError_t e = set_head_umma_smem_p<8>();
+  if (e == cudaSuccess) e = set_head_umma_smem_p<4>();
   return e == cudaSuccess ? GFN_OK : cuda_status(e, "head step: shared memory attribute");
 }
 
@@ -397,16 +425,25 @@ int gfn_leapfrog_layered_forward(const float* x_init, const float* v_init,
   int sms = 148, dev = 0;
   if (cudaGetDevice(&dev) == cudaSuccess)
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (dev < 0 || dev >= 64) return fail(GFN_ERR_UNSUPPORTED, "device %d", dev);
   LayPreInst inst;
   if (!lay_pre_for(rank, L.hd, pick_tile_rows(batch, heads, L.hd, sms), lo.hblock, &inst))
     return fail(GFN_ERR_UNSUPPORTED, "layered: head_dim %d must be 16, 32, 64 or 128", L.hd);
   LayPreKernel pre = inst.fn;
-  cublasHandle_t hb;
-  st = cublas_for_device(&hb);
-  if (st) return st;
+  const long long BD = (long long)batch * dim;
+  int mode = g_lay_mode.load();
+  // the tcgen05 kernel tiles K by 64 and N by at least 64 columns
+  if (mode == GFN_MIX_UMMA_F16 && (dim % 64 != 0 || 3LL * dim > (1LL << 31) / 4))
+    mode = GFN_MIX_SPLIT_F16;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  if (cublasSetStream(hb, s) != CUBLAS_STATUS_SUCCESS) return fail(GFN_ERR_CUDA, "cublasSetStream");
-  {
+  // cuBLAS only for the library-GEMM mixing modes (the default uses none)
+  cublasHandle_t hb = nullptr;
+  std::unique_lock<std::mutex> cublas_use(g_cublas_use_mu[dev], std::defer_lock);
+  if (mode != GFN_MIX_UMMA_F16) {
+    st = cublas_for_device(&hb);
+    if (st) return st;
+    cublas_use.lock();
+    if (cublasSetStream(hb, s) != CUBLAS_STATUS_SUCCESS) return fail(GFN_ERR_CUDA, "cublasSetStream");
     // cuBLAS wants a 256-byte aligned workspace: round the absolute address up
     const uintptr_t p0 = reinterpret_cast<uintptr_t>(workspace + lay_ws_base(batch, dim));
     const uintptr_t p1 = (p0 + 255) & ~(uintptr_t)255;
@@ -415,11 +452,6 @@ int gfn_leapfrog_layered_forward(const float* x_init, const float* v_init,
     if (cublasSetWorkspace(hb, cws, bytes) != CUBLAS_STATUS_SUCCESS)
       return fail(GFN_ERR_CUDA, "cublasSetWorkspace");
   }
-  const long long BD = (long long)batch * dim;
-  int mode = g_lay_mode.load();
-  // the tcgen05 kernel tiles K by 64 and N by at least 64 columns
-  if (mode == GFN_MIX_UMMA_F16 && (dim % 64 != 0 || 3LL * dim > (1LL << 31) / 4))
-    mode = GFN_MIX_SPLIT_F16;
   float* cat = workspace;
   __nv_bfloat16* catk = reinterpret_cast<__nv_bfloat16*>(workspace + 2 * BD);
   float* z = workspace + 8 * BD;

@@ -33,11 +33,14 @@ __global__ void split_absmax_kernel(const float* __restrict__ x, long long n, fl
   if ((threadIdx.x & 31) == 0 && m > 0.f) atomicMax(reinterpret_cast<unsigned*>(slot), __float_as_uint(m));
 }
 
+// Power-of-two scale putting max|x| s in [2^13, 2^14), capped at 2^60 so
+// that a tiny (or zero) operand never gives s = inf; the product of two
+// scales then stays below 2^120, so 1/(s_a s_b) is a normal float.
 GFN_DEV float split_scale(float m) {
   if (!(m > 0.f) || !(m < 3.0e38f)) return 1.f;
   int e;
   frexpf(m, &e);  // m = f 2^e, f in [0.5, 1)
-  return ldexpf(1.f, 14 - e);
+  return ldexpf(1.f, min(14 - e, 60));
 }
 
 // x [rows][cols] fp32 -> out fp16 with K' = 3K along the K dimension
@@ -77,15 +80,22 @@ __global__ void split_f16_kernel(const float* __restrict__ x, long long rows, lo
 }
 
 __global__ void split_alpha_kernel(const float* sa, const float* sb, float beta, float* ab) {
-  ab[0] = 1.f / (sa[1] * sb[1]);
+  // scales are powers of two: 1/(s_a s_b) = 2^-(e_a + e_b) exactly
+  int ea, eb;
+  frexpf(sa[1], &ea);
+  frexpf(sb[1], &eb);
+  ab[0] = ldexpf(1.f, 2 - ea - eb);
   ab[1] = beta;
   ab[2] = 1.f;
 }
 
 std::mutex g_mu;
 cublasHandle_t g_h[64] = {};
+// One lock per device handle, held from cublasSetStream to the last GEMM of a
+// call, so two host threads never interleave stream or pointer-mode changes.
+std::mutex g_use_mu[64];
 
-int handle(cublasHandle_t* out) {
+int handle(cublasHandle_t* out, int* dev_out = nullptr) {
   int dev;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return cuda_status(e, "cudaGetDevice");
@@ -96,6 +106,7 @@ int handle(cublasHandle_t* out) {
     cublasSetMathMode(g_h[dev], CUBLAS_DEFAULT_MATH);
   }
   *out = g_h[dev];
+  if (dev_out) *dev_out = dev;
   return GFN_OK;
 }
 
@@ -128,8 +139,10 @@ int gfn_gemm_split_f16(int M, int N, int K, const void* a2, int a_k_rows, const 
   if (M <= 0 || N <= 0 || K <= 0 || !a2 || !b2 || !scale_a || !scale_b || !c || !alpha_beta)
     return fail(GFN_ERR_INVALID, "gemm_split_f16: bad arguments");
   cublasHandle_t h;
-  int st = handle(&h);
+  int hdev = 0;
+  int st = handle(&h, &hdev);
   if (st) return st;
+  std::lock_guard<std::mutex> use(g_use_mu[hdev]);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   split_alpha_kernel<<<1, 1, 0, s>>>(scale_a, scale_b, beta, alpha_beta);
   st = launch_status("gemm_split_f16 alpha");

@@ -3,11 +3,11 @@ batch 64, parity-bit tokens) over 100k tokens.
 
 Test infrastructure, not part of the product; two phases:
 
-  python tests/drift_c2.py gpu --out gpurun_out/drift_gpu.npz
+  python tests/drift_c2.py gpu --out DRIFT.npz
       (B200) streams the whole batch through Manifold.recurrence in 2000-token
       chunks with the state carried between calls and records rows 0..R-1 of
       (x, v) every `--every` tokens.
-  python tests/drift_c2.py cpu --gpu gpurun_out/drift_gpu.npz
+  python tests/drift_c2.py cpu --gpu DRIFT.npz
       (host) replays the same rows with the numpy oracle (the reference's
       algorithm, oracle/gfn_oracle.py) in float64 and float32 and prints, per
       checkpoint, the row-relative L2 distance of the GPU state and of the
@@ -110,9 +110,13 @@ def main():
     ap.add_argument("--tokens", type=int, default=100000)
     ap.add_argument("--every", type=int, default=1000)
     ap.add_argument("--rows", type=int, default=16)
-    ap.add_argument("--out", default="gpurun_out/drift_gpu.npz")
-    ap.add_argument("--gpu", default="gpurun_out/drift_gpu.npz")
+    ap.add_argument("--out", help="gpu phase: where to write the recorded GPU states (.npz)")
+    ap.add_argument("--gpu", help="cpu phase: the .npz the gpu phase wrote")
     args = ap.parse_args()
+    if args.phase == "gpu" and not args.out:
+        ap.error("the gpu phase needs --out")
+    if args.phase == "cpu" and not args.gpu:
+        ap.error("the cpu phase needs --gpu")
     run_gpu(args) if args.phase == "gpu" else run_cpu(args)
 
 

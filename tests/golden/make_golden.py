@@ -24,7 +24,9 @@ import torch
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.dirname(os.path.dirname(HERE)))
-REF = os.environ.get("GFN_REFERENCE", "/root/reference")
+REF = os.environ.get("GFN_REFERENCE")
+if not REF:
+    sys.exit("set GFN_REFERENCE to the directory holding the reference's `gfn` package")
 sys.path.append(REF)
 
 from tests.golden import cases as C  # noqa: E402
