@@ -83,6 +83,75 @@ int gfn_leapfrog_fused(const float* x, const float* v, const float* f, const flo
                        float R_val, float r_val, gfn_stream_t stream);
 
 /* ------------------------------------------------------------------------
+ * One head's leapfrog with the full friction gate and both topologies.
+ * Same operation as launch_leapfrog_fused (gfn/cuda/cuda_kernels.cpp:74-83)
+ * plus the two terms that entry cannot express:
+ *   - the input gate: mu = 5 sigmoid((feat(x) W_forget^T + b_forget) + f W_input^T),
+ *     the friction the reference's Christoffel computes when no forget stack
+ *     is given (gfn/geometry/lowrank.py:114-123); W_input [dim, dim] or NULL;
+ *   - topology 1 (torus): Gamma of gfn/geometry/toroidal.py:70-108 (U, W
+ *     unused, R_val / r_val the radii), friction features [sin x, cos x]
+ *     (W_forget [dim, 2 dim]) and x wrapped into [0, 2 pi) after the drift
+ *     (gfn/integrators/symplectic/leapfrog.py:74-91, gfn/geometry/boundaries.py:4-17).
+ * dim <= 256; rank 4, 8 or 16 (topology 0).
+ */
+int gfn_leapfrog_fused_gated(const float* x, const float* v, const float* f, const float* U,
+                             const float* W, const float* W_forget, const float* b_forget,
+                             const float* W_input, float* x_new, float* v_new, float dt,
+                             const float* dt_scales, int dt_scales_count, int batch, int dim,
+                             int rank, int steps, int topology, float plasticity, float R_val,
+                             float r_val, gfn_stream_t stream);
+
+/* Toroidal Christoffel term for one head: the topology-1 form of
+ * launch_christoffel_fused (gfn/cuda/cuda_kernels.cpp:14-19), with the
+ * semantics of gfn/geometry/toroidal.py:70-108.  v, x, gamma [batch, dim]. */
+int gfn_christoffel_torus(const float* v, const float* x, float* gamma, int batch, int dim,
+                          float R_val, float r_val, gfn_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Backward of the Christoffel term.  Replaces launch_christoffel_backward
+ * (gfn/cuda/cuda_kernels.cpp:21-29) for plasticity 0 and no singularity
+ * potential (V_w / grad_V_w must be NULL).
+ * topology 0: grad_v = dGamma/dv^T grad_gamma, grad_U / grad_W [dim, rank]
+ *   summed over the batch (overwritten, fixed summation order), grad_x
+ *   (optional) zero; needs gfn_christoffel_backward_workspace_floats floats.
+ * topology 1: grad_v and grad_x (x required); U, W, grad_U, grad_W unused.
+ */
+long long gfn_christoffel_backward_workspace_floats(int batch, int dim, int rank);
+int gfn_christoffel_backward(const float* grad_gamma, const float* v, const float* U,
+                             const float* W, const float* x, const float* V_w, float* grad_v,
+                             float* grad_U, float* grad_W, float* grad_x, float* grad_V_w,
+                             int batch, int dim, int rank, float plasticity, float sing_thresh,
+                             float sing_strength, int topology, float R_val, float r_val,
+                             float* workspace, long long workspace_floats, gfn_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Backward of gfn_leapfrog_fused / gfn_leapfrog_fused_gated (`steps` steps,
+ * reverse replay: each step's forward is recomputed from its stored input).
+ * Replaces launch_leapfrog_backward (gfn/cuda/cuda_kernels.cpp:123), which
+ * takes no friction operands and leaves dU / dW out; this entry returns the
+ * gradients of every operand:
+ *   grad_x, grad_v [batch, dim] (from grad_x_new / grad_v_new; NULL = 0),
+ *   grad_f [batch, dim] (optional), grad_U / grad_W [dim, rank] (topology 0),
+ *   grad_W_forget [dim, fin] + grad_b_forget [dim] when W_forget is given,
+ *   grad_W_input [dim, dim] when W_input is given.
+ * Parameter gradients are batch sums in a fixed order (overwritten).  dt
+ * scales are constants (no gradient).  Workspace:
+ * gfn_leapfrog_step_backward_workspace_floats(batch, dim, rank, steps, topology).
+ */
+long long gfn_leapfrog_step_backward_workspace_floats(int batch, int dim, int rank, int steps,
+                                                      int topology);
+int gfn_leapfrog_backward(const float* grad_x_new, const float* grad_v_new, const float* x,
+                          const float* v, const float* f, const float* U, const float* W,
+                          const float* W_forget, const float* b_forget, const float* W_input,
+                          float* grad_x, float* grad_v, float* grad_f, float* grad_U,
+                          float* grad_W, float* grad_W_forget, float* grad_b_forget,
+                          float* grad_W_input, int batch, int dim, int rank, float dt,
+                          const float* dt_scales, int dt_scales_count, int steps, int topology,
+                          float R_val, float r_val, float* workspace, long long workspace_floats,
+                          gfn_stream_t stream);
+
+/* ------------------------------------------------------------------------
  * Whole-sequence fused leapfrog recurrence (all tokens x layers x heads in
  * one persistent launch).  The reference has no leapfrog entry here: its
  * launch_recurrent_manifold_fused (gfn/cuda/cuda_kernels.cpp:41-52) is

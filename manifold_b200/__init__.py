@@ -11,7 +11,7 @@ from .model import Manifold, ImplicitReadout
 from .model import Manifold as GFN
 from .layers import MLayer, ParallelMLayer, RiemannianGating
 from .layers import MLayer as GLayer
-from .geometry import LowRankChristoffel, ReactiveChristoffel
+from .geometry import LowRankChristoffel, ReactiveChristoffel, ToroidalChristoffel
 from .integrators import LeapfrogIntegrator
 from .embeddings import FunctionalEmbedding, ImplicitEmbedding, SineLayer
 from .scan import parallel_scan
@@ -20,6 +20,6 @@ from . import cuda
 INTEGRATORS = {"leapfrog": LeapfrogIntegrator}
 
 __all__ = ["GFN", "Manifold", "GLayer", "MLayer", "ParallelMLayer", "RiemannianGating",
-           "LowRankChristoffel", "ReactiveChristoffel", "LeapfrogIntegrator",
+           "LowRankChristoffel", "ReactiveChristoffel", "ToroidalChristoffel", "LeapfrogIntegrator",
            "FunctionalEmbedding", "ImplicitEmbedding", "SineLayer", "ImplicitReadout",
            "parallel_scan", "GfnError", "INTEGRATORS"]

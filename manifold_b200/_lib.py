@@ -59,6 +59,15 @@ _SIGS = {
     "gfn_parallel_scan_noalloc": [_p, _p, _p, _i, _i, _i, _p],
     "gfn_parallel_layer_scan": [_p, _p, _p, _i, _i, _i, _i, _f, _p],
     "gfn_functional_embedding": [_p, _ll, _p, _p, _p, _p, _p, _p, _p, _p, _p, _f, _i, _p, _p, _p],
+    "gfn_leapfrog_fused_gated": [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _f, _p, _i, _i, _i, _i, _i,
+                                 _i, _f, _f, _f, _p],
+    "gfn_christoffel_torus": [_p, _p, _p, _i, _i, _f, _f, _p],
+    "gfn_christoffel_backward_workspace_floats": [_i, _i, _i],
+    "gfn_christoffel_backward": [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i, _i, _i, _f, _f, _f,
+                                 _i, _f, _f, _p, _ll, _p],
+    "gfn_leapfrog_step_backward_workspace_floats": [_i, _i, _i, _i, _i],
+    "gfn_leapfrog_backward": [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p,
+                              _i, _i, _i, _f, _p, _i, _i, _i, _f, _f, _p, _ll, _p],
 }
 _RESTYPES = {
     "gfn_status_string": ctypes.c_char_p,
@@ -70,6 +79,8 @@ _RESTYPES = {
     "gfn_leapfrog_backward_workspace_floats": ctypes.c_longlong,
     "gfn_leapfrog_layered_pack_floats": ctypes.c_longlong,
     "gfn_leapfrog_layered_workspace_floats": ctypes.c_longlong,
+    "gfn_christoffel_backward_workspace_floats": ctypes.c_longlong,
+    "gfn_leapfrog_step_backward_workspace_floats": ctypes.c_longlong,
 }
 
 EXPORTED = tuple(_SIGS)

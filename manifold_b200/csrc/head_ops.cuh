@@ -1,0 +1,649 @@
+// Single-head operators of the gfn.cuda boundary, forward and backward, one
+// warp per batch row:
+//   Gamma only     : Christoffel contraction (low-rank, or toroidal)
+//   leapfrog       : `steps` kick-drift-kick steps with implicit friction
+//   backward       : reverse replay of the same steps (recomputes each step's
+//                    forward from the stored step inputs), per-row gradients
+//                    plus per-row "signals" whose batch sums are the weight
+//                    gradients (summed by outer_sum_kernel in a fixed order:
+//                    deterministic, no atomics).
+//
+// Semantics:
+//   low-rank Gamma  gfn/geometry/lowrank.py:93-98,125-127:
+//       p = vU, s = 1/((1 + |p|) + 1e-6), Gamma = 20 tanh(((p^2 s) W^T) / 20)
+//   toroidal Gamma  gfn/geometry/toroidal.py:70-108 (pairs (th, ph) = (x_i, x_i+1)):
+//       Gamma_i   = 0.05 (R + r cos th) sin th / r * v_ph^2
+//       Gamma_i+1 = 0.05 * 2 * (-(r sin th) / max(R + r cos th, 1e-6)) v_ph v_th
+//   friction        mu = 5 sigmoid((feat(x) Wf^T + bf) + F Wi^T), feat = x, or
+//                   [sin x, cos x] on the torus (gfn/geometry/lowrank.py:114-123,
+//                   gfn/integrators/symplectic/leapfrog.py:72-81,100-111)
+//   leapfrog        gfn/integrators/symplectic/leapfrog.py:50-114:
+//       h = dt dt_scale / 2; v' = (v + h (F - Gamma(v, x))) / (1 + h mu(x));
+//       x' = x + 2h v' (torus: remainder 2*pi, gfn/geometry/boundaries.py:4-17);
+//       v'' = (v' + h (F - Gamma(v', x'))) / (1 + h mu(x'))
+//
+// Lane l of the row's warp holds elements k = l + 32 e (e < EPL) of every
+// row vector; row-vector x matrix products go through a per-warp shared row
+// buffer (broadcast reads) and weights stored [out][in] with a padded row
+// stride (in + 1) so both the product and its transpose are bank-conflict
+// free.
+#pragma once
+#include "common.cuh"
+
+namespace gfn {
+namespace hops {
+
+constexpr int WARPS = 8;                 // rows per block
+constexpr float kTwoPi = 6.28318530718f; // float32 of 2 * 3.14159265359 (boundaries.py:13-14)
+constexpr float kTorusScale = 0.05f;     // toroidal.py:107
+
+struct Params {
+  const float* x;   // [B, hd]
+  const float* v;   // [B, hd]
+  const float* f;   // [B, hd] or null (zero force)
+  const float* U;   // [hd, RK] (low-rank topology only)
+  const float* W;   // [hd, RK]
+  const float* Wf;  // [hd, fin] or null (no friction)
+  const float* bf;  // [hd] or null
+  const float* Wi;  // [hd, hd] or null (no input gate)
+  const float* dt_scale;  // null, 1 or B values
+  int dt_scale_n;
+  float dt;
+  int steps;
+  int topo;
+  float R, r;
+  int B, hd, fin;
+  float* x_out;
+  float* v_out;
+  float* gamma_out;      // gamma-only mode
+  const float* gx_in;    // backward: upstream gradients (null: zero)
+  const float* gv_in;
+  const float* gg_in;    // christoffel backward: dL/dGamma
+  float* gx;
+  float* gv;
+  float* gf;
+  float* ws;             // states [steps][B][2 hd] then signals [steps][2][B][SR]
+};
+
+// Shared-memory layout (floats).
+struct Smem {
+  int U, W, Wf, ldf, Wi, ldi, bf, rb, rbn, total;
+};
+
+__host__ __device__ inline Smem smem_layout(int hd, int RK, int fin, bool fric, bool igate) {
+  Smem s;
+  s.U = 0;
+  s.W = s.U + hd * RK;
+  s.ldf = fin + 1;
+  s.Wf = s.W + hd * RK;
+  s.ldi = hd + 1;
+  s.Wi = s.Wf + (fric ? hd * s.ldf : 0);
+  s.bf = s.Wi + (igate ? hd * s.ldi : 0);
+  s.rbn = fin > hd ? fin : hd;
+  s.rb = s.bf + hd;
+  s.total = s.rb + WARPS * s.rbn;
+  return s;
+}
+
+// Signal record of one (step, half, row): [v point | dL/dpre | dL/dz | feat | e | dL/dp].
+__host__ __device__ inline int signal_floats(int hd, int fin, int RK) { return 3 * hd + fin + 2 * RK; }
+
+template <int EPL>
+GFN_DEV void row_load(float (&a)[EPL], const float* __restrict__ src, int hd, int lane) {
+#pragma unroll
+  for (int e = 0; e < EPL; ++e) {
+    const int k = lane + 32 * e;
+    a[e] = (src != nullptr && k < hd) ? src[k] : 0.f;
+  }
+}
+
+template <int EPL>
+GFN_DEV void row_store(const float (&a)[EPL], float* __restrict__ dst, int hd, int lane) {
+#pragma unroll
+  for (int e = 0; e < EPL; ++e) {
+    const int k = lane + 32 * e;
+    if (k < hd) dst[k] = a[e];
+  }
+}
+
+// out[j] = sum_k rb[k] M[j * ld + k] for the lane's outputs j (rb broadcast).
+template <int EPL>
+GFN_DEV void row_times_mT(const float* __restrict__ rb, const float* __restrict__ M, int ld, int nin,
+                          int hd, int lane, float (&out)[EPL]) {
+#pragma unroll
+  for (int e = 0; e < EPL; ++e) {
+    const int j = lane + 32 * e;
+    float s0 = 0.f, s1 = 0.f;
+    if (j < hd) {
+      const float* m = M + j * ld;
+      int k = 0;
+      for (; k + 1 < nin; k += 2) {
+        s0 = fmaf(rb[k], m[k], s0);
+        s1 = fmaf(rb[k + 1], m[k + 1], s1);
+      }
+      if (k < nin) s0 = fmaf(rb[k], m[k], s0);
+    }
+    out[e] = s0 + s1;
+  }
+}
+
+// out[k] += sum_j rb[j] M[j * ld + k] for k = lane + 32 e (+ koff), k < nout.
+template <int EPL>
+GFN_DEV void row_times_m(const float* __restrict__ rb, const float* __restrict__ M, int ld, int nrows,
+                         int nout, int koff, int lane, float (&out)[EPL]) {
+#pragma unroll
+  for (int e = 0; e < EPL; ++e) {
+    const int k = koff + lane + 32 * e;
+    if (k < koff + nout) {
+      float s0 = 0.f, s1 = 0.f;
+      int j = 0;
+      for (; j + 1 < nrows; j += 2) {
+        s0 = fmaf(rb[j], M[j * ld + k], s0);
+        s1 = fmaf(rb[j + 1], M[(j + 1) * ld + k], s1);
+      }
+      if (j < nrows) s0 = fmaf(rb[j], M[j * ld + k], s0);
+      out[e] += s0 + s1;
+    }
+  }
+}
+
+GFN_DEV float torus_wrap(float x) {
+  // torch.remainder for float: fmod, then shift into the divisor's sign
+  float m = fmodf(x, kTwoPi);
+  if (m != 0.f && (m < 0.f)) m += kTwoPi;
+  return m;
+}
+
+// Writes the friction features of x into the warp's row buffer.
+template <int EPL>
+GFN_DEV void put_features(const float (&x)[EPL], float* rb, int hd, int topo, int lane) {
+  __syncwarp();
+#pragma unroll
+  for (int e = 0; e < EPL; ++e) {
+    const int k = lane + 32 * e;
+    if (k < hd) {
+      if (topo) {
+        rb[k] = sinf(x[e]);
+        rb[hd + k] = cosf(x[e]);
+      } else {
+        rb[k] = x[e];
+      }
+    }
+  }
+  __syncwarp();
+}
+
+// sigma = sigmoid((feat Wf^T + bf) + zin); mu = 5 sigma.
+template <int EPL>
+GFN_DEV void friction(const float (&x)[EPL], const float (&zin)[EPL], const float* sm, const Smem& L,
+                      float* rb, int hd, int fin, int topo, int lane, float (&sg)[EPL]) {
+  put_features<EPL>(x, rb, hd, topo, lane);
+  float z[EPL];
+  row_times_mT<EPL>(rb, sm + L.Wf, L.ldf, fin, hd, lane, z);
+#pragma unroll
+  for (int e = 0; e < EPL; ++e) {
+    const int j = lane + 32 * e;
+    sg[e] = j < hd ? sigmoid_f((z[e] + sm[L.bf + j]) + zin[e]) : 0.f;
+  }
+}
+
+// Low-rank Gamma with the intermediates the backward needs.
+template <int RK, int EPL>
+GFN_DEV void gamma_lowrank(const float (&v)[EPL], const float* __restrict__ U, const float* __restrict__ W,
+                           int hd, int lane, float (&p)[RK], float& s, float (&t)[EPL], float (&g)[EPL]) {
+#pragma unroll
+  for (int q = 0; q < RK; ++q) {
+    float a = 0.f;
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) {
+      const int k = lane + 32 * e;
+      if (k < hd) a = fmaf(v[e], U[k * RK + q], a);
+    }
+    p[q] = warp_sum(a);
+  }
+  float ss = 0.f;
+#pragma unroll
+  for (int q = 0; q < RK; ++q) ss = fmaf(p[q], p[q], ss);
+  s = 1.f / ((1.f + sqrtf(ss)) + 1e-6f);
+#pragma unroll
+  for (int e = 0; e < EPL; ++e) {
+    const int k = lane + 32 * e;
+    float pre = 0.f;
+    if (k < hd) {
+#pragma unroll
+      for (int q = 0; q < RK; ++q) pre = fmaf((p[q] * p[q]) * s, W[k * RK + q], pre);
+    }
+    t[e] = tanhf(pre / 20.f);
+    g[e] = 20.f * t[e];
+  }
+}
+
+// Toroidal Gamma: lane element k pairs with k ^ 1 (same e, neighbouring lane).
+template <int EPL>
+GFN_DEV void gamma_torus(const float (&v)[EPL], const float (&x)[EPL], int hd, float R, float r, int lane,
+                         float (&g)[EPL]) {
+#pragma unroll
+  for (int e = 0; e < EPL; ++e) {
+    const int k = lane + 32 * e;
+    const float vo = __shfl_xor_sync(0xffffffffu, v[e], 1);
+    const float xo = __shfl_xor_sync(0xffffffffu, x[e], 1);
+    const bool even = (k & 1) == 0;
+    const bool paired = (k | 1) < hd;
+    const float th = even ? x[e] : xo;
+    const float vth = even ? v[e] : vo;
+    const float vph = even ? vo : v[e];
+    const float st = sinf(th), ct = cosf(th);
+    const float denom = R + r * ct;
+    float gm;
+    if (even) {
+      const float term = denom * st / r;
+      gm = term * (vph * vph);
+    } else {
+      const float ds = fmaxf(denom, 1e-6f);
+      const float term = -(r * st) / ds;
+      gm = 2.f * term * vph * vth;
+    }
+    g[e] = (paired && k < hd) ? gm * kTorusScale : 0.f;
+  }
+}
+
+// Backward of the toroidal Gamma: gv += dGamma/dv^T gg, gx += dGamma/dx^T gg.
+template <int EPL>
+GFN_DEV void gamma_torus_bwd(const float (&v)[EPL], const float (&x)[EPL], const float (&gg)[EPL], int hd,
+                             float R, float r, int lane, float (&gv)[EPL], float (&gx)[EPL]) {
+#pragma unroll
+  for (int e = 0; e < EPL; ++e) {
+    const int k = lane + 32 * e;
+    const float vo = __shfl_xor_sync(0xffffffffu, v[e], 1);
+    const float xo = __shfl_xor_sync(0xffffffffu, x[e], 1);
+    const float go = __shfl_xor_sync(0xffffffffu, gg[e], 1);
+    const bool even = (k & 1) == 0;
+    if (!((k | 1) < hd) || k >= hd) continue;
+    const float th = even ? x[e] : xo;
+    const float vth = even ? v[e] : vo;
+    const float vph = even ? vo : v[e];
+    const float gi = (even ? gg[e] : go) * kTorusScale;   // upstream of Gamma_i (scaled)
+    const float gi1 = (even ? go : gg[e]) * kTorusScale;  // upstream of Gamma_i+1
+    const float st = sinf(th), ct = cosf(th);
+    const float denom = R + r * ct;
+    const float A = denom * st / r;
+    const bool live = denom >= 1e-6f;
+    const float ds = fmaxf(denom, 1e-6f);
+    const float Bc = -(r * st) / ds;
+    if (even) {
+      // th and v_th live here
+      const float dA = (-r * st * st + denom * ct) / r;
+      const float dB = -(r * ct) / ds - (live ? (r * st) * (r * st) / (ds * ds) : 0.f);
+      gx[e] += gi * (vph * vph) * dA + gi1 * 2.f * vph * vth * dB;
+      gv[e] += gi1 * 2.f * Bc * vph;
+    } else {
+      gv[e] += gi * A * 2.f * vph + gi1 * 2.f * Bc * vth;
+    }
+  }
+}
+
+// Backward of the low-rank Gamma given dL/dGamma (gg).  Adds to gv; returns
+// the signals gpre (dL/dpre, per element) and e, gp (per rank).
+template <int RK, int EPL>
+GFN_DEV void gamma_lowrank_bwd(const float (&p)[RK], float s, const float (&t)[EPL], const float (&gg)[EPL],
+                               const float* __restrict__ U, const float* __restrict__ W, int hd, int lane,
+                               float (&gv)[EPL], float (&gpre)[EPL], float (&ev)[RK], float (&gp)[RK]) {
+  float ge[RK];
+#pragma unroll
+  for (int e = 0; e < EPL; ++e) gpre[e] = gg[e] * (1.f - t[e] * t[e]);
+#pragma unroll
+  for (int q = 0; q < RK; ++q) {
+    float a = 0.f;
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) {
+      const int k = lane + 32 * e;
+      if (k < hd) a = fmaf(gpre[e], W[k * RK + q], a);
+    }
+    ge[q] = warp_sum(a);
+  }
+  float ss = 0.f, S2 = 0.f;
+#pragma unroll
+  for (int q = 0; q < RK; ++q) {
+    ss = fmaf(p[q], p[q], ss);
+    S2 = fmaf(ge[q], p[q] * p[q], S2);
+  }
+  const float n = sqrtf(ss);
+  const float inv_n = n > 0.f ? 1.f / n : 0.f;
+#pragma unroll
+  for (int q = 0; q < RK; ++q) {
+    ev[q] = (p[q] * p[q]) * s;
+    gp[q] = 2.f * p[q] * s * ge[q] - s * s * S2 * p[q] * inv_n;
+  }
+#pragma unroll
+  for (int e = 0; e < EPL; ++e) {
+    const int k = lane + 32 * e;
+    if (k < hd) {
+      float a = 0.f;
+#pragma unroll
+      for (int q = 0; q < RK; ++q) a = fmaf(gp[q], U[k * RK + q], a);
+      gv[e] += a;
+    }
+  }
+}
+
+// Backward of the friction gate given dL/dz (gz) at feature point x:
+// gx += dz/dx^T gz, gF += Wi^T gz; writes the features into the row buffer
+// (and returns with them there for the signal record).
+template <int EPL>
+GFN_DEV void friction_bwd(const float (&x)[EPL], const float (&gz)[EPL], const float* sm, const Smem& L, float* rb,
+                          int hd, int fin, int topo, bool igate, int lane, float (&gx)[EPL], float (&gF)[EPL]) {
+  __syncwarp();
+  row_store<EPL>(gz, rb, hd, lane);
+  __syncwarp();
+  float gfe[EPL], gfe2[EPL];
+#pragma unroll
+  for (int e = 0; e < EPL; ++e) gfe[e] = gfe2[e] = 0.f;
+  row_times_m<EPL>(rb, sm + L.Wf, L.ldf, hd, hd, 0, lane, gfe);
+  if (topo) {
+    row_times_m<EPL>(rb, sm + L.Wf, L.ldf, hd, hd, hd, lane, gfe2);
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) gx[e] += gfe[e] * cosf(x[e]) - gfe2[e] * sinf(x[e]);
+  } else {
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) gx[e] += gfe[e];
+  }
+  if (igate) row_times_m<EPL>(rb, sm + L.Wi, L.ldi, hd, hd, 0, lane, gF);
+}
+
+template <int RK>
+GFN_DEV void stage_weights(const Params& a, float* sm, const Smem& L, bool fric, bool igate) {
+  const int hd = a.hd;
+  if (a.U) {
+    for (int i = threadIdx.x; i < hd * RK; i += blockDim.x) {
+      sm[L.U + i] = a.U[i];
+      sm[L.W + i] = a.W[i];
+    }
+  }
+  if (fric) {
+    for (int i = threadIdx.x; i < hd * a.fin; i += blockDim.x) {
+      const int j = i / a.fin, k = i - j * a.fin;
+      sm[L.Wf + j * L.ldf + k] = a.Wf[i];
+    }
+    for (int i = threadIdx.x; i < hd; i += blockDim.x) sm[L.bf + i] = a.bf ? a.bf[i] : 0.f;
+  } else {
+    for (int i = threadIdx.x; i < hd; i += blockDim.x) sm[L.bf + i] = 0.f;
+  }
+  if (igate) {
+    for (int i = threadIdx.x; i < hd * hd; i += blockDim.x) {
+      const int j = i / hd, k = i - j * hd;
+      sm[L.Wi + j * L.ldi + k] = a.Wi[i];
+    }
+  }
+  __syncthreads();
+}
+
+GFN_DEV float row_dt_scale(const Params& a, int row) {
+  if (!a.dt_scale) return 1.f;
+  return a.dt_scale[a.dt_scale_n == 1 ? 0 : row];
+}
+
+// zin = F Wi^T (constant over the steps: the force is).
+template <int EPL>
+GFN_DEV void input_gate(const float (&F)[EPL], const float* sm, const Smem& L, float* rb, int hd, bool igate,
+                        int lane, float (&zin)[EPL]) {
+  if (!igate) {
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) zin[e] = 0.f;
+    return;
+  }
+  __syncwarp();
+  row_store<EPL>(F, rb, hd, lane);
+  __syncwarp();
+  row_times_mT<EPL>(rb, sm + L.Wi, L.ldi, hd, hd, lane, zin);
+}
+
+// Forward: leapfrog steps (steps >= 1), or Gamma only (gamma_out set).
+template <int RK, int EPL>
+__global__ void __launch_bounds__(WARPS * 32) head_fwd_kernel(const Params a) {
+  extern __shared__ __align__(16) float sm[];
+  const bool fric = a.Wf != nullptr, igate = a.Wi != nullptr;
+  const Smem L = smem_layout(a.hd, RK, a.fin, fric, igate);
+  stage_weights<RK>(a, sm, L, fric, igate);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row = blockIdx.x * WARPS + warp;
+  if (row >= a.B) return;
+  const int hd = a.hd;
+  float* rb = sm + L.rb + warp * L.rbn;
+  const long long off = (long long)row * hd;
+  float x[EPL], v[EPL], F[EPL], zin[EPL], sg[EPL], g[EPL], t[EPL], p[RK], s;
+  row_load<EPL>(x, a.x ? a.x + off : nullptr, hd, lane);
+  row_load<EPL>(v, a.v + off, hd, lane);
+  if (a.gamma_out) {
+    if (a.topo) gamma_torus<EPL>(v, x, hd, a.R, a.r, lane, g);
+    else gamma_lowrank<RK, EPL>(v, sm + L.U, sm + L.W, hd, lane, p, s, t, g);
+    row_store<EPL>(g, a.gamma_out + off, hd, lane);
+    return;
+  }
+  row_load<EPL>(F, a.f ? a.f + off : nullptr, hd, lane);
+  input_gate<EPL>(F, sm, L, rb, hd, igate, lane, zin);
+  const float eff = a.dt * row_dt_scale(a, row);
+  const float h = 0.5f * eff;
+  for (int st = 0; st < a.steps; ++st) {
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      if (fric) friction<EPL>(x, zin, sm, L, rb, hd, a.fin, a.topo, lane, sg);
+      if (a.topo) gamma_torus<EPL>(v, x, hd, a.R, a.r, lane, g);
+      else gamma_lowrank<RK, EPL>(v, sm + L.U, sm + L.W, hd, lane, p, s, t, g);
+#pragma unroll
+      for (int e = 0; e < EPL; ++e) {
+        const float mu = fric ? sg[e] * 5.f : 0.f;
+        v[e] = (v[e] + h * (F[e] - g[e])) / (1.f + h * mu);
+        if (half == 0) {
+          x[e] = x[e] + eff * v[e];
+          if (a.topo) x[e] = torus_wrap(x[e]);
+        }
+      }
+    }
+  }
+  row_store<EPL>(x, a.x_out + off, hd, lane);
+  row_store<EPL>(v, a.v_out + off, hd, lane);
+}
+
+// Christoffel backward (low-rank): gv = dGamma/dv^T gg; signals per row
+// [gpre hd | e RK | gp RK] for the U / W sums.
+template <int RK, int EPL>
+__global__ void __launch_bounds__(WARPS * 32) gamma_bwd_kernel(const Params a) {
+  extern __shared__ __align__(16) float sm[];
+  const Smem L = smem_layout(a.hd, RK, a.fin, false, false);
+  stage_weights<RK>(a, sm, L, false, false);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row = blockIdx.x * WARPS + warp;
+  if (row >= a.B) return;
+  const int hd = a.hd;
+  const long long off = (long long)row * hd;
+  float v[EPL], gg[EPL], gv[EPL], g[EPL], t[EPL], gpre[EPL], p[RK], ev[RK], gp[RK], s;
+  row_load<EPL>(v, a.v + off, hd, lane);
+  row_load<EPL>(gg, a.gg_in + off, hd, lane);
+#pragma unroll
+  for (int e = 0; e < EPL; ++e) gv[e] = 0.f;
+  if (a.topo) {
+    float x[EPL], gx[EPL];
+    row_load<EPL>(x, a.x + off, hd, lane);
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) gx[e] = 0.f;
+    gamma_torus_bwd<EPL>(v, x, gg, hd, a.R, a.r, lane, gv, gx);
+    row_store<EPL>(gv, a.gv + off, hd, lane);
+    if (a.gx) row_store<EPL>(gx, a.gx + off, hd, lane);
+    return;
+  }
+  gamma_lowrank<RK, EPL>(v, sm + L.U, sm + L.W, hd, lane, p, s, t, g);
+  gamma_lowrank_bwd<RK, EPL>(p, s, t, gg, sm + L.U, sm + L.W, hd, lane, gv, gpre, ev, gp);
+  row_store<EPL>(gv, a.gv + off, hd, lane);
+  if (a.gx) {
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) g[e] = 0.f;
+    row_store<EPL>(g, a.gx + off, hd, lane);
+  }
+  float* rec = a.ws + (long long)row * (hd + 2 * RK);
+  row_store<EPL>(gpre, rec, hd, lane);
+  if (lane < RK) {
+#pragma unroll
+    for (int q = 0; q < RK; ++q)
+      if (q == lane) {
+        rec[hd + q] = ev[q];
+        rec[hd + RK + q] = gp[q];
+      }
+  }
+}
+
+// Writes one signal record: [v point | gpre | gz | feat | e | gp].
+template <int RK, int EPL>
+GFN_DEV void put_signal(float* rec, const float (&vpt)[EPL], const float (&gpre)[EPL], const float (&gz)[EPL],
+                        const float* rb, const float (&ev)[RK], const float (&gp)[RK], int hd, int fin, int lane) {
+  row_store<EPL>(vpt, rec, hd, lane);
+  row_store<EPL>(gpre, rec + hd, hd, lane);
+  row_store<EPL>(gz, rec + 2 * hd, hd, lane);
+  __syncwarp();
+  for (int k = lane; k < fin; k += 32) rec[3 * hd + k] = rb[k];
+#pragma unroll
+  for (int q = 0; q < RK; ++q)
+    if (q == lane) {
+      rec[3 * hd + fin + q] = ev[q];
+      rec[3 * hd + fin + RK + q] = gp[q];
+    }
+}
+
+// Leapfrog backward (reverse replay).  Forward states of each step go to the
+// workspace first; each step is then recomputed from its stored input.
+template <int RK, int EPL>
+__global__ void __launch_bounds__(WARPS * 32) head_bwd_kernel(const Params a) {
+  extern __shared__ __align__(16) float sm[];
+  const bool fric = a.Wf != nullptr, igate = a.Wi != nullptr;
+  const Smem L = smem_layout(a.hd, RK, a.fin, fric, igate);
+  stage_weights<RK>(a, sm, L, fric, igate);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row = blockIdx.x * WARPS + warp;
+  if (row >= a.B) return;
+  const int hd = a.hd, fin = a.fin, B = a.B;
+  const int SR = signal_floats(hd, fin, RK);
+  float* rb = sm + L.rb + warp * L.rbn;
+  const long long off = (long long)row * hd;
+  float* states = a.ws;                                          // [steps][B][2 hd]
+  float* signals = a.ws + (long long)a.steps * B * 2 * hd;       // [steps][2][B][SR]
+  float x[EPL], v[EPL], F[EPL], zin[EPL];
+  row_load<EPL>(x, a.x + off, hd, lane);
+  row_load<EPL>(v, a.v + off, hd, lane);
+  row_load<EPL>(F, a.f ? a.f + off : nullptr, hd, lane);
+  input_gate<EPL>(F, sm, L, rb, hd, igate, lane, zin);
+  const float eff = a.dt * row_dt_scale(a, row);
+  const float h = 0.5f * eff;
+  // forward, storing each step's input
+  for (int st = 0; st < a.steps; ++st) {
+    float* sp = states + ((long long)st * B + row) * 2 * hd;
+    row_store<EPL>(x, sp, hd, lane);
+    row_store<EPL>(v, sp + hd, hd, lane);
+    float sg[EPL], g[EPL], t[EPL], p[RK], s;
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      if (fric) friction<EPL>(x, zin, sm, L, rb, hd, fin, a.topo, lane, sg);
+      if (a.topo) gamma_torus<EPL>(v, x, hd, a.R, a.r, lane, g);
+      else gamma_lowrank<RK, EPL>(v, sm + L.U, sm + L.W, hd, lane, p, s, t, g);
+#pragma unroll
+      for (int e = 0; e < EPL; ++e) {
+        const float mu = fric ? sg[e] * 5.f : 0.f;
+        v[e] = (v[e] + h * (F[e] - g[e])) / (1.f + h * mu);
+        if (half == 0) {
+          x[e] = x[e] + eff * v[e];
+          if (a.topo) x[e] = torus_wrap(x[e]);
+        }
+      }
+    }
+  }
+  float gx[EPL], gv[EPL], gF[EPL];
+  row_load<EPL>(gx, a.gx_in ? a.gx_in + off : nullptr, hd, lane);
+  row_load<EPL>(gv, a.gv_in ? a.gv_in + off : nullptr, hd, lane);
+#pragma unroll
+  for (int e = 0; e < EPL; ++e) gF[e] = 0.f;
+  for (int st = a.steps - 1; st >= 0; --st) {
+    const float* sp = states + ((long long)st * B + row) * 2 * hd;
+    float xs[2][EPL], vs[3][EPL], sgs[2][EPL], ts[2][EPL], ps[2][RK], ss[2];
+    row_load<EPL>(xs[0], sp, hd, lane);
+    row_load<EPL>(vs[0], sp + hd, hd, lane);
+    // recompute both kicks
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      float g[EPL];
+      if (fric) friction<EPL>(xs[half], zin, sm, L, rb, hd, fin, a.topo, lane, sgs[half]);
+      else {
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) sgs[half][e] = 0.f;
+      }
+      if (a.topo) gamma_torus<EPL>(vs[half], xs[half], hd, a.R, a.r, lane, g);
+      else gamma_lowrank<RK, EPL>(vs[half], sm + L.U, sm + L.W, hd, lane, ps[half], ss[half], ts[half], g);
+#pragma unroll
+      for (int e = 0; e < EPL; ++e) {
+        const float mu = sgs[half][e] * 5.f;
+        vs[half + 1][e] = (vs[half][e] + h * (F[e] - g[e])) / (1.f + h * mu);
+        if (half == 0) {
+          float xn = xs[0][e] + eff * vs[1][e];
+          if (a.topo) xn = torus_wrap(xn);
+          xs[1][e] = xn;
+        }
+      }
+    }
+    // reverse: second kick (half 1), drift, first kick (half 0)
+#pragma unroll
+    for (int half = 1; half >= 0; --half) {
+      float ga[EPL], gz[EPL], gg[EPL], gvn[EPL], gpre[EPL], ev[RK], gp[RK];
+#pragma unroll
+      for (int e = 0; e < EPL; ++e) {
+        const float sgv = sgs[half][e];
+        const float den = 1.f + h * (sgv * 5.f);
+        ga[e] = gv[e] / den;
+        gz[e] = fric ? (-(gv[e] * vs[half + 1][e]) / den) * h * 5.f * sgv * (1.f - sgv) : 0.f;
+        gF[e] += h * ga[e];
+        gg[e] = -h * ga[e];
+        gvn[e] = ga[e];
+        gpre[e] = 0.f;
+      }
+#pragma unroll
+      for (int q = 0; q < RK; ++q) ev[q] = gp[q] = 0.f;
+      if (a.topo) gamma_torus_bwd<EPL>(vs[half], xs[half], gg, hd, a.R, a.r, lane, gvn, gx);
+      else gamma_lowrank_bwd<RK, EPL>(ps[half], ss[half], ts[half], gg, sm + L.U, sm + L.W, hd, lane, gvn, gpre,
+                                      ev, gp);
+      if (fric) friction_bwd<EPL>(xs[half], gz, sm, L, rb, hd, fin, a.topo, igate, lane, gx, gF);
+      if (fric) put_features<EPL>(xs[half], rb, hd, a.topo, lane);
+      float* rec = signals + (((long long)st * 2 + half) * B + row) * SR;
+      put_signal<RK, EPL>(rec, vs[half], gpre, gz, rb, ev, gp, hd, fric ? fin : 0, lane);
+      if (half == 1) {
+        // drift x1 = x0 + eff v1 (the wrap passes the gradient through)
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) gv[e] = gvn[e] + eff * gx[e];
+      } else {
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) gv[e] = gvn[e];
+      }
+    }
+  }
+  row_store<EPL>(gx, a.gx + off, hd, lane);
+  row_store<EPL>(gv, a.gv + off, hd, lane);
+  if (a.gf) row_store<EPL>(gF, a.gf + off, hd, lane);
+}
+
+// out[i * J + j] = sum_n A[n * sA + i] * Bm[(n % modB) * sB + j] (Bm null: 1),
+// n ascending: a fixed summation order.
+__global__ void outer_sum_kernel(const float* __restrict__ A, long long sA, const float* __restrict__ Bm,
+                                 long long sB, long long modB, int I, int J, long long N, float* __restrict__ out) {
+  const int o = blockIdx.x * blockDim.x + threadIdx.x;
+  if (o >= I * J) return;
+  const int i = o / J, j = o - i * J;
+  float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+  long long n = 0;
+  auto bval = [&](long long m) { return Bm ? Bm[(m % modB) * sB + j] : 1.f; };
+  for (; n + 3 < N; n += 4) {
+    s0 = fmaf(A[n * sA + i], bval(n), s0);
+    s1 = fmaf(A[(n + 1) * sA + i], bval(n + 1), s1);
+    s2 = fmaf(A[(n + 2) * sA + i], bval(n + 2), s2);
+    s3 = fmaf(A[(n + 3) * sA + i], bval(n + 3), s3);
+  }
+  for (; n < N; ++n) s0 = fmaf(A[n * sA + i], bval(n), s0);
+  out[o] = (s0 + s1) + (s2 + s3);
+}
+
+}  // namespace hops
+}  // namespace gfn

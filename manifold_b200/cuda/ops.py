@@ -24,12 +24,37 @@ def _stream(t):
     return _lib.stream_of(t.device)
 
 
+def _grad_wanted(*ts):
+    return torch.is_grad_enabled() and any(t is not None and t.requires_grad for t in ts)
+
+
 def christoffel_fused(v, U, W, x=None, V_w=None, plasticity=0.0, sing_thresh=1.0,
                       sing_strength=1.0, topology=0, R=2.0, r=1.0):
-    """Gamma(v) for one head (gfn/cuda/ops.py:88-118; gfn/geometry/lowrank.py:93-98,125-127)."""
-    require_cuda(v, U, W)
-    v, U, W = _f32c(v, "v"), _f32c(U, "U"), _f32c(W, "W")
+    """Gamma(v) for one head (gfn/cuda/ops.py:88-118).  topology 0: the low-rank
+    form (gfn/geometry/lowrank.py:93-98,125-127); topology 1: the toroidal form
+    (gfn/geometry/toroidal.py:70-108, needs x).  Differentiable when an input
+    requires grad (backward: christoffel_backward)."""
+    if _grad_wanted(v, U, W, x):
+        from .autograd import christoffel_fused_autograd
+        return christoffel_fused_autograd(v, U, W, x, V_w, plasticity, sing_thresh, sing_strength,
+                                          topology, R, r)
+    return _christoffel_forward(v, U, W, x, V_w, plasticity, sing_thresh, sing_strength, topology, R, r)
+
+
+def _christoffel_forward(v, U, W, x, V_w, plasticity, sing_thresh, sing_strength, topology, R, r):
+    require_cuda(v, U, W, x)
+    v = _f32c(v, "v")
     gamma = torch.empty_like(v)
+    if topology == 1:
+        if x is None:
+            raise GfnError("christoffel_fused: the toroidal form needs x")
+        if V_w is not None or plasticity != 0.0:
+            raise GfnError("christoffel_fused: active inference is not implemented on this build")
+        x = _f32c(x, "x")
+        call("gfn_christoffel_torus", ptr(v), ptr(x), ptr(gamma), v.shape[0], v.shape[1], float(R),
+             float(r), _stream(v))
+        return gamma
+    U, W = _f32c(U, "U"), _f32c(W, "W")
     call("gfn_christoffel_fused", ptr(v), ptr(U), ptr(W), ptr(gamma), None,
          ptr(V_w) if V_w is not None else None, v.shape[0], v.shape[1], U.shape[1],
          float(plasticity), float(sing_thresh), float(sing_strength), int(topology), float(R),
@@ -37,23 +62,134 @@ def christoffel_fused(v, U, W, x=None, V_w=None, plasticity=0.0, sing_thresh=1.0
     return gamma
 
 
-def leapfrog_fused(x, v, f, U, W, dt, dt_scale, steps, topology=0, Wf=None, bf=None,
-                   plasticity=0.0, R=2.0, r=1.0):
-    """One head's leapfrog, `steps` times (gfn/cuda/ops.py:131-182;
-    gfn/integrators/symplectic/leapfrog.py:50-114).  Returns (x_new, v_new)."""
-    require_cuda(x, v, f, U, W, Wf, bf)
-    x, v, U, W = _f32c(x, "x"), _f32c(v, "v"), _f32c(U, "U"), _f32c(W, "W")
-    f = _f32c(f, "f")
-    Wf, bf = _f32c(Wf, "Wf"), _f32c(bf, "bf")
+def reactive_christoffel(v, U, W, x=None, V_w=None, plasticity=0.0, sing_thresh=1.0,
+                         sing_strength=1.0, topology=0, R=2.0, r=1.0):
+    """gfn/cuda/ops.py:120-129: the reactive geometry.  With plasticity 0 and
+    no singularity potential (active inference off) it is christoffel_fused;
+    the active-inference terms raise."""
+    if plasticity != 0.0 or V_w is not None:
+        raise GfnError("reactive_christoffel: plasticity / singularities are not implemented on this build")
+    return christoffel_fused(v, U, W, x, None, 0.0, sing_thresh, sing_strength, topology, R, r)
+
+
+def christoffel_backward(grad_gamma, v, U, W, x=None, V_w=None, plasticity=0.0, sing_thresh=1.0,
+                         sing_strength=1.0, topology=0, R=2.0, r=1.0):
+    """Backward of christoffel_fused (the gfn_cuda.christoffel_backward binding,
+    gfn/cuda/cuda_kernels.cpp:139-148).  Returns [grad_v, grad_U, grad_W,
+    grad_x, grad_V_w]; grad_x is None without x, grad_V_w always None."""
+    require_cuda(grad_gamma, v, U, W, x)
+    gg, v = _f32c(grad_gamma, "grad_gamma"), _f32c(v, "v")
+    B, d = v.shape
+    dev = v.device
+    grad_v = torch.empty_like(v)
+    grad_x = torch.empty_like(v) if x is not None else None
+    if topology == 1:
+        if x is None:
+            raise GfnError("christoffel_backward: the toroidal form needs x")
+        x = _f32c(x, "x")
+        call("gfn_christoffel_backward", ptr(gg), ptr(v), None, None, ptr(x), None, ptr(grad_v), None,
+             None, ptr(grad_x), None, B, d, 4, float(plasticity), float(sing_thresh),
+             float(sing_strength), 1, float(R), float(r), None, 0, _stream(v))
+        gU = torch.zeros_like(U) if U is not None else None
+        gW = torch.zeros_like(W) if W is not None else None
+        return [grad_v, gU, gW, grad_x, None]
+    U, W = _f32c(U, "U"), _f32c(W, "W")
+    rank = U.shape[1]
+    grad_U = torch.empty_like(U)
+    grad_W = torch.empty_like(W)
+    n = _lib.load().gfn_christoffel_backward_workspace_floats(B, d, rank)
+    ws = torch.empty(max(int(n), 1), device=dev, dtype=torch.float32)
+    call("gfn_christoffel_backward", ptr(gg), ptr(v), ptr(U), ptr(W), ptr(x), ptr(V_w), ptr(grad_v),
+         ptr(grad_U), ptr(grad_W), ptr(grad_x), None, B, d, rank, float(plasticity), float(sing_thresh),
+         float(sing_strength), 0, float(R), float(r), ptr(ws), ws.numel(), _stream(v))
+    return [grad_v, grad_U, grad_W, grad_x, None]
+
+
+def _dt_scales(dt_scale, x):
     if not isinstance(dt_scale, torch.Tensor):
         dt_scale = torch.tensor([float(dt_scale)], device=x.device, dtype=torch.float32)
-    dts = dt_scale.reshape(-1).to(torch.float32).contiguous()
+    return dt_scale.reshape(-1).to(device=x.device, dtype=torch.float32).contiguous()
+
+
+def leapfrog_fused(x, v, f, U, W, dt, dt_scale, steps, topology=0, Wf=None, bf=None,
+                   plasticity=0.0, R=2.0, r=1.0, Wi=None):
+    """One head's leapfrog, `steps` times (gfn/cuda/ops.py:131-182;
+    gfn/integrators/symplectic/leapfrog.py:50-114).  Returns (x_new, v_new).
+
+    Wi (an addition to the reference signature): the input gate, friction
+    mu = 5 sigmoid(x Wf^T + bf + f Wi^T) (gfn/geometry/lowrank.py:114-123).
+    topology 1: the toroidal step (Wf [hd, 2 hd] over [sin x, cos x], x wrapped
+    into [0, 2 pi)).  Differentiable when an input requires grad."""
+    if _grad_wanted(x, v, f, U, W, Wf, bf, Wi):
+        from .autograd import leapfrog_fused_autograd
+        return leapfrog_fused_autograd(x, v, f, U, W, dt, dt_scale, steps, topology, Wf, bf,
+                                       plasticity, R, r, Wi)
+    return _leapfrog_forward(x, v, f, U, W, dt, dt_scale, steps, topology, Wf, bf, plasticity, R, r, Wi)
+
+
+def _leapfrog_forward(x, v, f, U, W, dt, dt_scale, steps, topology, Wf, bf, plasticity, R, r, Wi):
+    require_cuda(x, v, f, U, W, Wf, bf, Wi)
+    x, v = _f32c(x, "x"), _f32c(v, "v")
+    f, Wf, bf, Wi = _f32c(f, "f"), _f32c(Wf, "Wf"), _f32c(bf, "bf"), _f32c(Wi, "Wi")
+    U = _f32c(U, "U") if U is not None else None
+    W = _f32c(W, "W") if W is not None else None
+    dts = _dt_scales(dt_scale, x)
     x_new = torch.empty_like(x)
     v_new = torch.empty_like(v)
+    if Wi is not None or topology == 1:
+        rank = U.shape[1] if U is not None else 4
+        call("gfn_leapfrog_fused_gated", ptr(x), ptr(v), ptr(f), ptr(U), ptr(W), ptr(Wf), ptr(bf),
+             ptr(Wi), ptr(x_new), ptr(v_new), float(dt), ptr(dts), dts.numel(), x.shape[0],
+             x.shape[1], rank, int(steps), int(topology), float(plasticity), float(R), float(r),
+             _stream(x))
+        return x_new, v_new
     call("gfn_leapfrog_fused", ptr(x), ptr(v), ptr(f), ptr(U), ptr(W), ptr(Wf), ptr(bf),
          ptr(x_new), ptr(v_new), float(dt), ptr(dts), dts.numel(), x.shape[0], x.shape[1],
          U.shape[1], int(steps), int(topology), float(plasticity), float(R), float(r), _stream(x))
     return x_new, v_new
+
+
+def leapfrog_backward(grad_x_new, grad_v_new, x, v, f, U, W, dt, dt_scale, steps, topology=0,
+                      R=2.0, r=1.0, Wf=None, bf=None, Wi=None):
+    """Backward of leapfrog_fused (the gfn_cuda.leapfrog_backward binding,
+    gfn/cuda/cuda_kernels.cpp:190-196), by reverse replay.  Returns
+    [grad_x, grad_v, grad_f, grad_U, grad_W], followed by grad_Wf, grad_bf
+    when Wf is given and grad_Wi when Wi is given.  dt_scale is a constant."""
+    require_cuda(x, v, f, U, W, Wf, bf, Wi, grad_x_new, grad_v_new)
+    x, v = _f32c(x, "x"), _f32c(v, "v")
+    f, Wf, bf, Wi = _f32c(f, "f"), _f32c(Wf, "Wf"), _f32c(bf, "bf"), _f32c(Wi, "Wi")
+    gxn = _f32c(grad_x_new, "grad_x_new") if grad_x_new is not None else None
+    gvn = _f32c(grad_v_new, "grad_v_new") if grad_v_new is not None else None
+    B, d = x.shape
+    dev = x.device
+    if topology == 0:
+        U, W = _f32c(U, "U"), _f32c(W, "W")
+        rank = U.shape[1]
+    else:
+        rank = 4
+    fin = 2 * d if topology == 1 else d
+    if Wf is not None and bf is None:
+        bf = torch.zeros(d, device=dev, dtype=torch.float32)
+    dts = _dt_scales(dt_scale, x)
+    gx, gv = torch.empty_like(x), torch.empty_like(v)
+    gf = torch.empty_like(x) if f is not None else None
+    gU = torch.empty_like(U) if topology == 0 else None
+    gW = torch.empty_like(W) if topology == 0 else None
+    gWf = torch.empty(d, fin, device=dev, dtype=torch.float32) if Wf is not None else None
+    gbf = torch.empty(d, device=dev, dtype=torch.float32) if Wf is not None else None
+    gWi = torch.empty(d, d, device=dev, dtype=torch.float32) if Wi is not None else None
+    n = _lib.load().gfn_leapfrog_step_backward_workspace_floats(B, d, rank, int(steps), int(topology))
+    ws = torch.empty(max(int(n), 1), device=dev, dtype=torch.float32)
+    call("gfn_leapfrog_backward", ptr(gxn), ptr(gvn), ptr(x), ptr(v), ptr(f), ptr(U), ptr(W), ptr(Wf),
+         ptr(bf), ptr(Wi), ptr(gx), ptr(gv), ptr(gf), ptr(gU), ptr(gW), ptr(gWf), ptr(gbf), ptr(gWi),
+         B, d, rank, float(dt), ptr(dts), dts.numel(), int(steps), int(topology), float(R), float(r),
+         ptr(ws), ws.numel(), _stream(x))
+    out = [gx, gv, gf, gU, gW]
+    if Wf is not None:
+        out += [gWf, gbf]
+    if Wi is not None:
+        out.append(gWi)
+    return out
 
 
 def leapfrog_pack(U_stack, W_stack, Wf_stack, bf_stack, dt_params, mix=None):
@@ -199,6 +335,70 @@ def leapfrog_layered_sequence(x0, v0, packed, meta, base_dt, forces=None, ids=No
          float(base_dt), ptr(x_seq), ptr(v_seq), ptr(x_f), ptr(v_f), ptr(workspace),
          workspace.numel(), _lib.stream_of(dev))
     return x_seq, v_seq, x_f, v_f
+
+
+def recurrent_manifold_fused(x, v, f, U_stack, W_stack, dt, dt_scales, forget_rates, num_heads,
+                             plasticity=0.0, sing_thresh=1.0, sing_strength=1.0,
+                             mix_x=None, mix_v=None, Wf=None, Wi=None, bf=None,
+                             Wp=None, bp=None, topology=0, R=2.0, r=1.0):
+    """Whole-sequence recurrence with the reference's stacked operands
+    (gfn/cuda/ops.py:224-236, arguments as gfn/model.py:222-375 builds them).
+    Returns (x_final, v_final, x_seq, reg_loss).
+
+    The reference sends leapfrog models to its per-token loop instead
+    (gfn/model.py:207), so this entry computes that loop's leapfrog MLayer
+    recurrence (gfn/layers/base.py:198-338) on the library's fused sequence
+    kernel, for the operands given here:
+      x, v [B, d]; f [B, L, d]; U_stack / W_stack [NL*H, hd, r];
+      Wf [NL*H, hd, hd] and bf [NL*H, hd] (friction; None: no friction);
+      dt_scales [H]: softplus(dt_params) of the first layer, used by every
+      layer (as the reference's dispatch passes it);
+      mix_x / mix_v: [d, d] (one matrix for every layer, as the reference
+      passes layer 0's) or [NL, d, d]; the mixing biases are 0 and the
+      RMSNorm gains 1, since the reference's argument list carries neither.
+    forget_rates and Wi are accepted and unused (the leapfrog friction reads
+    the forget stack only, gfn/integrators/symplectic/leapfrog.py:72-81);
+    reg_loss is 0.  Active inference (plasticity, singularities) and the
+    torus raise.  Inference only (no autograd)."""
+    require_cuda(x, v, f, U_stack, W_stack, Wf, bf, mix_x, mix_v)
+    if plasticity != 0.0 or sing_strength != 1.0 or topology != 0:
+        raise GfnError("recurrent_manifold_fused: only the Euclidean leapfrog without active inference")
+    if Wp is not None and bool((Wp != 0).any()):
+        raise GfnError("recurrent_manifold_fused: singularity potentials are not implemented")
+    H = int(num_heads)
+    NLH, hd, rank = U_stack.shape
+    NL = NLH // H
+    d = hd * H
+    dev = x.device
+    if Wf is None:
+        # no friction: sigmoid(-inf) = 0 through a bias far below the gate's range
+        Wf = torch.zeros(NLH, hd, hd, device=dev, dtype=torch.float32)
+        bf = torch.full((NLH, hd), -1e30, device=dev, dtype=torch.float32)
+    elif bf is None:
+        bf = torch.zeros(NLH, hd, device=dev, dtype=torch.float32)
+    if not isinstance(dt_scales, torch.Tensor):
+        dt_scales = torch.full((H,), float(dt_scales), device=dev, dtype=torch.float32)
+    s = dt_scales.reshape(-1).to(device=dev, dtype=torch.float32)
+    if s.numel() == 1:
+        s = s.expand(H)
+    # dt_params whose softplus is the given scale (the pack applies softplus)
+    dtp = torch.where(s > 20.0, s, torch.log(torch.expm1(s.double())).float())
+    dt_params = dtp.repeat(NL).contiguous()
+    mix = None
+    if H > 1:
+        if mix_x is None or mix_v is None or mix_x.numel() == 0:
+            raise GfnError("recurrent_manifold_fused: heads > 1 needs mix_x and mix_v")
+        mx = mix_x.reshape(-1, d, d).expand(NL, d, d).contiguous()
+        mv = mix_v.reshape(-1, d, d).expand(NL, d, d).contiguous()
+        zeros = torch.zeros(NL, d, device=dev, dtype=torch.float32)
+        ones = torch.ones(NL, d, device=dev, dtype=torch.float32)
+        mix = (mx, zeros, ones, mv, zeros, ones)
+    packed, meta = leapfrog_pack(U_stack, W_stack, Wf.reshape(NLH, hd, hd), bf.reshape(NLH, hd),
+                                 dt_params, mix)
+    with torch.no_grad():
+        x_seq, _, xf, vf = leapfrog_sequence(x, v, packed, meta, float(dt), forces=f, want_v_seq=False)
+    reg_loss = torch.zeros((), device=dev, dtype=torch.float32)
+    return xf, vf, x_seq, reg_loss
 
 
 MIX_SPLIT_BF16, MIX_FP32_SIMT, MIX_SPLIT_F16, MIX_UMMA_F16 = 0, 1, 2, 3

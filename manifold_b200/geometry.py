@@ -91,3 +91,55 @@ class ReactiveChristoffel(LowRankChristoffel):
             raise GfnError("active-inference Christoffel (plasticity/singularities) is not "
                            "implemented on this build")
         return super().forward(v, x, force=force, **kwargs)
+
+
+class ToroidalChristoffel(nn.Module):
+    """Toroidal geometry (mirror of gfn/geometry/toroidal.py:4-148).
+
+    Coordinates pair up as (theta, phi) = (x_i, x_i+1):
+    Gamma_i = 0.05 (R + r cos th) sin th / r * v_ph^2,
+    Gamma_i+1 = 0.05 * 2 (-(r sin th) / max(R + r cos th, 1e-6)) v_ph v_th;
+    friction mu = 5 sigmoid(forget_gate([sin x, cos x]) + input_gate(F)).
+    Parameters and init follow toroidal.py:17-52 (state_dict compatible).
+    """
+
+    def __init__(self, dim, physics_config=None):
+        super().__init__()
+        self.dim = dim
+        self.config = physics_config or {}
+        self.R = self.config.get("topology", {}).get("major_radius", 2.0)
+        self.r = self.config.get("topology", {}).get("minor_radius", 1.0)
+        self.topology_id = 1
+        self.is_torus = True
+        gate_input_dim = 2 * dim
+        self.forget_gate = nn.Linear(gate_input_dim, dim)
+        nn.init.normal_(self.forget_gate.weight, std=0.01)
+        nn.init.constant_(self.forget_gate.bias, -5.0)
+        self.input_gate = nn.Linear(dim, dim, bias=False)
+        nn.init.normal_(self.input_gate.weight, std=0.01)
+        self.clamp_val = self.config.get("stability", {}).get("curvature_clamp", 5.0)
+        self.active_cfg = self.config.get("active_inference", {})
+        self.plasticity = self.active_cfg.get("reactive_curvature", {}).get("plasticity", 0.1)
+        self.singularity_threshold = self.active_cfg.get("singularities", {}).get("threshold", 0.8)
+        self.black_hole_strength = self.active_cfg.get("singularities", {}).get("strength", 10.0)
+        self.V = (nn.Linear(gate_input_dim, 1)
+                  if self.active_cfg.get("singularities", {}).get("enabled", False) else None)
+        if self.V is not None:
+            nn.init.constant_(self.V.bias, -2.0)
+
+    def forward(self, v, x=None, force=None, **kwargs):
+        """Reference semantics gfn/geometry/toroidal.py:70-148 (CUDA tensors only)."""
+        if x is None:
+            return torch.zeros_like(v)
+        if self.active_cfg.get("enabled", False):
+            raise GfnError("active-inference toroidal Christoffel is not implemented on this build")
+        require_cuda(v, x, force)
+        gamma = ops.christoffel_fused(v, None, None, x, topology=1, R=self.R, r=self.r)
+        x_in = torch.cat([torch.sin(x), torch.cos(x)], dim=-1)
+        gate = self.forget_gate(x_in)
+        if force is not None:
+            gate = gate + self.input_gate(force)
+        mu = torch.sigmoid(gate) * 5.0
+        if getattr(self, "return_friction_separately", False):
+            return gamma, mu
+        return gamma + mu * v

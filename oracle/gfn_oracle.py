@@ -90,6 +90,63 @@ def leapfrog_head_step(x, v, F, U, W, Wf, bf, dt, dt_scale, steps=1):
     return x, v
 
 
+TWO_PI_F32 = np.float32(2.0 * 3.14159265359)  # gfn/geometry/boundaries.py:13-14
+
+
+def torus_wrap(x):
+    """torch.remainder(x, 2*PI) (gfn/geometry/boundaries.py:4-17): fmod, then
+    shifted into [0, 2 pi) for negative remainders."""
+    m = np.fmod(x, x.dtype.type(TWO_PI_F32))
+    return np.where(m < 0, m + x.dtype.type(TWO_PI_F32), m).astype(x.dtype)
+
+
+def torus_christoffel(v, x, R=2.0, r=1.0):
+    """Toroidal Gamma (gfn/geometry/toroidal.py:70-108): for pairs
+    (th, ph) = (x_i, x_i+1), Gamma_i = (R + r cos th) sin th / r * v_ph^2,
+    Gamma_i+1 = 2 (-(r sin th) / max(R + r cos th, 1e-6)) v_ph v_th, times 0.05."""
+    dt = v.dtype.type
+    g = np.zeros_like(v)
+    R, r = dt(R), dt(r)
+    for i in range(0, v.shape[-1] - 1, 2):
+        th, vth, vph = x[..., i], v[..., i], v[..., i + 1]
+        denom = R + r * np.cos(th)
+        ds = np.maximum(denom, dt(1e-6))
+        g[..., i] = (denom * np.sin(th) / r) * (vph ** 2)
+        g[..., i + 1] = dt(2.0) * (-(r * np.sin(th)) / ds) * vph * vth
+    return g * dt(0.05)
+
+
+def leapfrog_head_step_gated(x, v, F, U, W, Wf, bf, Wi, dt, dt_scale, steps=1, topology=0,
+                             R=2.0, r=1.0):
+    """leapfrog_head_step with the full friction gate and both topologies:
+    mu = 5 sigmoid((feat(x) Wf^T + bf) + F Wi^T) (gfn/geometry/lowrank.py:114-123;
+    Wi None: no input gate), feat = [sin x, cos x] and Gamma the toroidal term
+    on the torus (gfn/geometry/toroidal.py:70-124), x wrapped after the drift
+    (gfn/integrators/symplectic/leapfrog.py:88-91)."""
+    dtp = x.dtype.type
+    eff = dtp(dt) * dtp(dt_scale)
+    h = dtp(0.5) * eff
+    one = dtp(1.0)
+    zin = (F @ Wi.T) if Wi is not None else dtp(0.0)
+
+    def mu(xc):
+        if Wf is None:
+            return dtp(0.0)
+        feat = np.concatenate([np.sin(xc), np.cos(xc)], -1) if topology == 1 else xc
+        return sigmoid(((feat @ Wf.T) + bf) + zin) * dtp(5.0)
+
+    def gam(vc, xc):
+        return torus_christoffel(vc, xc, R, r) if topology == 1 else christoffel(vc, U, W)
+
+    for _ in range(steps):
+        v_half = (v + h * (F - gam(v, x))) / (one + h * mu(x))
+        x = x + eff * v_half
+        if topology == 1:
+            x = torus_wrap(x)
+        v = (v_half + h * (F - gam(v_half, x))) / (one + h * mu(x))
+    return x, v
+
+
 def rmsnorm(y, g):
     """torch.nn.RMSNorm(d, eps=None): y * rsqrt(mean(y^2) + eps) * g."""
     dt = y.dtype

@@ -35,7 +35,7 @@ with contextlib.redirect_stdout(io.StringIO()), contextlib.redirect_stderr(io.St
     import gfn  # noqa: E402
     from gfn.model import Manifold  # noqa: E402
     from gfn.integrators import LeapfrogIntegrator  # noqa: E402
-    from gfn.geometry import LowRankChristoffel  # noqa: E402
+    from gfn.geometry import LowRankChristoffel, ToroidalChristoffel  # noqa: E402
     from gfn.layers import ParallelMLayer  # noqa: E402
     from gfn.scan import parallel_scan  # noqa: E402
 
@@ -153,6 +153,92 @@ def gen_units():
     print("units", len(out))
 
 
+def _leaf(a):
+    return T(a).clone().requires_grad_(True)
+
+
+def gen_ops():
+    """Goldens of the single-head operators with their reference autograd
+    gradients: the low-rank and toroidal Christoffel terms, and the leapfrog
+    integrator with the Christoffel's own gates (input gate included), with
+    explicit forget stacks, and on the torus."""
+    rng = np.random.default_rng(77)
+    out = {}
+    hd, r, B = 32, 8, 9
+    # low-rank Gamma and its gradients
+    U = (rng.standard_normal((hd, r)) * 0.4).astype(np.float32)
+    W = (rng.standard_normal((hd, r)) * 0.4).astype(np.float32)
+    v = (rng.standard_normal((B, hd)) * 3).astype(np.float32)
+    G = rng.standard_normal((B, hd)).astype(np.float32)
+    ch = LowRankChristoffel(hd, r)
+    with torch.no_grad():
+        ch.U.copy_(T(U)); ch.W.copy_(T(W))
+    ch.return_friction_separately = True
+    vv = _leaf(v)
+    g, _ = ch(vv, torch.zeros(B, hd))
+    (g * T(G)).sum().backward()
+    out.update(lr_U=U, lr_W=W, lr_v=v, lr_G=G, lr_gamma=g.detach().numpy(), lr_dv=vv.grad.numpy(),
+               lr_dU=ch.U.grad.numpy(), lr_dW=ch.W.grad.numpy())
+    # toroidal Gamma and its gradients
+    tc = ToroidalChristoffel(hd, physics_config={"topology": {"type": "torus", "major_radius": 2.0,
+                                                              "minor_radius": 1.0}})
+    tc.return_friction_separately = True
+    xt = rng.uniform(0, 2 * np.pi, (B, hd)).astype(np.float32)
+    xx, vv = _leaf(xt), _leaf(v)
+    g, _ = tc(vv, xx)
+    (g * T(G)).sum().backward()
+    out.update(tor_x=xt, tor_gamma=g.detach().numpy(), tor_dv=vv.grad.numpy(), tor_dx=xx.grad.numpy())
+    # leapfrog, the Christoffel's own gates (forget + input gate), 2 steps
+    x = rng.standard_normal((B, hd)).astype(np.float32)
+    F = rng.standard_normal((B, hd)).astype(np.float32)
+    Gx = rng.standard_normal((B, hd)).astype(np.float32)
+    Gv = rng.standard_normal((B, hd)).astype(np.float32)
+    Wf = (rng.standard_normal((hd, hd)) * 0.2).astype(np.float32)
+    bf = (rng.standard_normal(hd) * 0.5).astype(np.float32)
+    Wi = (rng.standard_normal((hd, hd)) * 0.2).astype(np.float32)
+    ch = LowRankChristoffel(hd, r)
+    with torch.no_grad():
+        ch.U.copy_(T(U)); ch.W.copy_(T(W))
+        ch.forget_gate.weight.copy_(T(Wf)); ch.forget_gate.bias.copy_(T(bf))
+        ch.input_gate.weight.copy_(T(Wi))
+    integ = LeapfrogIntegrator(ch, dt=0.1)
+    xx, vv, ff = _leaf(x), _leaf(v), _leaf(F)
+    xn, vn = integ(xx, vv, force=ff, dt_scale=torch.tensor(0.87), steps=2)
+    ((xn * T(Gx)).sum() + (vn * T(Gv)).sum()).backward()
+    out.update(ig_x=x, ig_F=F, ig_Gx=Gx, ig_Gv=Gv, ig_Wf=Wf, ig_bf=bf, ig_Wi=Wi,
+               ig_xn=xn.detach().numpy(), ig_vn=vn.detach().numpy(), ig_dx=xx.grad.numpy(),
+               ig_dv=vv.grad.numpy(), ig_dF=ff.grad.numpy(), ig_dU=ch.U.grad.numpy(),
+               ig_dW=ch.W.grad.numpy(), ig_dWf=ch.forget_gate.weight.grad.numpy(),
+               ig_dbf=ch.forget_gate.bias.grad.numpy(), ig_dWi=ch.input_gate.weight.grad.numpy())
+    # leapfrog with explicit forget stacks (the MLayer usage), 3 steps
+    ch = LowRankChristoffel(hd, r)
+    with torch.no_grad():
+        ch.U.copy_(T(U)); ch.W.copy_(T(W))
+    integ = LeapfrogIntegrator(ch, dt=0.1)
+    xx, vv, ff = _leaf(x), _leaf(v), _leaf(F)
+    wf, bb = _leaf(Wf[None]), _leaf(bf[None])
+    xn, vn = integ(xx, vv, force=ff, dt_scale=torch.tensor(1.13), steps=3, W_forget_stack=wf,
+                   b_forget_stack=bb, topology=0)
+    ((xn * T(Gx)).sum() + (vn * T(Gv)).sum()).backward()
+    out.update(st_xn=xn.detach().numpy(), st_vn=vn.detach().numpy(), st_dx=xx.grad.numpy(),
+               st_dv=vv.grad.numpy(), st_dF=ff.grad.numpy(), st_dU=ch.U.grad.numpy(),
+               st_dW=ch.W.grad.numpy(), st_dWf=wf.grad[0].numpy(), st_dbf=bb.grad[0].numpy())
+    # toroidal leapfrog with a forget stack over [sin x, cos x], 2 steps
+    tc = ToroidalChristoffel(hd, physics_config={"topology": {"type": "torus"}})
+    Wft = (rng.standard_normal((hd, 2 * hd)) * 0.2).astype(np.float32)
+    integ = LeapfrogIntegrator(tc, dt=0.1)
+    xx, vv, ff = _leaf(xt), _leaf(v), _leaf(F)
+    wf, bb = _leaf(Wft[None]), _leaf(bf[None])
+    xn, vn = integ(xx, vv, force=ff, dt_scale=torch.tensor(0.95), steps=2, W_forget_stack=wf,
+                   b_forget_stack=bb, topology=1)
+    ((xn * T(Gx)).sum() + (vn * T(Gv)).sum()).backward()
+    out.update(tl_Wf=Wft, tl_xn=xn.detach().numpy(), tl_vn=vn.detach().numpy(), tl_dx=xx.grad.numpy(),
+               tl_dv=vv.grad.numpy(), tl_dF=ff.grad.numpy(), tl_dWf=wf.grad[0].numpy(),
+               tl_dbf=bb.grad[0].numpy())
+    np.savez_compressed(os.path.join(HERE, "ops.npz"), **out)
+    print("ops", len(out))
+
+
 def gen_grad_case(name, cfg):
     """Reference autograd gradients of <Gx, x_seq> + <Gv, v_seq> + <gx, x_L> + <gv, v_L>."""
     P = C.make_params(cfg)
@@ -233,6 +319,8 @@ if __name__ == "__main__":
     for n in names:
         if n == "units":
             gen_units()
+        elif n == "ops":
+            gen_ops()
         elif n == "init":
             gen_init()
         elif n in C.GRAD_CASES:
@@ -241,6 +329,7 @@ if __name__ == "__main__":
             gen_model_case(n, C.CASES[n])
     if not sys.argv[1:]:
         gen_units()
+        gen_ops()
         gen_init()
         for n, cfg in C.GRAD_CASES.items():
             gen_grad_case(n, cfg)

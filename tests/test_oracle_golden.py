@@ -93,3 +93,23 @@ def test_oracle_units_match_reference():
     xs, vs = O.parallel_mlayer(g["pl_f"], pp, heads=4)
     close(xs, g["pl_x"], 1e-5, 1e-5)
     close(vs, g["pl_v"], 1e-5, 1e-5)
+
+
+def test_oracle_single_head_ops_match_reference():
+    """The gated / toroidal leapfrog and the toroidal Gamma of the oracle
+    against the reference's own outputs (tests/golden/ops.npz)."""
+    g = load("ops")
+    rowwise_close(O.torus_christoffel(g["lr_v"], g["tor_x"]), g["tor_gamma"], what="torus gamma")
+    rowwise_close(O.christoffel(g["lr_v"], g["lr_U"], g["lr_W"]), g["lr_gamma"], what="low-rank gamma")
+    xn, vn = O.leapfrog_head_step_gated(g["ig_x"], g["lr_v"], g["ig_F"], g["lr_U"], g["lr_W"],
+                                        g["ig_Wf"], g["ig_bf"], g["ig_Wi"], 0.1, np.float32(0.87), 2)
+    rowwise_close(xn, g["ig_xn"], what="input-gate leapfrog x")
+    rowwise_close(vn, g["ig_vn"], what="input-gate leapfrog v")
+    xn, vn = O.leapfrog_head_step_gated(g["ig_x"], g["lr_v"], g["ig_F"], g["lr_U"], g["lr_W"],
+                                        g["ig_Wf"], g["ig_bf"], None, 0.1, np.float32(1.13), 3)
+    rowwise_close(xn, g["st_xn"], what="stacked leapfrog x")
+    rowwise_close(vn, g["st_vn"], what="stacked leapfrog v")
+    xn, vn = O.leapfrog_head_step_gated(g["tor_x"], g["lr_v"], g["ig_F"], None, None, g["tl_Wf"],
+                                        g["ig_bf"], None, 0.1, np.float32(0.95), 2, topology=1)
+    rowwise_close(xn, g["tl_xn"], what="torus leapfrog x")
+    rowwise_close(vn, g["tl_vn"], what="torus leapfrog v")
