@@ -109,6 +109,39 @@ int gfn_christoffel_torus(const float* v, const float* x, float* gamma, int batc
                           float R_val, float r_val, gfn_stream_t stream);
 
 /* ------------------------------------------------------------------------
+ * The reference's other integrators, and the leapfrog, over every head of a
+ * layer in one launch.  Replaces launch_euler_fused, launch_heun_fused,
+ * launch_rk4_fused, launch_verlet_fused, launch_yoshida_fused,
+ * launch_dormand_prince_fused (gfn/cuda/cuda_kernels.cpp:85-126; the
+ * reference's generic_integrator_cuda takes the scheme the same way) and the
+ * Python-only Forest-Ruth and Omelyan integrators.  scheme:
+ *   0 Euler (gfn/integrators/runge_kutta/euler.py:46-62)
+ *   1 Heun (runge_kutta/heun.py:46-77)      2 RK4 (runge_kutta/rk4.py:46-82)
+ *   3 Verlet (symplectic/verlet.py:41-72)   4 Yoshida (symplectic/yoshida.py:24-86)
+ *   5 Forest-Ruth (symplectic/forest_ruth.py:28-89)
+ *   6 Omelyan PEFRL (symplectic/omelyan.py:26-96)
+ *   7 Dormand-Prince 5th order (runge_kutta/dormand_prince.py:26-122)
+ *   8 leapfrog (symplectic/leapfrog.py:50-114, implicit friction)
+ * Schemes 0-7 step with a(x, v) = f - C(v, x), C the Christoffel term in its
+ * combined form: low-rank 20 tanh((((vU)^2 s) W^T + mu v) / 20)
+ * (gfn/geometry/lowrank.py:128-131), torus Gamma_torus + mu v
+ * (gfn/geometry/toroidal.py:146-148); mu = 5 sigmoid((feat(x) W_forget^T +
+ * b_forget) + f W_input^T), 0 without W_forget.
+ * x, v, f, x_new, v_new [batch, heads * head_dim] (head h at columns
+ * h * head_dim); stacks per head: U, W [heads, head_dim, rank],
+ * W_forget [heads, head_dim, fin] (fin = head_dim, 2 head_dim on the torus),
+ * b_forget [heads, head_dim], W_input [heads, head_dim, head_dim].
+ * dt_scales: NULL, 1 value, one per head (heads > 1) or one per row (heads == 1).
+ * head_dim <= 256 (the gates' weights must fit in shared memory).
+ */
+int gfn_integrator_heads(int scheme, const float* x, const float* v, const float* f,
+                         const float* U_stack, const float* W_stack, const float* W_forget_stack,
+                         const float* b_forget_stack, const float* W_input_stack, float* x_new,
+                         float* v_new, float dt, const float* dt_scales, int dt_scales_count,
+                         int batch, int heads, int head_dim, int rank, int steps, int topology,
+                         float R_val, float r_val, gfn_stream_t stream);
+
+/* ------------------------------------------------------------------------
  * Backward of the Christoffel term.  Replaces launch_christoffel_backward
  * (gfn/cuda/cuda_kernels.cpp:21-29) for plasticity 0 and no singularity
  * potential (V_w / grad_V_w must be NULL).

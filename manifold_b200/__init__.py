@@ -12,14 +12,18 @@ from .model import Manifold as GFN
 from .layers import MLayer, ParallelMLayer, RiemannianGating
 from .layers import MLayer as GLayer
 from .geometry import LowRankChristoffel, ReactiveChristoffel, ToroidalChristoffel
-from .integrators import LeapfrogIntegrator
+from .integrators import (DormandPrinceIntegrator, EulerIntegrator, ForestRuthIntegrator,
+                          HeunIntegrator, LeapfrogIntegrator, OmelyanIntegrator, RK4Integrator,
+                          SymplecticIntegrator, VerletIntegrator, YoshidaIntegrator)
+from .integrators import INTEGRATOR_CLASSES as INTEGRATORS
 from .embeddings import FunctionalEmbedding, ImplicitEmbedding, SineLayer
 from .scan import parallel_scan
 from . import cuda
 
-INTEGRATORS = {"leapfrog": LeapfrogIntegrator}
-
 __all__ = ["GFN", "Manifold", "GLayer", "MLayer", "ParallelMLayer", "RiemannianGating",
            "LowRankChristoffel", "ReactiveChristoffel", "ToroidalChristoffel", "LeapfrogIntegrator",
+           "EulerIntegrator", "HeunIntegrator", "RK4Integrator", "DormandPrinceIntegrator",
+           "SymplecticIntegrator", "VerletIntegrator", "YoshidaIntegrator", "ForestRuthIntegrator",
+           "OmelyanIntegrator",
            "FunctionalEmbedding", "ImplicitEmbedding", "SineLayer", "ImplicitReadout",
            "parallel_scan", "GfnError", "INTEGRATORS"]

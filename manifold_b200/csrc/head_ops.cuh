@@ -625,9 +625,297 @@ __global__ void __launch_bounds__(WARPS * 32) head_bwd_kernel(const Params a) {
   if (a.gf) row_store<EPL>(gF, a.gf + off, hd, lane);
 }
 
+// ---------------------------------------------------------------- other integrators
+// The non-leapfrog integrators step with the acceleration
+//   a(x, v) = F - C(v, x)
+// where C is the Christoffel term in its combined form (the form those
+// integrators call, gfn/geometry/lowrank.py:128-131, gfn/geometry/toroidal.py:146-148):
+//   low-rank: C = 20 tanh((((vU)^2 s) W^T + mu v) / 20)
+//   torus:    C = Gamma_torus(v, x) + mu v
+// with mu the friction gate above (0 without W_forget).
+enum Scheme {
+  kEuler = 0,        // gfn/integrators/runge_kutta/euler.py:46-62
+  kHeun = 1,         // gfn/integrators/runge_kutta/heun.py:46-77
+  kRK4 = 2,          // gfn/integrators/runge_kutta/rk4.py:46-82
+  kVerlet = 3,       // gfn/integrators/symplectic/verlet.py:41-72
+  kYoshida = 4,      // gfn/integrators/symplectic/yoshida.py:24-86
+  kForestRuth = 5,   // gfn/integrators/symplectic/forest_ruth.py:28-89
+  kOmelyan = 6,      // gfn/integrators/symplectic/omelyan.py:26-96
+  kDormandPrince = 7, // gfn/integrators/runge_kutta/dormand_prince.py:26-122
+  kLeapfrog = 8       // gfn/integrators/symplectic/leapfrog.py:50-114 (implicit friction)
+};
+
+struct IntegArgs {
+  Params p;        // x, v, f, U, W, Wf, bf, Wi, dt_scale, dt, steps, topo, R, r, hd, fin, x_out, v_out
+  int scheme;
+  int heads;       // heads of one launch (blockIdx.y); 1 for a single head
+  long long ld;    // row stride of x, v, f, x_out, v_out (elements); head h at column h * hd
+  long long hU, hWf, hWi, hb;  // per-head strides of U / W, Wf, Wi, bf (elements)
+  int dts_per_head;            // dt_scale holds one value per head (else 1 or B values)
+  float c[20];                 // scheme coefficients (float32, as the reference's tensors see them)
+};
+
+template <int RK, int EPL>
+GFN_DEV void accel(const float (&x)[EPL], const float (&v)[EPL], const float (&F)[EPL], const float (&zin)[EPL],
+                   const float* sm, const Smem& L, float* rb, const Params& a, int lane, float (&acc)[EPL]) {
+  const int hd = a.hd;
+  float mu[EPL];
+  if (a.Wf) {
+    friction<EPL>(x, zin, sm, L, rb, hd, a.fin, a.topo, lane, mu);
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) mu[e] *= 5.f;
+  } else {
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) mu[e] = 0.f;
+  }
+  if (a.topo) {
+    float g[EPL];
+    gamma_torus<EPL>(v, x, hd, a.R, a.r, lane, g);
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) acc[e] = F[e] - (g[e] + mu[e] * v[e]);
+  } else {
+    float p[RK];
+#pragma unroll
+    for (int q = 0; q < RK; ++q) {
+      float s0 = 0.f;
+#pragma unroll
+      for (int e = 0; e < EPL; ++e) {
+        const int k = lane + 32 * e;
+        if (k < hd) s0 = fmaf(v[e], sm[L.U + k * RK + q], s0);
+      }
+      p[q] = warp_sum(s0);
+    }
+    float ss = 0.f;
+#pragma unroll
+    for (int q = 0; q < RK; ++q) ss = fmaf(p[q], p[q], ss);
+    const float s = 1.f / ((1.f + sqrtf(ss)) + 1e-6f);
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) {
+      const int k = lane + 32 * e;
+      float pre = 0.f;
+      if (k < hd) {
+#pragma unroll
+        for (int q = 0; q < RK; ++q) pre = fmaf((p[q] * p[q]) * s, sm[L.W + k * RK + q], pre);
+      }
+      acc[e] = F[e] - 20.f * tanhf((pre + mu[e] * v[e]) / 20.f);
+    }
+  }
+}
+
+template <int EPL>
+GFN_DEV void wrap_if(float (&x)[EPL], int topo) {
+  if (topo) {
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) x[e] = torus_wrap(x[e]);
+  }
+}
+
+// One row per warp; blockIdx.y = head.  Weights of the head are staged in
+// shared memory as for the leapfrog kernels.
+template <int RK, int EPL>
+__global__ void __launch_bounds__(WARPS * 32) integrate_kernel(const IntegArgs ia) {
+  extern __shared__ __align__(16) float sm[];
+  Params a = ia.p;
+  const int hh = blockIdx.y;
+  if (a.U) { a.U += hh * ia.hU; a.W += hh * ia.hU; }
+  if (a.Wf) { a.Wf += hh * ia.hWf; if (a.bf) a.bf += hh * ia.hb; }
+  if (a.Wi) a.Wi += hh * ia.hWi;
+  const bool fric = a.Wf != nullptr, igate = a.Wi != nullptr;
+  const Smem L = smem_layout(a.hd, RK, a.fin, fric, igate);
+  stage_weights<RK>(a, sm, L, fric, igate);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row = blockIdx.x * WARPS + warp;
+  if (row >= a.B) return;
+  const int hd = a.hd;
+  float* rb = sm + L.rb + warp * L.rbn;
+  const long long off = (long long)row * ia.ld + (long long)hh * hd;
+  float x[EPL], v[EPL], F[EPL], zin[EPL];
+  row_load<EPL>(x, a.x + off, hd, lane);
+  row_load<EPL>(v, a.v + off, hd, lane);
+  row_load<EPL>(F, a.f ? a.f + off : nullptr, hd, lane);
+  input_gate<EPL>(F, sm, L, rb, hd, igate, lane, zin);
+  float sc = 1.f;
+  if (a.dt_scale) sc = a.dt_scale[ia.dts_per_head ? hh : (a.dt_scale_n == 1 ? 0 : row)];
+  const float dt = a.dt * sc;
+  const float* c = ia.c;
+  float k1[EPL], k2[EPL], k3[EPL], k4[EPL], xt[EPL], vt[EPL];
+  for (int st = 0; st < a.steps; ++st) {
+    switch (ia.scheme) {
+      case kEuler: {
+        accel<RK, EPL>(x, v, F, zin, sm, L, rb, a, lane, k1);
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) {
+          x[e] = x[e] + dt * v[e];
+          v[e] = v[e] + dt * k1[e];
+        }
+        wrap_if<EPL>(x, a.topo);
+        break;
+      }
+      case kHeun: {
+        accel<RK, EPL>(x, v, F, zin, sm, L, rb, a, lane, k1);
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) {
+          vt[e] = v[e] + dt * k1[e];
+          xt[e] = x[e] + dt * v[e];
+        }
+        wrap_if<EPL>(xt, a.topo);
+        accel<RK, EPL>(xt, vt, F, zin, sm, L, rb, a, lane, k2);
+        const float h2 = dt / 2.f;
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) {
+          x[e] = x[e] + h2 * (v[e] + vt[e]);
+          v[e] = v[e] + h2 * (k1[e] + k2[e]);
+        }
+        wrap_if<EPL>(x, a.topo);
+        break;
+      }
+      case kRK4: {
+        // k*: velocity slopes; the position slopes are the stage velocities
+        float dx2[EPL], dx3[EPL];
+        const float hdt = 0.5f * dt;
+        accel<RK, EPL>(x, v, F, zin, sm, L, rb, a, lane, k1);
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) {
+          vt[e] = v[e] + hdt * k1[e];
+          xt[e] = x[e] + hdt * v[e];
+        }
+        wrap_if<EPL>(xt, a.topo);
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) dx2[e] = vt[e];
+        accel<RK, EPL>(xt, vt, F, zin, sm, L, rb, a, lane, k2);
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) {
+          vt[e] = v[e] + hdt * k2[e];
+          xt[e] = x[e] + hdt * dx2[e];
+        }
+        wrap_if<EPL>(xt, a.topo);
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) dx3[e] = vt[e];
+        accel<RK, EPL>(xt, vt, F, zin, sm, L, rb, a, lane, k3);
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) {
+          vt[e] = v[e] + dt * k3[e];
+          xt[e] = x[e] + dt * dx3[e];
+        }
+        wrap_if<EPL>(xt, a.topo);
+        accel<RK, EPL>(xt, vt, F, zin, sm, L, rb, a, lane, k4);
+        const float s6 = dt / 6.f;
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) {
+          x[e] = x[e] + s6 * (((v[e] + 2.f * dx2[e]) + 2.f * dx3[e]) + vt[e]);
+          v[e] = v[e] + s6 * (((k1[e] + 2.f * k2[e]) + 2.f * k3[e]) + k4[e]);
+        }
+        wrap_if<EPL>(x, a.topo);
+        break;
+      }
+      case kVerlet: {
+        const float hdt = 0.5f * dt;
+        accel<RK, EPL>(x, v, F, zin, sm, L, rb, a, lane, k1);
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) {
+          v[e] = v[e] + hdt * k1[e];
+          x[e] = x[e] + dt * v[e];
+        }
+        wrap_if<EPL>(x, a.topo);
+        accel<RK, EPL>(x, v, F, zin, sm, L, rb, a, lane, k2);
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) v[e] = v[e] + hdt * k2[e];
+        break;
+      }
+      case kYoshida:
+      case kForestRuth:
+      case kOmelyan: {
+        // drift c_i, kick d_i at the drifted position with the previous
+        // velocity; c[0..4] drifts, c[5..8] kicks (the final kick reuses the
+        // last kick coefficient, as the reference does)
+        const int nd = ia.scheme == kOmelyan ? 5 : 4;
+        for (int i = 0; i < nd; ++i) {
+          const float cd = c[i] * dt;
+#pragma unroll
+          for (int e = 0; e < EPL; ++e) x[e] = x[e] + cd * v[e];
+          wrap_if<EPL>(x, a.topo);
+          const float kd = c[5 + (i < nd - 1 ? i : nd - 2)] * dt;
+          accel<RK, EPL>(x, v, F, zin, sm, L, rb, a, lane, k1);
+#pragma unroll
+          for (int e = 0; e < EPL; ++e) v[e] = v[e] + kd * k1[e];
+        }
+        break;
+      }
+      case kDormandPrince: {
+        // six stages; stage slopes kept as (position slope = stage velocity,
+        // velocity slope = acceleration); c[] holds a21..a65 then b5
+        float kv[6][EPL], kx[6][EPL];
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) kx[0][e] = v[e];
+        accel<RK, EPL>(x, v, F, zin, sm, L, rb, a, lane, kv[0]);
+        int ci = 0;
+#pragma unroll 1
+        for (int sidx = 1; sidx < 6; ++sidx) {
+          float sx[EPL], sv[EPL];
+#pragma unroll
+          for (int e = 0; e < EPL; ++e) {
+            sx[e] = c[ci] * kx[0][e];
+            sv[e] = c[ci] * kv[0][e];
+          }
+#pragma unroll 1
+          for (int j = 1; j < sidx; ++j) {
+#pragma unroll
+            for (int e = 0; e < EPL; ++e) {
+              sx[e] = sx[e] + c[ci + j] * kx[j][e];
+              sv[e] = sv[e] + c[ci + j] * kv[j][e];
+            }
+          }
+          ci += sidx;
+#pragma unroll
+          for (int e = 0; e < EPL; ++e) {
+            xt[e] = x[e] + dt * sx[e];
+            vt[e] = v[e] + dt * sv[e];
+            kx[sidx][e] = vt[e];
+          }
+          wrap_if<EPL>(xt, a.topo);
+          accel<RK, EPL>(xt, vt, F, zin, sm, L, rb, a, lane, kv[sidx]);
+        }
+        // b5 = c[15..] : weights of k1, k3, k4, k5, k6 (b2 = 0)
+        const float* b = c + 15;
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) {
+          const float sx = (((b[0] * kx[0][e] + b[1] * kx[2][e]) + b[2] * kx[3][e]) + b[3] * kx[4][e]) + b[4] * kx[5][e];
+          const float sv = (((b[0] * kv[0][e] + b[1] * kv[2][e]) + b[2] * kv[3][e]) + b[3] * kv[4][e]) + b[4] * kv[5][e];
+          x[e] = x[e] + dt * sx;
+          v[e] = v[e] + dt * sv;
+        }
+        wrap_if<EPL>(x, a.topo);
+        break;
+      }
+      case kLeapfrog: {
+        const float h = 0.5f * dt;
+        float sg[EPL], g[EPL], t[EPL], p[RK], s;
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          if (fric) friction<EPL>(x, zin, sm, L, rb, hd, a.fin, a.topo, lane, sg);
+          if (a.topo) gamma_torus<EPL>(v, x, hd, a.R, a.r, lane, g);
+          else gamma_lowrank<RK, EPL>(v, sm + L.U, sm + L.W, hd, lane, p, s, t, g);
+#pragma unroll
+          for (int e = 0; e < EPL; ++e) {
+            const float mu = fric ? sg[e] * 5.f : 0.f;
+            v[e] = (v[e] + h * (F[e] - g[e])) / (1.f + h * mu);
+            if (half == 0) x[e] = x[e] + dt * v[e];
+          }
+          if (half == 0) wrap_if<EPL>(x, a.topo);
+        }
+        break;
+      }
+      default:
+        break;
+    }
+  }
+  row_store<EPL>(x, a.x_out + off, hd, lane);
+  row_store<EPL>(v, a.v_out + off, hd, lane);
+}
+
 // out[i * J + j] = sum_n A[n * sA + i] * Bm[(n % modB) * sB + j] (Bm null: 1),
 // n ascending: a fixed summation order.
-__global__ void outer_sum_kernel(const float* __restrict__ A, long long sA, const float* __restrict__ Bm,
+static __global__ void outer_sum_kernel(const float* __restrict__ A, long long sA, const float* __restrict__ Bm,
                                  long long sB, long long modB, int I, int J, long long N, float* __restrict__ out) {
   const int o = blockIdx.x * blockDim.x + threadIdx.x;
   if (o >= I * J) return;

@@ -481,17 +481,56 @@ def device_error(reset=True):
     return _lib.device_error(reset)
 
 
-def _unsupported(name):
-    def fn(*args, **kwargs):
-        raise GfnError(f"{name}: only the leapfrog integrator is implemented on this build")
-    fn.__name__ = name
+SCHEMES = {"euler": 0, "heun": 1, "rk4": 2, "verlet": 3, "yoshida": 4, "forest_ruth": 5,
+           "omelyan": 6, "dormand_prince": 7, "rk45": 7, "leapfrog": 8}
+
+
+def integrator_heads(scheme, x, v, f, U, W, dt, dt_scale, steps=1, topology=0, Wf=None, bf=None,
+                     Wi=None, heads=1, R=2.0, r=1.0):
+    """One launch of integrator `scheme` (a SCHEMES name or id) over every head.
+
+    x, v, f: [B, heads * hd]; U, W: [heads, hd, rank] (or [hd, rank] for one
+    head; unused on the torus); Wf [heads, hd, fin], bf [heads, hd], Wi
+    [heads, hd, hd] (the friction gate, optional); dt_scale: a number, one
+    value per head (heads > 1) or per row (heads == 1).  Returns (x_new, v_new).
+    """
+    sid = SCHEMES[scheme] if isinstance(scheme, str) else int(scheme)
+    require_cuda(x, v, f, U, W, Wf, bf, Wi)
+    if _grad_wanted(x, v, f, U, W, Wf, bf, Wi):
+        raise GfnError("integrator backward is implemented for the leapfrog only")
+    x, v = _f32c(x, "x"), _f32c(v, "v")
+    f, Wf, bf, Wi = _f32c(f, "f"), _f32c(Wf, "Wf"), _f32c(bf, "bf"), _f32c(Wi, "Wi")
+    B, d = x.shape
+    hd = d // heads
+    if topology == 0:
+        U, W = _f32c(U, "U"), _f32c(W, "W")
+        rank = U.shape[-1]
+    else:
+        U = W = None
+        rank = 4
+    dts = _dt_scales(dt_scale, x)
+    x_new, v_new = torch.empty_like(x), torch.empty_like(v)
+    call("gfn_integrator_heads", sid, ptr(x), ptr(v), ptr(f), ptr(U), ptr(W), ptr(Wf), ptr(bf), ptr(Wi),
+         ptr(x_new), ptr(v_new), float(dt), ptr(dts), dts.numel(), B, int(heads), hd, rank, int(steps),
+         int(topology), float(R), float(r), _stream(x))
+    return x_new, v_new
+
+
+def _integrator_op(name):
+    def fn(x, v, f, U, W, dt, dt_scale, steps, topology=0, R=2.0, r=1.0, Wf=None, bf=None, Wi=None):
+        return integrator_heads(name, x, v, f, U, W, dt, dt_scale, steps, topology, Wf, bf, Wi, 1, R, r)
+    fn.__name__ = f"{name}_fused"
+    fn.__doc__ = (f"One head's {name} integrator, `steps` times (the reference's gfn.cuda.ops."
+                  f"{name}_fused signature, gfn/cuda/ops.py:184-222), with the optional friction "
+                  "gate (Wf, bf, Wi) the reference's Christoffel applies in its combined form.")
     return fn
 
 
-euler_fused = _unsupported("euler_fused")
-heun_fused = _unsupported("heun_fused")
-rk4_fused = _unsupported("rk4_fused")
-verlet_fused = _unsupported("verlet_fused")
-yoshida_fused = _unsupported("yoshida_fused")
-forest_ruth_fused = _unsupported("forest_ruth_fused")
-dormand_prince_fused = _unsupported("dormand_prince_fused")
+euler_fused = _integrator_op("euler")
+heun_fused = _integrator_op("heun")
+rk4_fused = _integrator_op("rk4")
+verlet_fused = _integrator_op("verlet")
+yoshida_fused = _integrator_op("yoshida")
+forest_ruth_fused = _integrator_op("forest_ruth")
+omelyan_fused = _integrator_op("omelyan")
+dormand_prince_fused = _integrator_op("dormand_prince")

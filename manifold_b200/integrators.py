@@ -59,3 +59,103 @@ class LeapfrogIntegrator(nn.Module):
                                       Wf=Wf, bf=bf, R=R, r=r, Wi=Wi)
         return ops.leapfrog_fused(x, v, force, U, W, self.dt, dt_scale, steps, topology=0,
                                   Wf=Wf, bf=bf, Wi=Wi)
+
+
+def _gates(christoffel, force, kwargs, with_input):
+    """The friction gate the reference's Christoffel applies: the forget /
+    input stacks MLayer passes (gfn/geometry/lowrank.py:108-117; the torus
+    reads its own gates, gfn/geometry/toroidal.py:113-124), else the module's
+    own gates (lowrank.py:118-121).  Returns (Wf, bf, Wi)."""
+    Wf = kwargs.get("W_forget_stack", None)
+    Wi = kwargs.get("W_input_stack", None)
+    bf = kwargs.get("b_forget_stack", None)
+    if getattr(christoffel, "is_torus", False) or Wf is None or bf is None:
+        gate = getattr(christoffel, "forget_gate", None)
+        if gate is None:
+            return None, None, None
+        ig = getattr(christoffel, "input_gate", None)
+        Wi = ig.weight if (ig is not None and force is not None and with_input) else None
+        return gate.weight, gate.bias, Wi
+    Wf = Wf[0] if Wf.dim() == 3 else Wf
+    bf = bf[0] if bf.dim() == 2 else bf
+    if Wi is not None and Wi.dim() == 3:
+        Wi = Wi[0]
+    if force is None or not with_input:
+        Wi = None
+    return Wf, bf, Wi
+
+
+class _SchemeIntegrator(nn.Module):
+    """Base of the non-leapfrog integrators: forward(x, v, force, dt_scale,
+    steps) -> (x, v) through the library's multi-scheme kernel, with the
+    acceleration a = F - Christoffel(v, x, F) in the Christoffel's combined
+    form (friction included)."""
+
+    scheme = None
+
+    def __init__(self, christoffel, dt=0.01):
+        super().__init__()
+        self.christoffel = christoffel
+        self.dt = dt
+
+    def forward(self, x, v, force=None, dt_scale=1.0, steps=1, collect_christ=False, **kwargs):
+        require_cuda(x, v, force)
+        topology = 1 if getattr(self.christoffel, "is_torus", False) else 0
+        Wf, bf, Wi = _gates(self.christoffel, force, kwargs, True)
+        U = getattr(self.christoffel, "U", None)
+        W = getattr(self.christoffel, "W", None)
+        if topology == 0 and (U is None or W is None):
+            raise GfnError(f"{type(self).__name__} needs a low-rank Christoffel (U, W) or the torus")
+        return ops.integrator_heads(self.scheme, x, v, force, U, W, self.dt, dt_scale, steps, topology,
+                                    Wf, bf, Wi, 1, getattr(self.christoffel, "R", 2.0),
+                                    getattr(self.christoffel, "r", 1.0))
+
+
+class EulerIntegrator(_SchemeIntegrator):
+    """gfn/integrators/runge_kutta/euler.py:20-64."""
+    scheme = "euler"
+
+
+class HeunIntegrator(_SchemeIntegrator):
+    """gfn/integrators/runge_kutta/heun.py:20-78 (the reference's default)."""
+    scheme = "heun"
+
+
+class RK4Integrator(_SchemeIntegrator):
+    """gfn/integrators/runge_kutta/rk4.py:20-83."""
+    scheme = "rk4"
+
+
+class DormandPrinceIntegrator(_SchemeIntegrator):
+    """gfn/integrators/runge_kutta/dormand_prince.py:20-122 (fixed step, 5th-order weights)."""
+    scheme = "dormand_prince"
+
+
+class SymplecticIntegrator(_SchemeIntegrator):
+    """Velocity Verlet (gfn/integrators/symplectic/verlet.py:20-73)."""
+    scheme = "verlet"
+
+
+VerletIntegrator = SymplecticIntegrator
+
+
+class YoshidaIntegrator(_SchemeIntegrator):
+    """gfn/integrators/symplectic/yoshida.py:18-86."""
+    scheme = "yoshida"
+
+
+class ForestRuthIntegrator(_SchemeIntegrator):
+    """gfn/integrators/symplectic/forest_ruth.py:20-89."""
+    scheme = "forest_ruth"
+
+
+class OmelyanIntegrator(_SchemeIntegrator):
+    """gfn/integrators/symplectic/omelyan.py:18-96 (PEFRL)."""
+    scheme = "omelyan"
+
+
+INTEGRATOR_CLASSES = {
+    "leapfrog": LeapfrogIntegrator, "euler": EulerIntegrator, "heun": HeunIntegrator,
+    "rk4": RK4Integrator, "rk45": DormandPrinceIntegrator, "yoshida": YoshidaIntegrator,
+    "forest_ruth": ForestRuthIntegrator, "omelyan": OmelyanIntegrator,
+}

@@ -12,8 +12,8 @@ import torch.nn as nn
 
 from ._lib import GfnError, require_cuda
 from .cuda import ops
-from .geometry import ReactiveChristoffel
-from .integrators import LeapfrogIntegrator
+from .geometry import ReactiveChristoffel, ToroidalChristoffel
+from .integrators import INTEGRATOR_CLASSES, SymplecticIntegrator
 from .packing import PackCache
 
 
@@ -40,11 +40,9 @@ class RiemannianGating(nn.Module):
 
 def _check_config(physics_config, integrator_type):
     pc = physics_config or {}
-    if integrator_type != "leapfrog":
-        raise GfnError(f"integrator_type={integrator_type!r}: only 'leapfrog' is implemented on "
+    if integrator_type in ("coupling", "neural"):
+        raise GfnError(f"integrator_type={integrator_type!r} (a learned flow) is not implemented on "
                        "this build")
-    if pc.get("topology", {}).get("type", "euclidean").lower() == "torus":
-        raise GfnError("toroidal topology is not implemented on this build")
     for key in ("mixture", "hyper_curvature"):
         if pc.get(key, {}).get("enabled", False):
             raise GfnError(f"physics_config[{key!r}] is not implemented on this build")
@@ -95,13 +93,17 @@ class MLayer(nn.Module):
         self.norm_x = nn.LayerNorm(dim)
         self.norm_v = nn.LayerNorm(dim)
         head_rank = max(4, rank // heads)
+        topo_type = self.physics_config.get("topology", {}).get("type", "euclidean").lower()
+        self.topology_id = 1 if topo_type == "torus" else 0
+        Geo = ToroidalChristoffel if self.topology_id == 1 else ReactiveChristoffel
         self.christoffels = nn.ModuleList(
-            [ReactiveChristoffel(self.head_dim, head_rank, physics_config=self.physics_config)
+            [Geo(self.head_dim, physics_config=self.physics_config) if self.topology_id == 1
+             else Geo(self.head_dim, head_rank, physics_config=self.physics_config)
              for _ in range(heads)])
         self.register_buffer("headless_mode", torch.tensor(False))
         self.use_dynamic_time = False
-        self.topology_id = 0
-        self.gatings = nn.ModuleList([RiemannianGating(self.head_dim, topology=0) for _ in range(heads)])
+        self.gatings = nn.ModuleList([RiemannianGating(self.head_dim, topology=self.topology_id)
+                                      for _ in range(heads)])
         scale_vals = []
         for i in range(heads):
             target_dt = self.base_dt / 0.9
@@ -110,10 +112,15 @@ class MLayer(nn.Module):
         self.dt_params = nn.Parameter(torch.tensor(scale_vals))
         self.time_heads = None
         self.friction_gates = nn.ModuleList([self.christoffels[i].forget_gate for i in range(heads)])
-        self.integrators = nn.ModuleList(
-            [LeapfrogIntegrator(self.christoffels[i], dt=self.base_dt) for i in range(heads)])
+        Integ = INTEGRATOR_CLASSES.get(integrator_type, SymplecticIntegrator)
+        self.integrator_type = integrator_type
+        self.integrators = nn.ModuleList([Integ(self.christoffels[i], dt=self.base_dt) for i in range(heads)])
+        # the fused / layered recurrence kernels compute the Euclidean
+        # leapfrog; every other configuration steps layer by layer through the
+        # multi-scheme integrator kernel (generic path)
+        self.generic = self.topology_id == 1 or integrator_type != "leapfrog"
         if heads > 1:
-            self.out_proj_x = nn.Linear(dim, dim)
+            self.out_proj_x = nn.Linear(3 * dim if self.topology_id == 1 else dim, dim)
             self.out_proj_v = nn.Linear(dim, dim)
             self.mixed_norm_x = nn.RMSNorm(dim)
             self.mixed_norm_v = nn.RMSNorm(dim)
@@ -135,6 +142,8 @@ class MLayer(nn.Module):
         B = x.shape[0]
         if force is None:
             force = torch.zeros_like(x)
+        if self.generic:
+            return self._generic_step(x, v, force)
         if torch.is_grad_enabled() and any(t.requires_grad for t in
                                            [x, v, force, *self.parameters()]):
             from .training import leapfrog_sequence_train
@@ -147,6 +156,50 @@ class MLayer(nn.Module):
                            want_x_seq=False, want_v_seq=False)
         context_next = torch.ones(B, self.heads, device=x.device, dtype=x.dtype)
         return xn, vn, context_next, []
+
+
+    def _generic_step(self, x, v, force):
+        """One layer step for the torus and the non-leapfrog integrators:
+        every head's integrator in one launch of the multi-scheme kernel, then
+        the head mixing of gfn/layers/base.py:304-335 (torus: the mixer reads
+        [sin x, cos x, tanh(v / 100)] and x wraps into [0, 2 pi) instead of
+        the RMSNorm)."""
+        if self.training and torch.is_grad_enabled() and any(p.requires_grad for p in self.parameters()):
+            raise GfnError("training is implemented for the Euclidean leapfrog path only (call eval() "
+                           "or run under torch.no_grad() for inference)")
+        with torch.no_grad():
+            return self._generic_step_nograd(x, v, force)
+
+    def _generic_step_nograd(self, x, v, force):
+        B = x.shape[0]
+        H, hd = self.heads, self.head_dim
+        leap = self.integrator_type == "leapfrog"
+        ch = self.christoffels
+        Wf = torch.stack([c.forget_gate.weight for c in ch]).contiguous()
+        bf = torch.stack([c.forget_gate.bias for c in ch]).contiguous()
+        Wi = None if leap else torch.stack([c.input_gate.weight for c in ch]).contiguous()
+        if self.topology_id == 0:
+            U = torch.stack([c.U for c in ch]).contiguous()
+            W = torch.stack([c.W for c in ch]).contiguous()
+            R = r = 1.0
+        else:
+            U = W = None
+            R, r = ch[0].R, ch[0].r
+        scheme = self.integrator_type if self.integrator_type in ops.SCHEMES else "verlet"
+        dts = torch.nn.functional.softplus(self.dt_params)
+        xc, vc = ops.integrator_heads(scheme, x.contiguous(), v.contiguous(), force.contiguous(), U, W,
+                                      self.base_dt, dts, 1, self.topology_id, Wf, bf, Wi, H, R, r)
+        if H > 1:
+            if self.topology_id == 1:
+                mix_in = torch.cat([torch.sin(xc), torch.cos(xc), torch.tanh(vc / 100.0)], dim=-1)
+                xn = torch.remainder(self.out_proj_x(mix_in), 2.0 * 3.14159265359)
+            else:
+                xn = self.mixed_norm_x(self.out_proj_x(xc))
+            vn = self.mixed_norm_v(self.out_proj_v(vc))
+        else:
+            xn, vn = xc, vc
+        vn = 100.0 * torch.tanh(vn / 100.0)
+        return xn, vn, torch.ones(B, H, device=x.device, dtype=x.dtype), []
 
 
 class ParallelMLayer(nn.Module):

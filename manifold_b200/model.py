@@ -156,6 +156,8 @@ class Manifold(nn.Module):
         src = force_manual if force_manual is not None else input_ids
         require_cuda(src)
         B = src.shape[0]
+        if self.layers[0].generic:
+            return self._generic_recurrence(input_ids, attention_mask, state, force_manual, want_v_seq)
         layered = self._use_layered(B)
         packed, meta = self._pack.get(list(self.layers), layered=layered)
         seq = ops.leapfrog_layered_sequence if layered else ops.leapfrog_sequence
@@ -175,6 +177,30 @@ class Manifold(nn.Module):
                                        want_v_seq=want_v_seq)
         return x_seq, v_seq, (xf, vf), forces
 
+    def _generic_recurrence(self, input_ids, attention_mask, state, force_manual, want_v_seq):
+        """Token-by-token loop of gfn/model.py:377-402 for the torus and the
+        non-leapfrog integrators (one multi-scheme integrator launch plus the
+        head mixing per layer and token)."""
+        forces = self._forces(input_ids, force_manual)
+        B, L = forces.shape[:2]
+        if state is None:
+            x = self.x0.expand(B, -1)
+            v = self.v0.expand(B, -1)
+        else:
+            x, v = state
+        xs, vs = [], []
+        for t in range(L):
+            f = forces[:, t].to(torch.float32)
+            if attention_mask is not None:
+                f = f * attention_mask[:, t].unsqueeze(-1).float()
+            for layer in self.layers:
+                x, v, _, _ = layer(x, v, f)
+            xs.append(x)
+            vs.append(v)
+        x_seq = torch.stack(xs, 1)
+        v_seq = torch.stack(vs, 1) if want_v_seq else None
+        return x_seq, v_seq, (x, v), forces
+
     def forward(self, input_ids=None, attention_mask=None, state=None, force_manual=None,
                 collect_christ=False):
         if collect_christ:
@@ -188,7 +214,8 @@ class Manifold(nn.Module):
             x_final = cur if self.holographic else self.readout_norm(cur)
             logits = self.readout(x_final)
             return logits, (x_final[:, -1], None), []
-        if torch.is_grad_enabled() and any(p.requires_grad for p in self.parameters()):
+        if torch.is_grad_enabled() and any(p.requires_grad for p in self.parameters()) \
+                and not self.layers[0].generic:
             from .training import manifold_train_forward
             return manifold_train_forward(self, input_ids, attention_mask, state, force_manual)
         x_seq, v_seq, (x, v), forces = self.recurrence(input_ids, attention_mask, state, force_manual)

@@ -147,6 +147,151 @@ def leapfrog_head_step_gated(x, v, F, U, W, Wf, bf, Wi, dt, dt_scale, steps=1, t
     return x, v
 
 
+def combined_accel(x, v, F, U, W, Wf, bf, Wi, topology=0, R=2.0, r=1.0):
+    """a = F - C(v, x): the Christoffel term in the combined form the
+    non-leapfrog integrators call (gfn/geometry/lowrank.py:100-131,
+    gfn/geometry/toroidal.py:70-148): mu = 5 sigmoid(feat(x) Wf^T + bf + F Wi^T);
+    low-rank C = 20 tanh((((vU)^2 s) W^T + mu v) / 20), torus C = Gamma + mu v."""
+    dtp = x.dtype.type
+    if Wf is not None:
+        feat = np.concatenate([np.sin(x), np.cos(x)], -1) if topology == 1 else x
+        gate = (feat @ Wf.T) + bf
+        if Wi is not None:
+            gate = gate + (F @ Wi.T)
+        mu = sigmoid(gate) * dtp(5.0)
+    else:
+        mu = dtp(0.0)
+    if topology == 1:
+        c = torus_christoffel(v, x, R, r) + mu * v
+    else:
+        one = dtp(1.0)
+        proj = v @ U
+        norm = np.sqrt(np.sum(proj * proj, axis=-1, keepdims=True))
+        scale = one / ((one + norm) + dtp(1e-6))
+        g = ((proj * proj) * scale) @ W.T
+        c = dtp(20.0) * np.tanh((g + mu * v) / dtp(20.0))
+    return F - c
+
+
+_CBRT2 = 2.0 ** (1.0 / 3.0)
+_YOSHIDA = ([1 / (2 - _CBRT2) / 2, (1 - 1 / (2 - _CBRT2)) / 2, (1 - 1 / (2 - _CBRT2)) / 2,
+             1 / (2 - _CBRT2) / 2],
+            [1 / (2 - _CBRT2), -_CBRT2 / (2 - _CBRT2), 1 / (2 - _CBRT2), 1 / (2 - _CBRT2)])
+_OMELYAN_XI, _OMELYAN_LAM, _OMELYAN_CHI = 0.1786178958448091, -0.2123418310626054, -0.06626458266981849
+_OMELYAN = ([_OMELYAN_XI, _OMELYAN_CHI, 1.0 - 2.0 * (_OMELYAN_CHI + _OMELYAN_XI), _OMELYAN_CHI, _OMELYAN_XI],
+            [(1.0 - 2.0 * _OMELYAN_LAM) / 2.0, _OMELYAN_LAM, _OMELYAN_LAM, (1.0 - 2.0 * _OMELYAN_LAM) / 2.0,
+             (1.0 - 2.0 * _OMELYAN_LAM) / 2.0])
+_DP_A = [[1 / 5], [3 / 40, 9 / 40], [44 / 45, -56 / 15, 32 / 9],
+         [19372 / 6561, -25360 / 2187, 64448 / 6561, -212 / 729],
+         [9017 / 3168, -355 / 33, 46732 / 5247, 49 / 176, -5103 / 18656]]
+_DP_B = [35 / 384, 0, 500 / 1113, 125 / 192, -2187 / 6784, 11 / 84]
+
+
+def integrator_step(scheme, x, v, F, U, W, Wf, bf, Wi, dt, dt_scale, steps=1, topology=0, R=2.0, r=1.0):
+    """The reference's other integrators (gfn/integrators/runge_kutta/{euler,heun,
+    rk4,dormand_prince}.py, gfn/integrators/symplectic/{verlet,yoshida,forest_ruth,
+    omelyan}.py), with the combined-form acceleration.  Forest-Ruth and Yoshida
+    share their coefficients (theta = 1 / (2 - 2^(1/3)))."""
+    dtp = x.dtype.type
+    dt = dtp(dt) * dtp(dt_scale)
+    wrap = torus_wrap if topology == 1 else (lambda z: z)
+
+    def acc(xx, vv):
+        return combined_accel(xx, vv, F, U, W, Wf, bf, Wi, topology, R, r)
+
+    for _ in range(steps):
+        if scheme == "euler":
+            a = acc(x, v)
+            x, v = wrap(x + dt * v), v + dt * a
+        elif scheme == "heun":
+            dv1 = acc(x, v)
+            vp = v + dt * dv1
+            xp = wrap(x + dt * v)
+            dv2 = acc(xp, vp)
+            h2 = dt / dtp(2.0)
+            x, v = wrap(x + h2 * (v + vp)), v + h2 * (dv1 + dv2)
+        elif scheme == "rk4":
+            hh = dtp(0.5) * dt
+            dv1 = acc(x, v)
+            v2, x2 = v + hh * dv1, wrap(x + hh * v)
+            dv2 = acc(x2, v2)
+            v3, x3 = v + hh * dv2, wrap(x + hh * v2)
+            dv3 = acc(x3, v3)
+            v4, x4 = v + dt * dv3, wrap(x + dt * v3)
+            dv4 = acc(x4, v4)
+            s6 = dt / dtp(6.0)
+            x = wrap(x + s6 * (v + dtp(2) * v2 + dtp(2) * v3 + v4))
+            v = v + s6 * (dv1 + dtp(2) * dv2 + dtp(2) * dv3 + dv4)
+        elif scheme == "verlet":
+            hh = dtp(0.5) * dt
+            vh = v + hh * acc(x, v)
+            x = wrap(x + dt * vh)
+            v = vh + hh * acc(x, vh)
+        elif scheme in ("yoshida", "forest_ruth", "omelyan"):
+            cs, ds = _OMELYAN if scheme == "omelyan" else _YOSHIDA
+            for c, d in zip(cs, ds):
+                x = wrap(x + (dtp(c) * dt) * v)
+                v = v + (dtp(d) * dt) * acc(x, v)
+        elif scheme in ("rk45", "dormand_prince"):
+            kx, kv = [v], [acc(x, v)]
+            for row in _DP_A:
+                sx = sum((dtp(a) * kx[j] for j, a in enumerate(row)), dtp(0.0))
+                sv = sum((dtp(a) * kv[j] for j, a in enumerate(row)), dtp(0.0))
+                xs, vs = wrap(x + dt * sx), v + dt * sv
+                kx.append(vs)
+                kv.append(acc(xs, vs))
+            sx = sum((dtp(b) * kx[j] for j, b in enumerate(_DP_B) if b), dtp(0.0))
+            sv = sum((dtp(b) * kv[j] for j, b in enumerate(_DP_B) if b), dtp(0.0))
+            x, v = wrap(x + dt * sx), v + dt * sv
+        else:
+            raise ValueError(scheme)
+    return x, v
+
+
+def mlayer_step_generic(x, v, F, lp, heads, base_dt, scheme="leapfrog", topology=0):
+    """MLayer.forward for the torus and the non-leapfrog integrators
+    (gfn/layers/base.py:198-338): per head, the integrator with the stacked
+    gates (the leapfrog reads the forget gate only, the others add the input
+    gate); mixing reads [sin x, cos x, tanh(v/100)] and wraps x on the torus."""
+    B, d = x.shape
+    hd = d // heads
+    dtp = x.dtype.type
+    sc = softplus(lp["dt_params"].astype(x.dtype))
+    xo, vo = np.empty_like(x), np.empty_like(v)
+    for h in range(heads):
+        sl = slice(h * hd, (h + 1) * hd)
+        U = lp["U"][h] if "U" in lp else None
+        W = lp["W"][h] if "W" in lp else None
+        if scheme == "leapfrog":
+            xo[:, sl], vo[:, sl] = leapfrog_head_step_gated(x[:, sl], v[:, sl], F[:, sl], U, W, lp["Wf"][h],
+                                                            lp["bf"][h], None, base_dt, sc[h], 1, topology)
+        else:
+            xo[:, sl], vo[:, sl] = integrator_step(scheme, x[:, sl], v[:, sl], F[:, sl], U, W, lp["Wf"][h],
+                                                   lp["bf"][h], lp["Wi"][h], base_dt, sc[h], 1, topology)
+    if heads > 1:
+        if topology == 1:
+            mix_in = np.concatenate([np.sin(xo), np.cos(xo), np.tanh(vo / dtp(100.0))], -1)
+            xn = torus_wrap((mix_in @ lp["Wx"].T) + lp["bx"])
+        else:
+            xn = rmsnorm((xo @ lp["Wx"].T) + lp["bx"], lp["gx"])
+        vn = rmsnorm((vo @ lp["Wv"].T) + lp["bv"], lp["gv"])
+    else:
+        xn, vn = xo, vo
+    return xn, dtp(100.0) * np.tanh(vn / dtp(100.0))
+
+
+def manifold_forward_generic(x0, v0, forces, layers, heads, base_dt, scheme="leapfrog", topology=0):
+    """manifold_forward with mlayer_step_generic (gfn/model.py:377-402)."""
+    B, L, d = forces.shape
+    x, v = x0.copy(), v0.copy()
+    xs, vs = np.empty((B, L, d), x0.dtype), np.empty((B, L, d), x0.dtype)
+    for t in range(L):
+        for lp in layers:
+            x, v = mlayer_step_generic(x, v, forces[:, t], lp, heads, base_dt, scheme, topology)
+        xs[:, t], vs[:, t] = x, v
+    return xs, vs, x, v
+
+
 def rmsnorm(y, g):
     """torch.nn.RMSNorm(d, eps=None): y * rsqrt(mean(y^2) + eps) * g."""
     dt = y.dtype

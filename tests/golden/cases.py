@@ -22,7 +22,23 @@ CASES = {
     "c3s":   dict(V=50257, d=512, NL=12, H=8, rank=32, B=2, L=3, dt=0.1, seed=13, functional=True),
     "c4s":   dict(V=32000, d=1024, NL=24, H=16, rank=64, B=3, L=1, dt=0.1, seed=14),
     "c5s":   dict(V=32000, d=512, NL=8, H=8, rank=32, B=2, L=4, dt=0.1, seed=15),
+    # other integrators and the torus (model path of the multi-scheme kernel)
+    "heun_s":   dict(V=6, d=32, NL=2, H=2, rank=8, B=3, L=4, dt=0.1, seed=41, integrator="heun"),
+    "rk4_s":    dict(V=6, d=64, NL=2, H=4, rank=16, B=2, L=3, dt=0.1, seed=42, integrator="rk4"),
+    "euler_s":  dict(V=6, d=32, NL=2, H=2, rank=8, B=2, L=3, dt=0.1, seed=45, integrator="euler"),
+    "verlet_s": dict(V=6, d=32, NL=2, H=2, rank=8, B=2, L=3, dt=0.1, seed=46, integrator="verlet"),
+    "yoshida_s": dict(V=6, d=32, NL=2, H=2, rank=8, B=2, L=3, dt=0.1, seed=47, integrator="yoshida"),
+    "forest_ruth_s": dict(V=6, d=32, NL=2, H=2, rank=8, B=2, L=3, dt=0.1, seed=48,
+                          integrator="forest_ruth"),
+    "omelyan_s": dict(V=6, d=32, NL=2, H=2, rank=8, B=2, L=3, dt=0.1, seed=49, integrator="omelyan"),
+    "rk45_s":   dict(V=6, d=32, NL=2, H=2, rank=8, B=2, L=3, dt=0.1, seed=50, integrator="rk45"),
+    "torus_s":  dict(V=6, d=32, NL=2, H=2, rank=8, B=3, L=4, dt=0.1, seed=43, torus=True),
+    "torus_heun_s": dict(V=6, d=64, NL=2, H=4, rank=16, B=2, L=3, dt=0.1, seed=44, torus=True,
+                         integrator="heun"),
+    "torus_h1": dict(V=5, d=16, NL=2, H=1, rank=4, B=2, L=4, dt=0.1, seed=51, torus=True),
 }
+VARIANT_CASES = ["heun_s", "rk4_s", "euler_s", "verlet_s", "yoshida_s", "forest_ruth_s", "omelyan_s",
+                 "rk45_s", "torus_s", "torus_heun_s", "torus_h1"]
 
 # Gradient (BPTT) cases: upstream gradients on x_seq, v_seq and the final
 # state, gradients taken by the reference's autograd.  "gc5" has the C5 layer
@@ -45,9 +61,24 @@ def dt_param_init(dt, H):
     return np.array([base + 0.1 * i for i in range(H)], np.float32)
 
 
-def make_layer_params(rng, d, H, r, dt):
+def make_layer_params(rng, d, H, r, dt, torus=False):
     hd = d // H
     f = np.float32
+    if torus:
+        # ToroidalChristoffel: the gate reads [sin x, cos x]; the x mixer reads
+        # [sin x, cos x, tanh(v / 100)]; no U / W
+        return dict(
+            Wf=(rng.standard_normal((H, hd, 2 * hd)) * 0.1).astype(f),
+            bf=(rng.standard_normal((H, hd)) * 0.5).astype(f),
+            Wi=(rng.standard_normal((H, hd, hd)) * 0.1).astype(f),
+            dt_params=(dt_param_init(dt, H) + rng.standard_normal(H).astype(f) * 0.05).astype(f),
+            Wx=(rng.standard_normal((d, 3 * d)) / math.sqrt(3 * d)).astype(f),
+            bx=(rng.standard_normal(d) * 0.1).astype(f),
+            gx=(1.0 + rng.standard_normal(d) * 0.1).astype(f),
+            Wv=(rng.standard_normal((d, d)) / math.sqrt(d)).astype(f),
+            bv=(rng.standard_normal(d) * 0.1).astype(f),
+            gv=(1.0 + rng.standard_normal(d) * 0.1).astype(f),
+        )
     return dict(
         U=(rng.standard_normal((H, hd, r)) * 0.2).astype(f),
         W=(rng.standard_normal((H, hd, r)) * 0.2).astype(f),
@@ -88,7 +119,7 @@ def make_params(cfg):
     P = dict(
         x0=(rng.standard_normal(d) * 0.02).astype(f),
         v0=(rng.standard_normal(d) * 0.01).astype(f),
-        layers=[make_layer_params(rng, d, H, r, cfg["dt"]) for _ in range(NL)],
+        layers=[make_layer_params(rng, d, H, r, cfg["dt"], cfg.get("torus", False)) for _ in range(NL)],
     )
     if cfg.get("functional"):
         P["func"] = make_functional_params(rng, d)
@@ -168,8 +199,9 @@ def load_into_layer(layer, cfg, lp):
     with torch.no_grad():
         layer.dt_params.copy_(T(lp["dt_params"]))
         for h, ch in enumerate(layer.christoffels):
-            ch.U.copy_(T(lp["U"][h]))
-            ch.W.copy_(T(lp["W"][h]))
+            if "U" in lp:
+                ch.U.copy_(T(lp["U"][h]))
+                ch.W.copy_(T(lp["W"][h]))
             ch.forget_gate.weight.copy_(T(lp["Wf"][h]))
             ch.forget_gate.bias.copy_(T(lp["bf"][h]))
             ch.input_gate.weight.copy_(T(lp["Wi"][h]))
@@ -186,5 +218,8 @@ def model_kwargs(cfg):
     pc = {}
     if cfg.get("functional"):
         pc = {"embedding": {"type": "functional", "mode": "binary", "coord_dim": 16}}
+    if cfg.get("torus"):
+        pc = dict(pc, topology={"type": "torus"})
     return dict(vocab_size=cfg["V"], dim=cfg["d"], depth=cfg["NL"], rank=cfg["rank"],
-                heads=cfg["H"], integrator_type="leapfrog", base_dt=cfg["dt"], physics_config=pc)
+                heads=cfg["H"], integrator_type=cfg.get("integrator", "leapfrog"), base_dt=cfg["dt"],
+                physics_config=pc)

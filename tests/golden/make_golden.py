@@ -291,6 +291,9 @@ INIT_CONFIGS = {
                       base_dt=0.1, physics_config={"embedding": {"type": "functional"}}),
     "scan_init": dict(vocab_size=50, dim=32, depth=2, heads=4, integrator_type="leapfrog",
                       use_scan=True),
+    "heun_init": dict(vocab_size=9, dim=32, depth=2, rank=8, heads=2, base_dt=0.1),
+    "torus_init": dict(vocab_size=9, dim=32, depth=2, rank=8, heads=2, integrator_type="rk4", base_dt=0.1,
+                       physics_config={"topology": {"type": "torus"}}),
 }
 
 

@@ -77,11 +77,16 @@ def test_init_matches_reference_checksums():
 
 
 def test_unsupported_configurations_raise():
-    with pytest.raises(gfn.GfnError):
-        gfn.Manifold(vocab_size=4, dim=32, depth=1, heads=2, integrator_type="heun")
+    for integ in ("coupling", "neural"):
+        with pytest.raises(gfn.GfnError):
+            gfn.Manifold(vocab_size=4, dim=32, depth=1, heads=2, integrator_type=integ)
     with pytest.raises(gfn.GfnError):
         gfn.Manifold(vocab_size=4, dim=32, depth=1, heads=2, integrator_type="leapfrog",
+                     physics_config={"mixture": {"enabled": True}})
+    # the torus and the other integrators build (generic path)
+    m = gfn.Manifold(vocab_size=4, dim=32, depth=1, heads=2, integrator_type="heun",
                      physics_config={"topology": {"type": "torus"}})
+    assert m.layers[0].generic and m.layers[0].out_proj_x.in_features == 96
 
 
 def test_no_cpu_fallback():

@@ -113,3 +113,19 @@ def test_oracle_single_head_ops_match_reference():
                                         g["ig_bf"], None, 0.1, np.float32(0.95), 2, topology=1)
     rowwise_close(xn, g["tl_xn"], what="torus leapfrog x")
     rowwise_close(vn, g["tl_vn"], what="torus leapfrog v")
+
+
+@pytest.mark.parametrize("name", C.VARIANT_CASES)
+def test_oracle_generic_variants_match_reference(name):
+    """The other integrators and the torus, whole model, against the reference."""
+    cfg = C.CASES[name]
+    P = C.make_params(cfg)
+    g = load(name)
+    F = C.oracle_forces(P, g["ids"])
+    B = cfg["B"]
+    x0 = np.broadcast_to(P["x0"], (B, cfg["d"])).copy()
+    v0 = np.broadcast_to(P["v0"], (B, cfg["d"])).copy()
+    xs, vs, x, v = O.manifold_forward_generic(x0, v0, F, P["layers"], cfg["H"], cfg["dt"],
+                                              cfg.get("integrator", "leapfrog"), 1 if cfg.get("torus") else 0)
+    close(xs, g["x_seq"], 1e-4, 1e-5)
+    close(vs, g["v_seq"], 1e-4, 1e-5)
