@@ -131,7 +131,14 @@ int gfn_christoffel_torus(const float* v, const float* x, float* gamma, int batc
  * h * head_dim); stacks per head: U, W [heads, head_dim, rank],
  * W_forget [heads, head_dim, fin] (fin = head_dim, 2 head_dim on the torus),
  * b_forget [heads, head_dim], W_input [heads, head_dim, head_dim].
- * dt_scales: NULL, 1 value, one per head (heads > 1) or one per row (heads == 1).
+ * dt_scales: NULL, 1 value, one per head (heads > 1), one per row (heads == 1),
+ * or [batch][heads] (the dynamic-time gate, gfn/layers/base.py:222-229).
+ * Active inference (the Christoffel term times M, gfn/geometry/reactive.py:53-81,
+ * gfn/geometry/toroidal.py:126-141): plasticity != 0 multiplies by
+ * 1 + plasticity tanh(mean_k v_k^2); singularity_mode 1 (low-rank: soft,
+ * sigmoid(10 (p - thresh))) or 2 (torus: p > thresh) multiplies by
+ * 1 + s (strength - 1), p = sigmoid(feat(x) . V + b), V_stack [heads, fin],
+ * V_bias [heads] or NULL; singularity_mode 0 leaves V unused.
  * head_dim <= 256 (the gates' weights must fit in shared memory).
  */
 int gfn_integrator_heads(int scheme, const float* x, const float* v, const float* f,
@@ -139,7 +146,9 @@ int gfn_integrator_heads(int scheme, const float* x, const float* v, const float
                          const float* b_forget_stack, const float* W_input_stack, float* x_new,
                          float* v_new, float dt, const float* dt_scales, int dt_scales_count,
                          int batch, int heads, int head_dim, int rank, int steps, int topology,
-                         float R_val, float r_val, gfn_stream_t stream);
+                         float R_val, float r_val, float plasticity, const float* V_stack,
+                         const float* V_bias, int singularity_mode, float sing_thresh,
+                         float sing_strength, gfn_stream_t stream);
 
 /* ------------------------------------------------------------------------
  * Backward of the Christoffel term.  Replaces launch_christoffel_backward

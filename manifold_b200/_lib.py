@@ -62,7 +62,7 @@ _SIGS = {
     "gfn_leapfrog_fused_gated": [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _f, _p, _i, _i, _i, _i, _i,
                                  _i, _f, _f, _f, _p],
     "gfn_integrator_heads": [_i, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _f, _p, _i, _i, _i, _i, _i,
-                             _i, _i, _f, _f, _p],
+                             _i, _i, _f, _f, _f, _p, _p, _i, _f, _f, _p],
     "gfn_christoffel_torus": [_p, _p, _p, _i, _i, _f, _f, _p],
     "gfn_christoffel_backward_workspace_floats": [_i, _i, _i],
     "gfn_christoffel_backward": [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i, _i, _i, _f, _f, _f,

@@ -377,6 +377,32 @@ GFN_DEV void stage_weights(const Params& a, float* sm, const Smem& L, bool fric,
   __syncthreads();
 }
 
+GFN_DEV void stage_weights_rt(const Params& a, float* sm, const Smem& L, int rk, bool fric, bool igate) {
+  const int hd = a.hd;
+  if (a.U) {
+    for (int i = threadIdx.x; i < hd * rk; i += blockDim.x) {
+      sm[L.U + i] = a.U[i];
+      sm[L.W + i] = a.W[i];
+    }
+  }
+  if (fric) {
+    for (int i = threadIdx.x; i < hd * a.fin; i += blockDim.x) {
+      const int j = i / a.fin, k = i - j * a.fin;
+      sm[L.Wf + j * L.ldf + k] = a.Wf[i];
+    }
+    for (int i = threadIdx.x; i < hd; i += blockDim.x) sm[L.bf + i] = a.bf ? a.bf[i] : 0.f;
+  } else {
+    for (int i = threadIdx.x; i < hd; i += blockDim.x) sm[L.bf + i] = 0.f;
+  }
+  if (igate) {
+    for (int i = threadIdx.x; i < hd * hd; i += blockDim.x) {
+      const int j = i / hd, k = i - j * hd;
+      sm[L.Wi + j * L.ldi + k] = a.Wi[i];
+    }
+  }
+  __syncthreads();
+}
+
 GFN_DEV float row_dt_scale(const Params& a, int row) {
   if (!a.dt_scale) return 1.f;
   return a.dt_scale[a.dt_scale_n == 1 ? 0 : row];
@@ -652,13 +678,92 @@ struct IntegArgs {
   long long ld;    // row stride of x, v, f, x_out, v_out (elements); head h at column h * hd
   long long hU, hWf, hWi, hb;  // per-head strides of U / W, Wf, Wi, bf (elements)
   int dts_per_head;            // dt_scale holds one value per head (else 1 or B values)
+  int dts_row_head;            // dt_scale holds [B][heads] values (dynamic time)
   float c[20];                 // scheme coefficients (float32, as the reference's tensors see them)
+  // active inference (gfn/geometry/reactive.py:53-81, gfn/geometry/toroidal.py:126-141):
+  // the Christoffel term times M = (1 + plasticity tanh(mean v^2)) * (1 + s (strength - 1)),
+  // s = sigmoid(10 (sigmoid(feat(x) . V + b) - thr)) (low-rank) or [sigmoid(...) > thr] (torus)
+  float plasticity;            // 0: off
+  const float* Vw;             // [heads][fin] potential weights (null: no singularities)
+  const float* Vb;             // [heads] potential bias (null: none)
+  int sing_hard;
+  float sing_thr, sing_strength;
+  int rank;                    // per-head Christoffel rank (<= 16)
 };
 
-template <int RK, int EPL>
+// The active-inference factor M of one row (warp-uniform).
+template <int EPL>
+GFN_DEV float active_scale(const float (&x)[EPL], const float (&v)[EPL], const IntegArgs& ia, const float* Vw,
+                           float Vb, int hd, int topo, int lane) {
+  float m = 1.f;
+  if (ia.plasticity != 0.f) {
+    float s2 = 0.f;
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) s2 = fmaf(v[e], v[e], s2);
+    const float energy = tanhf(warp_sum(s2) / (float)hd);
+    m = m * (1.f + ia.plasticity * energy);
+  }
+  if (Vw) {
+    float pz = 0.f;
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) {
+      const int k = lane + 32 * e;
+      if (k < hd) {
+        if (topo) pz = fmaf(sinf(x[e]), Vw[k], fmaf(cosf(x[e]), Vw[hd + k], pz));
+        else pz = fmaf(x[e], Vw[k], pz);
+      }
+    }
+    const float pot = sigmoid_f(warp_sum(pz) + Vb);
+    const float sg = ia.sing_hard ? (pot > ia.sing_thr ? 1.f : 0.f) : sigmoid_f(10.f * (pot - ia.sing_thr));
+    m = m * (1.f + sg * (ia.sing_strength - 1.f));
+  }
+  return m;
+}
+
+// Low-rank pre-activation ((vU)^2 s) W^T with the rank a runtime value
+// (<= 16): the multi-scheme kernel is instantiated per lane width only.
+template <int EPL>
+GFN_DEV void lowrank_pre_rt(const float (&v)[EPL], const float* __restrict__ U, const float* __restrict__ W,
+                            int hd, int rk, int lane, float (&pre)[EPL]) {
+  float p[16];
+#pragma unroll
+  for (int q = 0; q < 16; ++q) {
+    p[q] = 0.f;
+    if (q < rk) {
+      float a = 0.f;
+#pragma unroll
+      for (int e = 0; e < EPL; ++e) {
+        const int k = lane + 32 * e;
+        if (k < hd) a = fmaf(v[e], U[k * rk + q], a);
+      }
+      p[q] = warp_sum(a);
+    }
+  }
+  float ss = 0.f;
+#pragma unroll
+  for (int q = 0; q < 16; ++q)
+    if (q < rk) ss = fmaf(p[q], p[q], ss);
+  const float s = 1.f / ((1.f + sqrtf(ss)) + 1e-6f);
+#pragma unroll
+  for (int e = 0; e < EPL; ++e) {
+    const int k = lane + 32 * e;
+    float acc = 0.f;
+    if (k < hd) {
+#pragma unroll
+      for (int q = 0; q < 16; ++q)
+        if (q < rk) acc = fmaf((p[q] * p[q]) * s, W[k * rk + q], acc);
+    }
+    pre[e] = acc;
+  }
+}
+
+template <int EPL>
 GFN_DEV void accel(const float (&x)[EPL], const float (&v)[EPL], const float (&F)[EPL], const float (&zin)[EPL],
-                   const float* sm, const Smem& L, float* rb, const Params& a, int lane, float (&acc)[EPL]) {
+                   const float* sm, const Smem& L, float* rb, const Params& a, const IntegArgs& ia,
+                   const float* Vw, float Vb, int lane, float (&acc)[EPL]) {
   const int hd = a.hd;
+  const bool active = ia.plasticity != 0.f || Vw != nullptr;
+  const float M = active ? active_scale<EPL>(x, v, ia, Vw, Vb, hd, a.topo, lane) : 1.f;
   float mu[EPL];
   if (a.Wf) {
     friction<EPL>(x, zin, sm, L, rb, hd, a.fin, a.topo, lane, mu);
@@ -672,32 +777,14 @@ GFN_DEV void accel(const float (&x)[EPL], const float (&v)[EPL], const float (&F
     float g[EPL];
     gamma_torus<EPL>(v, x, hd, a.R, a.r, lane, g);
 #pragma unroll
-    for (int e = 0; e < EPL; ++e) acc[e] = F[e] - (g[e] + mu[e] * v[e]);
+    for (int e = 0; e < EPL; ++e) acc[e] = F[e] - ((active ? g[e] * M : g[e]) + mu[e] * v[e]);
   } else {
-    float p[RK];
-#pragma unroll
-    for (int q = 0; q < RK; ++q) {
-      float s0 = 0.f;
-#pragma unroll
-      for (int e = 0; e < EPL; ++e) {
-        const int k = lane + 32 * e;
-        if (k < hd) s0 = fmaf(v[e], sm[L.U + k * RK + q], s0);
-      }
-      p[q] = warp_sum(s0);
-    }
-    float ss = 0.f;
-#pragma unroll
-    for (int q = 0; q < RK; ++q) ss = fmaf(p[q], p[q], ss);
-    const float s = 1.f / ((1.f + sqrtf(ss)) + 1e-6f);
+    float pre[EPL];
+    lowrank_pre_rt<EPL>(v, sm + L.U, sm + L.W, hd, ia.rank, lane, pre);
 #pragma unroll
     for (int e = 0; e < EPL; ++e) {
-      const int k = lane + 32 * e;
-      float pre = 0.f;
-      if (k < hd) {
-#pragma unroll
-        for (int q = 0; q < RK; ++q) pre = fmaf((p[q] * p[q]) * s, sm[L.W + k * RK + q], pre);
-      }
-      acc[e] = F[e] - 20.f * tanhf((pre + mu[e] * v[e]) / 20.f);
+      const float cc = 20.f * tanhf((pre[e] + mu[e] * v[e]) / 20.f);
+      acc[e] = F[e] - (active ? cc * M : cc);
     }
   }
 }
@@ -712,17 +799,20 @@ GFN_DEV void wrap_if(float (&x)[EPL], int topo) {
 
 // One row per warp; blockIdx.y = head.  Weights of the head are staged in
 // shared memory as for the leapfrog kernels.
-template <int RK, int EPL>
+template <int EPL>
 __global__ void __launch_bounds__(WARPS * 32) integrate_kernel(const IntegArgs ia) {
   extern __shared__ __align__(16) float sm[];
   Params a = ia.p;
+  const int RK = ia.rank;
   const int hh = blockIdx.y;
   if (a.U) { a.U += hh * ia.hU; a.W += hh * ia.hU; }
   if (a.Wf) { a.Wf += hh * ia.hWf; if (a.bf) a.bf += hh * ia.hb; }
   if (a.Wi) a.Wi += hh * ia.hWi;
+  const float* Vw = ia.Vw ? ia.Vw + (long long)hh * a.fin : nullptr;
+  const float Vb = ia.Vb ? ia.Vb[hh] : 0.f;
   const bool fric = a.Wf != nullptr, igate = a.Wi != nullptr;
   const Smem L = smem_layout(a.hd, RK, a.fin, fric, igate);
-  stage_weights<RK>(a, sm, L, fric, igate);
+  stage_weights_rt(a, sm, L, RK, fric, igate);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row = blockIdx.x * WARPS + warp;
   if (row >= a.B) return;
@@ -735,14 +825,16 @@ __global__ void __launch_bounds__(WARPS * 32) integrate_kernel(const IntegArgs i
   row_load<EPL>(F, a.f ? a.f + off : nullptr, hd, lane);
   input_gate<EPL>(F, sm, L, rb, hd, igate, lane, zin);
   float sc = 1.f;
-  if (a.dt_scale) sc = a.dt_scale[ia.dts_per_head ? hh : (a.dt_scale_n == 1 ? 0 : row)];
+  if (a.dt_scale)
+    sc = a.dt_scale[ia.dts_row_head ? (long long)row * ia.heads + hh
+                                    : ia.dts_per_head ? hh : (a.dt_scale_n == 1 ? 0 : row)];
   const float dt = a.dt * sc;
   const float* c = ia.c;
   float k1[EPL], k2[EPL], k3[EPL], k4[EPL], xt[EPL], vt[EPL];
   for (int st = 0; st < a.steps; ++st) {
     switch (ia.scheme) {
       case kEuler: {
-        accel<RK, EPL>(x, v, F, zin, sm, L, rb, a, lane, k1);
+        accel<EPL>(x, v, F, zin, sm, L, rb, a, ia, Vw, Vb, lane, k1);
 #pragma unroll
         for (int e = 0; e < EPL; ++e) {
           x[e] = x[e] + dt * v[e];
@@ -752,14 +844,14 @@ __global__ void __launch_bounds__(WARPS * 32) integrate_kernel(const IntegArgs i
         break;
       }
       case kHeun: {
-        accel<RK, EPL>(x, v, F, zin, sm, L, rb, a, lane, k1);
+        accel<EPL>(x, v, F, zin, sm, L, rb, a, ia, Vw, Vb, lane, k1);
 #pragma unroll
         for (int e = 0; e < EPL; ++e) {
           vt[e] = v[e] + dt * k1[e];
           xt[e] = x[e] + dt * v[e];
         }
         wrap_if<EPL>(xt, a.topo);
-        accel<RK, EPL>(xt, vt, F, zin, sm, L, rb, a, lane, k2);
+        accel<EPL>(xt, vt, F, zin, sm, L, rb, a, ia, Vw, Vb, lane, k2);
         const float h2 = dt / 2.f;
 #pragma unroll
         for (int e = 0; e < EPL; ++e) {
@@ -773,7 +865,7 @@ __global__ void __launch_bounds__(WARPS * 32) integrate_kernel(const IntegArgs i
         // k*: velocity slopes; the position slopes are the stage velocities
         float dx2[EPL], dx3[EPL];
         const float hdt = 0.5f * dt;
-        accel<RK, EPL>(x, v, F, zin, sm, L, rb, a, lane, k1);
+        accel<EPL>(x, v, F, zin, sm, L, rb, a, ia, Vw, Vb, lane, k1);
 #pragma unroll
         for (int e = 0; e < EPL; ++e) {
           vt[e] = v[e] + hdt * k1[e];
@@ -782,7 +874,7 @@ __global__ void __launch_bounds__(WARPS * 32) integrate_kernel(const IntegArgs i
         wrap_if<EPL>(xt, a.topo);
 #pragma unroll
         for (int e = 0; e < EPL; ++e) dx2[e] = vt[e];
-        accel<RK, EPL>(xt, vt, F, zin, sm, L, rb, a, lane, k2);
+        accel<EPL>(xt, vt, F, zin, sm, L, rb, a, ia, Vw, Vb, lane, k2);
 #pragma unroll
         for (int e = 0; e < EPL; ++e) {
           vt[e] = v[e] + hdt * k2[e];
@@ -791,14 +883,14 @@ __global__ void __launch_bounds__(WARPS * 32) integrate_kernel(const IntegArgs i
         wrap_if<EPL>(xt, a.topo);
 #pragma unroll
         for (int e = 0; e < EPL; ++e) dx3[e] = vt[e];
-        accel<RK, EPL>(xt, vt, F, zin, sm, L, rb, a, lane, k3);
+        accel<EPL>(xt, vt, F, zin, sm, L, rb, a, ia, Vw, Vb, lane, k3);
 #pragma unroll
         for (int e = 0; e < EPL; ++e) {
           vt[e] = v[e] + dt * k3[e];
           xt[e] = x[e] + dt * dx3[e];
         }
         wrap_if<EPL>(xt, a.topo);
-        accel<RK, EPL>(xt, vt, F, zin, sm, L, rb, a, lane, k4);
+        accel<EPL>(xt, vt, F, zin, sm, L, rb, a, ia, Vw, Vb, lane, k4);
         const float s6 = dt / 6.f;
 #pragma unroll
         for (int e = 0; e < EPL; ++e) {
@@ -810,14 +902,14 @@ __global__ void __launch_bounds__(WARPS * 32) integrate_kernel(const IntegArgs i
       }
       case kVerlet: {
         const float hdt = 0.5f * dt;
-        accel<RK, EPL>(x, v, F, zin, sm, L, rb, a, lane, k1);
+        accel<EPL>(x, v, F, zin, sm, L, rb, a, ia, Vw, Vb, lane, k1);
 #pragma unroll
         for (int e = 0; e < EPL; ++e) {
           v[e] = v[e] + hdt * k1[e];
           x[e] = x[e] + dt * v[e];
         }
         wrap_if<EPL>(x, a.topo);
-        accel<RK, EPL>(x, v, F, zin, sm, L, rb, a, lane, k2);
+        accel<EPL>(x, v, F, zin, sm, L, rb, a, ia, Vw, Vb, lane, k2);
 #pragma unroll
         for (int e = 0; e < EPL; ++e) v[e] = v[e] + hdt * k2[e];
         break;
@@ -835,7 +927,7 @@ __global__ void __launch_bounds__(WARPS * 32) integrate_kernel(const IntegArgs i
           for (int e = 0; e < EPL; ++e) x[e] = x[e] + cd * v[e];
           wrap_if<EPL>(x, a.topo);
           const float kd = c[5 + (i < nd - 1 ? i : nd - 2)] * dt;
-          accel<RK, EPL>(x, v, F, zin, sm, L, rb, a, lane, k1);
+          accel<EPL>(x, v, F, zin, sm, L, rb, a, ia, Vw, Vb, lane, k1);
 #pragma unroll
           for (int e = 0; e < EPL; ++e) v[e] = v[e] + kd * k1[e];
         }
@@ -847,7 +939,7 @@ __global__ void __launch_bounds__(WARPS * 32) integrate_kernel(const IntegArgs i
         float kv[6][EPL], kx[6][EPL];
 #pragma unroll
         for (int e = 0; e < EPL; ++e) kx[0][e] = v[e];
-        accel<RK, EPL>(x, v, F, zin, sm, L, rb, a, lane, kv[0]);
+        accel<EPL>(x, v, F, zin, sm, L, rb, a, ia, Vw, Vb, lane, kv[0]);
         int ci = 0;
 #pragma unroll 1
         for (int sidx = 1; sidx < 6; ++sidx) {
@@ -873,7 +965,7 @@ __global__ void __launch_bounds__(WARPS * 32) integrate_kernel(const IntegArgs i
             kx[sidx][e] = vt[e];
           }
           wrap_if<EPL>(xt, a.topo);
-          accel<RK, EPL>(xt, vt, F, zin, sm, L, rb, a, lane, kv[sidx]);
+          accel<EPL>(xt, vt, F, zin, sm, L, rb, a, ia, Vw, Vb, lane, kv[sidx]);
         }
         // b5 = c[15..] : weights of k1, k3, k4, k5, k6 (b2 = 0)
         const float* b = c + 15;
@@ -889,12 +981,22 @@ __global__ void __launch_bounds__(WARPS * 32) integrate_kernel(const IntegArgs i
       }
       case kLeapfrog: {
         const float h = 0.5f * dt;
-        float sg[EPL], g[EPL], t[EPL], p[RK], s;
+        float sg[EPL], g[EPL];
 #pragma unroll
         for (int half = 0; half < 2; ++half) {
           if (fric) friction<EPL>(x, zin, sm, L, rb, hd, a.fin, a.topo, lane, sg);
-          if (a.topo) gamma_torus<EPL>(v, x, hd, a.R, a.r, lane, g);
-          else gamma_lowrank<RK, EPL>(v, sm + L.U, sm + L.W, hd, lane, p, s, t, g);
+          if (a.topo) {
+            gamma_torus<EPL>(v, x, hd, a.R, a.r, lane, g);
+          } else {
+            lowrank_pre_rt<EPL>(v, sm + L.U, sm + L.W, hd, RK, lane, g);
+#pragma unroll
+            for (int e = 0; e < EPL; ++e) g[e] = soft_clamp20(g[e]);
+          }
+          if (ia.plasticity != 0.f || Vw) {
+            const float M = active_scale<EPL>(x, v, ia, Vw, Vb, hd, a.topo, lane);
+#pragma unroll
+            for (int e = 0; e < EPL; ++e) g[e] = g[e] * M;
+          }
 #pragma unroll
           for (int e = 0; e < EPL; ++e) {
             const float mu = fric ? sg[e] * 5.f : 0.f;

@@ -10,17 +10,15 @@ using namespace gfn_head_ops;
 
 namespace {
 
-template <int RK, int EPL>
-struct IntegLaunch {
-  static int run(const hops::IntegArgs& ia, size_t smem, cudaStream_t s) {
-    cudaError_t e = cudaFuncSetAttribute(hops::integrate_kernel<RK, EPL>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return cuda_status(e, "integrator: shared memory attribute");
-    const dim3 grid((unsigned)((ia.p.B + hops::WARPS - 1) / hops::WARPS), (unsigned)ia.heads);
-    hops::integrate_kernel<RK, EPL><<<grid, hops::WARPS * 32, smem, s>>>(ia);
-    return launch_status("integrate_kernel");
-  }
-};
+template <int EPL>
+int integ_launch(const hops::IntegArgs& ia, size_t smem, cudaStream_t s) {
+  cudaError_t e = cudaFuncSetAttribute(hops::integrate_kernel<EPL>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)smem);
+  if (e != cudaSuccess) return cuda_status(e, "integrator: shared memory attribute");
+  const dim3 grid((unsigned)((ia.p.B + hops::WARPS - 1) / hops::WARPS), (unsigned)ia.heads);
+  hops::integrate_kernel<EPL><<<grid, hops::WARPS * 32, smem, s>>>(ia);
+  return launch_status("integrate_kernel");
+}
 
 // Scheme coefficients as float32 (the reference multiplies its Python-float
 // coefficients into float32 tensors).
@@ -65,8 +63,11 @@ int gfn_integrator_heads(int scheme, const float* x, const float* v, const float
                          const float* W_stack, const float* W_forget_stack, const float* b_forget_stack,
                          const float* W_input_stack, float* x_new, float* v_new, float dt, const float* dt_scales,
                          int dt_scales_count, int batch, int heads, int head_dim, int rank, int steps, int topology,
-                         float R_val, float r_val, gfn_stream_t stream) {
-  int st = check_common("integrator", batch, head_dim, rank, topology, 0.f, R_val, r_val);
+                         float R_val, float r_val, float plasticity, const float* V_stack, const float* V_bias,
+                         int singularity_mode, float sing_thresh, float sing_strength, gfn_stream_t stream) {
+  if (topology == 0 && (rank < 1 || rank > 16))
+    return fail(GFN_ERR_UNSUPPORTED, "integrator: rank %d not in [1, 16]", rank);
+  int st = check_common("integrator", batch, head_dim, topology ? 4 : 4, topology, 0.f, R_val, r_val);
   if (st) return st;
   if (scheme < hops::kEuler || scheme > hops::kLeapfrog)
     return fail(GFN_ERR_UNSUPPORTED, "integrator: scheme %d", scheme);
@@ -74,9 +75,13 @@ int gfn_integrator_heads(int scheme, const float* x, const float* v, const float
   if (!x || !v || !x_new || !v_new || (topology == 0 && (!U_stack || !W_stack)))
     return fail(GFN_ERR_INVALID, "integrator: NULL operand");
   if (steps < 0) return fail(GFN_ERR_INVALID, "integrator: steps %d", steps);
-  if (dt_scales && dt_scales_count != 1 && dt_scales_count != (heads > 1 ? heads : batch))
-    return fail(GFN_ERR_INVALID, "integrator: dt_scales_count %d (need 1, or one per %s)", dt_scales_count,
-                heads > 1 ? "head" : "row");
+  const long long per_rh = (long long)batch * heads;
+  if (dt_scales && dt_scales_count != 1 && dt_scales_count != (heads > 1 ? heads : batch) &&
+      dt_scales_count != per_rh)
+    return fail(GFN_ERR_INVALID, "integrator: dt_scales_count %d (need 1, one per %s, or batch * heads)",
+                dt_scales_count, heads > 1 ? "head" : "row");
+  if (singularity_mode < 0 || singularity_mode > 2 || (singularity_mode && !V_stack))
+    return fail(GFN_ERR_INVALID, "integrator: singularity mode %d needs V_stack", singularity_mode);
   if (b_forget_stack && !W_forget_stack) return fail(GFN_ERR_INVALID, "integrator: b_forget without W_forget");
   if (W_input_stack && !f) return fail(GFN_ERR_INVALID, "integrator: W_input without a force");
   if (batch == 0) return GFN_OK;
@@ -92,11 +97,25 @@ int gfn_integrator_heads(int scheme, const float* x, const float* v, const float
   ia.scheme = scheme; ia.heads = heads; ia.ld = (long long)heads * head_dim;
   ia.hU = (long long)head_dim * rank; ia.hWf = (long long)head_dim * fin; ia.hWi = (long long)head_dim * head_dim;
   ia.hb = head_dim;
+  ia.dts_row_head = dt_scales && heads > 1 && dt_scales_count == per_rh && per_rh != heads;
   ia.dts_per_head = dt_scales && heads > 1 && dt_scales_count == heads;
+  ia.plasticity = plasticity;
+  ia.Vw = singularity_mode ? V_stack : nullptr;
+  ia.Vb = singularity_mode ? V_bias : nullptr;
+  ia.sing_hard = singularity_mode == 2;
+  ia.sing_thr = sing_thresh;
+  ia.sing_strength = sing_strength;
   scheme_coeffs(scheme, ia.c);
   const size_t smem = smem_bytes(head_dim, rank, fin, W_forget_stack != nullptr, W_input_stack != nullptr);
   if (smem > kMaxSmem) return fail(GFN_ERR_RESOURCES, "integrator: head dim %d too large for the gates", head_dim);
-  return dispatch<IntegLaunch>(rank, head_dim, ia, smem, reinterpret_cast<cudaStream_t>(stream));
+  ia.rank = rank;
+  cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);
+  switch (epl_for(head_dim)) {
+    case 1: return integ_launch<1>(ia, smem, cs);
+    case 2: return integ_launch<2>(ia, smem, cs);
+    case 4: return integ_launch<4>(ia, smem, cs);
+    default: return integ_launch<8>(ia, smem, cs);
+  }
 }
 
 }  // extern "C"

@@ -486,13 +486,16 @@ SCHEMES = {"euler": 0, "heun": 1, "rk4": 2, "verlet": 3, "yoshida": 4, "forest_r
 
 
 def integrator_heads(scheme, x, v, f, U, W, dt, dt_scale, steps=1, topology=0, Wf=None, bf=None,
-                     Wi=None, heads=1, R=2.0, r=1.0):
+                     Wi=None, heads=1, R=2.0, r=1.0, plasticity=0.0, V=None, V_bias=None,
+                     singularity=0, sing_thresh=1.0, sing_strength=1.0):
     """One launch of integrator `scheme` (a SCHEMES name or id) over every head.
 
     x, v, f: [B, heads * hd]; U, W: [heads, hd, rank] (or [hd, rank] for one
     head; unused on the torus); Wf [heads, hd, fin], bf [heads, hd], Wi
     [heads, hd, hd] (the friction gate, optional); dt_scale: a number, one
-    value per head (heads > 1) or per row (heads == 1).  Returns (x_new, v_new).
+    value per head (heads > 1), per row (heads == 1) or [B, heads].  Active
+    inference: plasticity, and singularity 1 (soft) / 2 (hard) with the
+    potential weights V [heads, fin] and V_bias [heads].  Returns (x_new, v_new).
     """
     sid = SCHEMES[scheme] if isinstance(scheme, str) else int(scheme)
     require_cuda(x, v, f, U, W, Wf, bf, Wi)
@@ -509,10 +512,12 @@ def integrator_heads(scheme, x, v, f, U, W, dt, dt_scale, steps=1, topology=0, W
         U = W = None
         rank = 4
     dts = _dt_scales(dt_scale, x)
+    V, V_bias = _f32c(V, "V"), _f32c(V_bias, "V_bias")
     x_new, v_new = torch.empty_like(x), torch.empty_like(v)
     call("gfn_integrator_heads", sid, ptr(x), ptr(v), ptr(f), ptr(U), ptr(W), ptr(Wf), ptr(bf), ptr(Wi),
          ptr(x_new), ptr(v_new), float(dt), ptr(dts), dts.numel(), B, int(heads), hd, rank, int(steps),
-         int(topology), float(R), float(r), _stream(x))
+         int(topology), float(R), float(r), float(plasticity), ptr(V), ptr(V_bias), int(singularity),
+         float(sing_thresh), float(sing_strength), _stream(x))
     return x_new, v_new
 
 

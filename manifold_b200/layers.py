@@ -47,9 +47,15 @@ def _check_config(physics_config, integrator_type):
         if pc.get(key, {}).get("enabled", False):
             raise GfnError(f"physics_config[{key!r}] is not implemented on this build")
     ai = pc.get("active_inference", {})
-    if ai.get("enabled", False) or ai.get("dynamic_time", {}).get("enabled", False) \
-            or ai.get("recursive_geodesics", {}).get("enabled", False):
-        raise GfnError("active-inference options are not implemented on this build")
+    torus = pc.get("topology", {}).get("type", "euclidean").lower() == "torus"
+    if (integrator_type == "leapfrog" and not torus and ai.get("enabled", False)
+            and (ai.get("reactive_curvature", {}).get("enabled", False)
+                 or ai.get("singularities", {}).get("enabled", False))):
+        # ReactiveChristoffel multiplies the (gamma, mu) pair the leapfrog asks
+        # for by a tensor (gfn/geometry/reactive.py:54-72 after
+        # gfn/integrators/symplectic/leapfrog.py:58): the reference fails here
+        raise GfnError("reactive curvature / singularities with the Euclidean leapfrog: the "
+                       "reference raises on this combination (tuple times tensor)")
     if pc.get("symmetries", {}).get("isomeric_groups"):
         raise GfnError("isomeric head groups are not implemented on this build")
 
@@ -101,7 +107,7 @@ class MLayer(nn.Module):
              else Geo(self.head_dim, head_rank, physics_config=self.physics_config)
              for _ in range(heads)])
         self.register_buffer("headless_mode", torch.tensor(False))
-        self.use_dynamic_time = False
+        self.use_dynamic_time = self.physics_config.get("active_inference", {}).get("dynamic_time", {}).get("enabled", False)
         self.gatings = nn.ModuleList([RiemannianGating(self.head_dim, topology=self.topology_id)
                                       for _ in range(heads)])
         scale_vals = []
@@ -118,7 +124,13 @@ class MLayer(nn.Module):
         # the fused / layered recurrence kernels compute the Euclidean
         # leapfrog; every other configuration steps layer by layer through the
         # multi-scheme integrator kernel (generic path)
-        self.generic = self.topology_id == 1 or integrator_type != "leapfrog"
+        ai = self.physics_config.get("active_inference", {})
+        self.use_dynamic_time = ai.get("dynamic_time", {}).get("enabled", False)
+        self.generic = (self.topology_id == 1 or integrator_type != "leapfrog" or self.use_dynamic_time
+                        or ai.get("recursive_geodesics", {}).get("enabled", False)
+                        or (ai.get("enabled", False)
+                            and (ai.get("reactive_curvature", {}).get("enabled", False)
+                                 or ai.get("singularities", {}).get("enabled", False))))
         if heads > 1:
             self.out_proj_x = nn.Linear(3 * dim if self.topology_id == 1 else dim, dim)
             self.out_proj_v = nn.Linear(dim, dim)
@@ -128,7 +140,10 @@ class MLayer(nn.Module):
             nn.init.zeros_(self.out_proj_x.bias)
             nn.init.xavier_uniform_(self.out_proj_v.weight)
             nn.init.zeros_(self.out_proj_v.bias)
-        self.use_recursive = False
+        self.use_recursive = ai.get("recursive_geodesics", {}).get("enabled", False)
+        if self.use_recursive:
+            self.context_proj = nn.Linear(heads, dim)
+            nn.init.zeros_(self.context_proj.weight)
         self._pack = PackCache()
         # "auto" (by batch size), "fused" or "layered": which recurrence kernel
         # computes an inference step (the same choice as Manifold.recurrence)
@@ -143,7 +158,7 @@ class MLayer(nn.Module):
         if force is None:
             force = torch.zeros_like(x)
         if self.generic:
-            return self._generic_step(x, v, force)
+            return self._generic_step(x, v, force, context)
         if torch.is_grad_enabled() and any(t.requires_grad for t in
                                            [x, v, force, *self.parameters()]):
             from .training import leapfrog_sequence_train
@@ -158,7 +173,7 @@ class MLayer(nn.Module):
         return xn, vn, context_next, []
 
 
-    def _generic_step(self, x, v, force):
+    def _generic_step(self, x, v, force, context=None):
         """One layer step for the torus and the non-leapfrog integrators:
         every head's integrator in one launch of the multi-scheme kernel, then
         the head mixing of gfn/layers/base.py:304-335 (torus: the mixer reads
@@ -168,10 +183,30 @@ class MLayer(nn.Module):
             raise GfnError("training is implemented for the Euclidean leapfrog path only (call eval() "
                            "or run under torch.no_grad() for inference)")
         with torch.no_grad():
-            return self._generic_step_nograd(x, v, force)
+            return self._generic_step_nograd(x, v, force, context)
 
-    def _generic_step_nograd(self, x, v, force):
+    def _active_terms(self):
+        """Active-inference operands (gfn/geometry/reactive.py:53-81,
+        gfn/geometry/toroidal.py:126-141): plasticity, singularity mode,
+        potential weights / bias, threshold, strength."""
+        ai = self.physics_config.get("active_inference", {})
+        ch = self.christoffels
+        if not ai.get("enabled", False):
+            return 0.0, 0, None, None, 1.0, 1.0
+        plast = ch[0].plasticity if ai.get("reactive_curvature", {}).get("enabled", False) else 0.0
+        mode, V, Vb = 0, None, None
+        if ai.get("singularities", {}).get("enabled", False) and getattr(ch[0], "V", None) is not None:
+            mode = 2 if self.topology_id == 1 else 1
+            V = torch.stack([c.V.weight.reshape(-1) for c in ch]).contiguous()
+            if ch[0].V.bias is not None:
+                Vb = torch.stack([c.V.bias.reshape(()) for c in ch]).contiguous()
+        return (float(plast), mode, V, Vb, float(ch[0].singularity_threshold),
+                float(ch[0].black_hole_strength))
+
+    def _generic_step_nograd(self, x, v, force, context):
         B = x.shape[0]
+        if self.use_recursive and context is not None:
+            force = force + self.context_proj(context)
         H, hd = self.heads, self.head_dim
         leap = self.integrator_type == "leapfrog"
         ch = self.christoffels
@@ -186,9 +221,23 @@ class MLayer(nn.Module):
             U = W = None
             R, r = ch[0].R, ch[0].r
         scheme = self.integrator_type if self.integrator_type in ops.SCHEMES else "verlet"
-        dts = torch.nn.functional.softplus(self.dt_params)
+        dt_base = torch.nn.functional.softplus(self.dt_params)
+        if self.use_dynamic_time:
+            # dt scale per head and row: softplus(dt_params) * curvature gate
+            # (gfn/layers/base.py:219-229, gfn/layers/gating.py:38-51)
+            hv = x.view(B, H, hd)
+            gates = torch.stack([self.gatings[i](hv[:, i]) for i in range(H)], dim=0)  # [H, B, 1]
+            dts = (dt_base.view(H, 1, 1) * gates).squeeze(-1).t().contiguous()       # [B, H]
+            if H == 1:
+                dts = dts.reshape(B)
+            context_next = gates.squeeze(-1).t()
+        else:
+            dts = dt_base
+            context_next = torch.ones(B, H, device=x.device, dtype=x.dtype)
+        plast, mode, V, Vb, thr, strength = self._active_terms()
         xc, vc = ops.integrator_heads(scheme, x.contiguous(), v.contiguous(), force.contiguous(), U, W,
-                                      self.base_dt, dts, 1, self.topology_id, Wf, bf, Wi, H, R, r)
+                                      self.base_dt, dts, 1, self.topology_id, Wf, bf, Wi, H, R, r,
+                                      plast, V, Vb, mode, thr, strength)
         if H > 1:
             if self.topology_id == 1:
                 mix_in = torch.cat([torch.sin(xc), torch.cos(xc), torch.tanh(vc / 100.0)], dim=-1)
@@ -199,7 +248,7 @@ class MLayer(nn.Module):
         else:
             xn, vn = xc, vc
         vn = 100.0 * torch.tanh(vn / 100.0)
-        return xn, vn, torch.ones(B, H, device=x.device, dtype=x.dtype), []
+        return xn, vn, context_next, []
 
 
 class ParallelMLayer(nn.Module):

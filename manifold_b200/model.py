@@ -189,12 +189,13 @@ class Manifold(nn.Module):
         else:
             x, v = state
         xs, vs = [], []
+        context = None
         for t in range(L):
             f = forces[:, t].to(torch.float32)
             if attention_mask is not None:
                 f = f * attention_mask[:, t].unsqueeze(-1).float()
             for layer in self.layers:
-                x, v, _, _ = layer(x, v, f)
+                x, v, context, _ = layer(x, v, f, context)
             xs.append(x)
             vs.append(v)
         x_seq = torch.stack(xs, 1)

@@ -117,7 +117,7 @@ def torus_christoffel(v, x, R=2.0, r=1.0):
 
 
 def leapfrog_head_step_gated(x, v, F, U, W, Wf, bf, Wi, dt, dt_scale, steps=1, topology=0,
-                             R=2.0, r=1.0):
+                             R=2.0, r=1.0, act=None):
     """leapfrog_head_step with the full friction gate and both topologies:
     mu = 5 sigmoid((feat(x) Wf^T + bf) + F Wi^T) (gfn/geometry/lowrank.py:114-123;
     Wi None: no input gate), feat = [sin x, cos x] and Gamma the toroidal term
@@ -136,7 +136,8 @@ def leapfrog_head_step_gated(x, v, F, U, W, Wf, bf, Wi, dt, dt_scale, steps=1, t
         return sigmoid(((feat @ Wf.T) + bf) + zin) * dtp(5.0)
 
     def gam(vc, xc):
-        return torus_christoffel(vc, xc, R, r) if topology == 1 else christoffel(vc, U, W)
+        g = torus_christoffel(vc, xc, R, r) if topology == 1 else christoffel(vc, U, W)
+        return g * active_factor(xc, vc, act, topology) if act is not None else g
 
     for _ in range(steps):
         v_half = (v + h * (F - gam(v, x))) / (one + h * mu(x))
@@ -147,7 +148,33 @@ def leapfrog_head_step_gated(x, v, F, U, W, Wf, bf, Wi, dt, dt_scale, steps=1, t
     return x, v
 
 
-def combined_accel(x, v, F, U, W, Wf, bf, Wi, topology=0, R=2.0, r=1.0):
+def active_factor(x, v, act, topology):
+    """Active-inference multiplier of the Christoffel term (gfn/geometry/reactive.py:62-81,
+    gfn/geometry/toroidal.py:126-141): (1 + plasticity tanh(mean v^2)) times
+    (1 + s (strength - 1)), s = sigmoid(10 (p - thr)) (low-rank) or [p > thr]
+    (torus), p = sigmoid(feat(x) . V + b).  act None: 1."""
+    dtp = x.dtype.type
+    if act is None:
+        return dtp(1.0)
+    m = dtp(1.0)
+    if act.get("plasticity", 0.0):
+        energy = np.tanh(np.mean(v * v, axis=-1, keepdims=True))
+        m = m * (dtp(1.0) + dtp(act["plasticity"]) * energy)
+    if act.get("V") is not None:
+        feat = np.concatenate([np.sin(x), np.cos(x)], -1) if topology == 1 else x
+        z = feat @ act["V"][:, None]
+        if act.get("Vb") is not None:
+            z = z + act["Vb"]
+        pot = sigmoid(z.astype(x.dtype))
+        if topology == 1:
+            sg = (pot > dtp(act["thr"])).astype(x.dtype)
+        else:
+            sg = sigmoid((dtp(10.0) * (pot - dtp(act["thr"]))).astype(x.dtype))
+        m = m * (dtp(1.0) + sg * (dtp(act["strength"]) - dtp(1.0)))
+    return m
+
+
+def combined_accel(x, v, F, U, W, Wf, bf, Wi, topology=0, R=2.0, r=1.0, act=None):
     """a = F - C(v, x): the Christoffel term in the combined form the
     non-leapfrog integrators call (gfn/geometry/lowrank.py:100-131,
     gfn/geometry/toroidal.py:70-148): mu = 5 sigmoid(feat(x) Wf^T + bf + F Wi^T);
@@ -161,15 +188,16 @@ def combined_accel(x, v, F, U, W, Wf, bf, Wi, topology=0, R=2.0, r=1.0):
         mu = sigmoid(gate) * dtp(5.0)
     else:
         mu = dtp(0.0)
+    M = active_factor(x, v, act, topology)
     if topology == 1:
-        c = torus_christoffel(v, x, R, r) + mu * v
+        c = torus_christoffel(v, x, R, r) * M + mu * v
     else:
         one = dtp(1.0)
         proj = v @ U
         norm = np.sqrt(np.sum(proj * proj, axis=-1, keepdims=True))
         scale = one / ((one + norm) + dtp(1e-6))
         g = ((proj * proj) * scale) @ W.T
-        c = dtp(20.0) * np.tanh((g + mu * v) / dtp(20.0))
+        c = dtp(20.0) * np.tanh((g + mu * v) / dtp(20.0)) * M
     return F - c
 
 
@@ -187,7 +215,8 @@ _DP_A = [[1 / 5], [3 / 40, 9 / 40], [44 / 45, -56 / 15, 32 / 9],
 _DP_B = [35 / 384, 0, 500 / 1113, 125 / 192, -2187 / 6784, 11 / 84]
 
 
-def integrator_step(scheme, x, v, F, U, W, Wf, bf, Wi, dt, dt_scale, steps=1, topology=0, R=2.0, r=1.0):
+def integrator_step(scheme, x, v, F, U, W, Wf, bf, Wi, dt, dt_scale, steps=1, topology=0, R=2.0, r=1.0,
+                    act=None):
     """The reference's other integrators (gfn/integrators/runge_kutta/{euler,heun,
     rk4,dormand_prince}.py, gfn/integrators/symplectic/{verlet,yoshida,forest_ruth,
     omelyan}.py), with the combined-form acceleration.  Forest-Ruth and Yoshida
@@ -197,7 +226,7 @@ def integrator_step(scheme, x, v, F, U, W, Wf, bf, Wi, dt, dt_scale, steps=1, to
     wrap = torus_wrap if topology == 1 else (lambda z: z)
 
     def acc(xx, vv):
-        return combined_accel(xx, vv, F, U, W, Wf, bf, Wi, topology, R, r)
+        return combined_accel(xx, vv, F, U, W, Wf, bf, Wi, topology, R, r, act)
 
     for _ in range(steps):
         if scheme == "euler":
@@ -248,7 +277,15 @@ def integrator_step(scheme, x, v, F, U, W, Wf, bf, Wi, dt, dt_scale, steps=1, to
     return x, v
 
 
-def mlayer_step_generic(x, v, F, lp, heads, base_dt, scheme="leapfrog", topology=0):
+def _gate_mlp(xh, lp, h, topology):
+    """RiemannianGating.curvature_net (gfn/layers/gating.py:16-23,38-51)."""
+    feat = np.concatenate([np.sin(xh), np.cos(xh)], -1) if topology == 1 else xh
+    z = np.tanh((feat @ lp["gW1"][h].T) + lp["gb1"][h])
+    return sigmoid(((z @ lp["gW2"][h].T) + lp["gb2"][h]).astype(xh.dtype))
+
+
+def mlayer_step_generic(x, v, F, lp, heads, base_dt, scheme="leapfrog", topology=0, active=None,
+                        context=None):
     """MLayer.forward for the torus and the non-leapfrog integrators
     (gfn/layers/base.py:198-338): per head, the integrator with the stacked
     gates (the leapfrog reads the forget gate only, the others add the input
@@ -256,18 +293,38 @@ def mlayer_step_generic(x, v, F, lp, heads, base_dt, scheme="leapfrog", topology
     B, d = x.shape
     hd = d // heads
     dtp = x.dtype.type
+    active = active or {}
+    if active.get("recursive_geodesics", {}).get("enabled", False) and context is not None:
+        F = F + ((context @ lp["cW"].T) + lp["cb"])          # gfn/layers/base.py:212-214
     sc = softplus(lp["dt_params"].astype(x.dtype))
+    dyn = active.get("dynamic_time", {}).get("enabled", False)
+    gates = np.ones((heads, B, 1), x.dtype)
+    if dyn:
+        gates = np.stack([_gate_mlp(x[:, h * hd:(h + 1) * hd], lp, h, topology) for h in range(heads)])
     xo, vo = np.empty_like(x), np.empty_like(v)
+    on = active.get("enabled", False)
     for h in range(heads):
         sl = slice(h * hd, (h + 1) * hd)
         U = lp["U"][h] if "U" in lp else None
         W = lp["W"][h] if "W" in lp else None
+        scale = (sc[h] * gates[h]) if dyn else sc[h]
+        act = None
+        if on:
+            rc = active.get("reactive_curvature", {})
+            sgc = active.get("singularities", {})
+            plast = rc.get("plasticity", 0.1 if topology == 1 else 0.0) if rc.get("enabled", False) else 0.0
+            act = dict(plasticity=plast)
+            if sgc.get("enabled", False):
+                act.update(V=lp["V"][h], Vb=lp["Vb"][h] if topology == 1 else None,
+                           thr=sgc.get("threshold", 0.8), strength=sgc.get("strength", 10.0))
         if scheme == "leapfrog":
             xo[:, sl], vo[:, sl] = leapfrog_head_step_gated(x[:, sl], v[:, sl], F[:, sl], U, W, lp["Wf"][h],
-                                                            lp["bf"][h], None, base_dt, sc[h], 1, topology)
+                                                            lp["bf"][h], None, base_dt, scale, 1, topology,
+                                                            act=act)
         else:
             xo[:, sl], vo[:, sl] = integrator_step(scheme, x[:, sl], v[:, sl], F[:, sl], U, W, lp["Wf"][h],
-                                                   lp["bf"][h], lp["Wi"][h], base_dt, sc[h], 1, topology)
+                                                   lp["bf"][h], lp["Wi"][h], base_dt, scale, 1, topology,
+                                                   act=act)
     if heads > 1:
         if topology == 1:
             mix_in = np.concatenate([np.sin(xo), np.cos(xo), np.tanh(vo / dtp(100.0))], -1)
@@ -277,17 +334,21 @@ def mlayer_step_generic(x, v, F, lp, heads, base_dt, scheme="leapfrog", topology
         vn = rmsnorm((vo @ lp["Wv"].T) + lp["bv"], lp["gv"])
     else:
         xn, vn = xo, vo
-    return xn, dtp(100.0) * np.tanh(vn / dtp(100.0))
+    return xn, dtp(100.0) * np.tanh(vn / dtp(100.0)), gates[..., 0].T
 
 
-def manifold_forward_generic(x0, v0, forces, layers, heads, base_dt, scheme="leapfrog", topology=0):
-    """manifold_forward with mlayer_step_generic (gfn/model.py:377-402)."""
+def manifold_forward_generic(x0, v0, forces, layers, heads, base_dt, scheme="leapfrog", topology=0,
+                             active=None):
+    """manifold_forward with mlayer_step_generic (gfn/model.py:377-402); the
+    per-head gates flow to the next layer as its context (gfn/model.py:385)."""
     B, L, d = forces.shape
     x, v = x0.copy(), v0.copy()
     xs, vs = np.empty((B, L, d), x0.dtype), np.empty((B, L, d), x0.dtype)
+    ctx = None
     for t in range(L):
         for lp in layers:
-            x, v = mlayer_step_generic(x, v, forces[:, t], lp, heads, base_dt, scheme, topology)
+            x, v, ctx = mlayer_step_generic(x, v, forces[:, t], lp, heads, base_dt, scheme, topology,
+                                            active, ctx)
         xs[:, t], vs[:, t] = x, v
     return xs, vs, x, v
 

@@ -36,9 +36,21 @@ CASES = {
     "torus_heun_s": dict(V=6, d=64, NL=2, H=4, rank=16, B=2, L=3, dt=0.1, seed=44, torus=True,
                          integrator="heun"),
     "torus_h1": dict(V=5, d=16, NL=2, H=1, rank=4, B=2, L=4, dt=0.1, seed=51, torus=True),
+    # active inference (reactive curvature, singularities, dynamic time, recursive geodesics)
+    "ai_heun_s": dict(V=6, d=32, NL=2, H=2, rank=8, B=3, L=4, dt=0.1, seed=52, integrator="heun",
+                      active={"enabled": True, "reactive_curvature": {"enabled": True, "plasticity": 0.5},
+                              "singularities": {"enabled": True, "threshold": 0.5, "strength": 3.0}}),
+    "ai_torus_s": dict(V=6, d=32, NL=2, H=2, rank=8, B=3, L=4, dt=0.1, seed=53, torus=True,
+                       active={"enabled": True, "reactive_curvature": {"enabled": True, "plasticity": 0.2},
+                               "singularities": {"enabled": True, "threshold": 0.55, "strength": 2.0}}),
+    "dyn_s": dict(V=6, d=64, NL=2, H=4, rank=16, B=3, L=4, dt=0.1, seed=54,
+                  active={"dynamic_time": {"enabled": True}, "recursive_geodesics": {"enabled": True}}),
+    "dyn_rk4_torus_s": dict(V=6, d=32, NL=2, H=2, rank=8, B=2, L=3, dt=0.1, seed=55, torus=True,
+                            integrator="rk4", active={"dynamic_time": {"enabled": True}}),
 }
 VARIANT_CASES = ["heun_s", "rk4_s", "euler_s", "verlet_s", "yoshida_s", "forest_ruth_s", "omelyan_s",
-                 "rk45_s", "torus_s", "torus_heun_s", "torus_h1"]
+                 "rk45_s", "torus_s", "torus_heun_s", "torus_h1", "ai_heun_s", "ai_torus_s", "dyn_s",
+                 "dyn_rk4_torus_s"]
 
 # Gradient (BPTT) cases: upstream gradients on x_seq, v_seq and the final
 # state, gradients taken by the reference's autograd.  "gc5" has the C5 layer
@@ -125,6 +137,22 @@ def make_params(cfg):
         P["func"] = make_functional_params(rng, d)
     else:
         P["emb"] = rng.standard_normal((cfg["V"], d)).astype(f)
+    if cfg.get("active"):
+        # active-inference parameters from a separate stream (the draws above
+        # stay those of the plain cases)
+        ra = np.random.default_rng(cfg["seed"] + 500)
+        hd = d // H
+        fin = 2 * hd if cfg.get("torus") else hd
+        for lp in P["layers"]:
+            lp["V"] = (ra.standard_normal((H, fin)) * 0.5).astype(f)
+            lp["Vb"] = (ra.standard_normal(H) * 0.3).astype(f)
+            q = hd // 4
+            lp["gW1"] = (ra.standard_normal((H, q, fin)) * 0.3).astype(f)
+            lp["gb1"] = (ra.standard_normal((H, q)) * 0.1).astype(f)
+            lp["gW2"] = (ra.standard_normal((H, 1, q)) * 0.5).astype(f)
+            lp["gb2"] = (ra.standard_normal((H, 1)) * 0.5 + 1.0).astype(f)
+            lp["cW"] = (ra.standard_normal((d, H)) * 0.2).astype(f)
+            lp["cb"] = (ra.standard_normal(d) * 0.05).astype(f)
     return P
 
 
@@ -205,6 +233,20 @@ def load_into_layer(layer, cfg, lp):
             ch.forget_gate.weight.copy_(T(lp["Wf"][h]))
             ch.forget_gate.bias.copy_(T(lp["bf"][h]))
             ch.input_gate.weight.copy_(T(lp["Wi"][h]))
+        if "V" in lp:
+            for h, ch in enumerate(layer.christoffels):
+                if getattr(ch, "V", None) is not None:
+                    ch.V.weight.copy_(T(lp["V"][h])[None])
+                    if ch.V.bias is not None:
+                        ch.V.bias.copy_(T(lp["Vb"][h])[None])
+            for h, g in enumerate(layer.gatings):
+                g.curvature_net[0].weight.copy_(T(lp["gW1"][h]))
+                g.curvature_net[0].bias.copy_(T(lp["gb1"][h]))
+                g.curvature_net[2].weight.copy_(T(lp["gW2"][h]))
+                g.curvature_net[2].bias.copy_(T(lp["gb2"][h]))
+            if getattr(layer, "context_proj", None) is not None:
+                layer.context_proj.weight.copy_(T(lp["cW"]))
+                layer.context_proj.bias.copy_(T(lp["cb"]))
         if cfg["H"] > 1:
             layer.out_proj_x.weight.copy_(T(lp["Wx"]))
             layer.out_proj_x.bias.copy_(T(lp["bx"]))
@@ -220,6 +262,8 @@ def model_kwargs(cfg):
         pc = {"embedding": {"type": "functional", "mode": "binary", "coord_dim": 16}}
     if cfg.get("torus"):
         pc = dict(pc, topology={"type": "torus"})
+    if cfg.get("active"):
+        pc = dict(pc, active_inference=cfg["active"])
     return dict(vocab_size=cfg["V"], dim=cfg["d"], depth=cfg["NL"], rank=cfg["rank"],
                 heads=cfg["H"], integrator_type=cfg.get("integrator", "leapfrog"), base_dt=cfg["dt"],
                 physics_config=pc)

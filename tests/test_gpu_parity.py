@@ -176,8 +176,8 @@ def test_units_match_reference():
     xn, vn = ops.leapfrog_fused(cu(g["lf_x"]), cu(g["ch_v"]), cu(g["lf_F"]), cu(g["ch_U"]),
                                 cu(g["ch_W"]), 0.1, torch.tensor([0.87]).cuda(), 3,
                                 Wf=cu(g["lf_Wf"]), bf=cu(g["lf_bf"]))
-    rowwise_close(xn.cpu().numpy(), g["lf_xn"], what="x")
-    rowwise_close(vn.cpu().numpy(), g["lf_vn"], what="v")
+    rowwise_close(xn.detach().cpu().numpy(), g["lf_xn"], what="x")
+    rowwise_close(vn.detach().cpu().numpy(), g["lf_vn"], what="v")
     for L in (20, 100):
         y = ops.parallel_scan_fused(cu(g[f"scan{L}_a"]), cu(g[f"scan{L}_x"]))
         rowwise_close(y.cpu().numpy(), g[f"scan{L}_y"], 1e-5, 1e-6, f"scan{L}")
@@ -194,8 +194,8 @@ def test_integrator_module_matches_reference():
     xn, vn = integ(cu(g["lf_x"]), cu(g["ch_v"]), force=cu(g["lf_F"]),
                    dt_scale=torch.tensor([[0.87]]).cuda(), steps=3,
                    W_forget_stack=cu(g["lf_Wf"])[None], b_forget_stack=cu(g["lf_bf"])[None])
-    rowwise_close(xn.cpu().numpy(), g["lf_xn"], what="x")
-    rowwise_close(vn.cpu().numpy(), g["lf_vn"], what="v")
+    rowwise_close(xn.detach().cpu().numpy(), g["lf_xn"], what="x")
+    rowwise_close(vn.detach().cpu().numpy(), g["lf_vn"], what="v")
 
 
 def test_parallel_layer_matches_reference():

@@ -126,6 +126,7 @@ def test_oracle_generic_variants_match_reference(name):
     x0 = np.broadcast_to(P["x0"], (B, cfg["d"])).copy()
     v0 = np.broadcast_to(P["v0"], (B, cfg["d"])).copy()
     xs, vs, x, v = O.manifold_forward_generic(x0, v0, F, P["layers"], cfg["H"], cfg["dt"],
-                                              cfg.get("integrator", "leapfrog"), 1 if cfg.get("torus") else 0)
+                                              cfg.get("integrator", "leapfrog"), 1 if cfg.get("torus") else 0,
+                                              cfg.get("active"))
     close(xs, g["x_seq"], 1e-4, 1e-5)
     close(vs, g["v_seq"], 1e-4, 1e-5)
