@@ -158,10 +158,11 @@ __global__ void __launch_bounds__(HeadUmmaCfg<HD, P>::THREADS, HeadUmmaCfg<HD, P
   const float* lay = a.lay;
   GFN_HEAD_STAMP(0);
 
+  const bool zin = a.z != nullptr;
   if (threadIdx.x == 0) {
     for (int i = 0; i < 3; ++i) mbar_init(&bars[i], 1);
     fence_mbar_init();
-    const bool zin = a.z != nullptr;
+    // the head's weights (constant: issued before waiting on the previous kernel)
     constexpr int UWB = (2 * HD * RK + HD) * 4;  // U | W^T | b_f bytes
     mbar_arrive_expect_tx(&bars[0], 2 * C::W_BYTES + UWB + (zin ? 4 * HD * 4 : 0));
     bulk_g2s(sW, lay + o.HU + (long long)h * (HD * HD), 2 * C::W_BYTES, &bars[0]);
@@ -170,27 +171,6 @@ __global__ void __launch_bounds__(HeadUmmaCfg<HD, P>::THREADS, HeadUmmaCfg<HD, P
       const int offs[4] = {o.bx, o.bv, o.gx, o.gv};
 #pragma unroll
       for (int i = 0; i < 4; ++i) bulk_g2s(sBG + i * HD, a.prev + offs[i] + h * HD, HD * 4, &bars[0]);
-      mbar_arrive_expect_tx(&bars[1], 4 * C::ZBOX);
-#pragma unroll
-      for (int i = 0; i < 4; ++i)  // (x, v) x (column half)
-        umma::tma_load_2d(sZ + i * C::ZBOX, &tmz, &bars[1], h * HD + (i & 1) * 32, (i >> 1) * B + b0);
-    }
-  }
-  // RMSNorm factors of this row from the mixing GEMM's partial sums (issued
-  // first: their latency overlaps the copies below)
-  float rx = 0.f, rv = 0.f;
-  if (a.z && live) {
-    if (a.spart) {
-      float sx = 0.f, sv = 0.f;
-      for (int p = 0; p < a.nparts; ++p) {
-        sx += a.spart[(long long)p * B + b];
-        sv += a.spart[((long long)a.nparts + p) * B + b];
-      }
-      rx = 1.f / sqrtf(sx * (1.f / (float)d) + 1.1920928955078125e-07f);
-      rv = 1.f / sqrtf(sv * (1.f / (float)d) + 1.1920928955078125e-07f);
-    } else {
-      rx = a.stat[b];
-      rv = a.stat[B + b];
     }
   }
   // the token's force for this thread's columns, fetched now (it is used in
@@ -254,6 +234,35 @@ __global__ void __launch_bounds__(HeadUmmaCfg<HD, P>::THREADS, HeadUmmaCfg<HD, P
     }
   }
   if (warp == 0) umma::tmem_alloc(tslot, 2 * HD);
+  __syncthreads();  // barriers initialised before any thread waits on them
+  // the previous kernel (the mixing GEMM or the finalize) wrote z / the state
+  // and still reads this kernel's output buffer until it completes
+  umma::gdc_launch_dependents();
+  umma::gdc_wait();
+  if (threadIdx.x == 0 && zin) {
+    mbar_arrive_expect_tx(&bars[1], 4 * C::ZBOX);
+#pragma unroll
+    for (int i = 0; i < 4; ++i)  // (x, v) x (column half)
+      umma::tma_load_2d(sZ + i * C::ZBOX, &tmz, &bars[1], h * HD + (i & 1) * 32, (i >> 1) * B + b0);
+  }
+  // RMSNorm factors of this row from the mixing GEMM's partial sums (issued
+  // first: their latency overlaps the copies below)
+  float rx = 0.f, rv = 0.f;
+  if (a.z && live) {
+    if (a.spart) {
+      float sx = 0.f, sv = 0.f;
+      for (int p = 0; p < a.nparts; ++p) {
+        sx += a.spart[(long long)p * B + b];
+        sv += a.spart[((long long)a.nparts + p) * B + b];
+      }
+      rx = 1.f / sqrtf(sx * (1.f / (float)d) + 1.1920928955078125e-07f);
+      rv = 1.f / sqrtf(sv * (1.f / (float)d) + 1.1920928955078125e-07f);
+    } else {
+      rx = a.stat[b];
+      rv = a.stat[B + b];
+    }
+  }
+
   const float eff = a.base_dt * lay[o.sc + h];
   const float hh = 0.5f * eff;
   const float inv_s = lay[o.HUs + 2 * h + 1];
@@ -422,11 +431,11 @@ __global__ void __launch_bounds__(HeadUmmaCfg<HD, P>::THREADS, HeadUmmaCfg<HD, P
         const int j = j4 + i;
         const float gam = soft_clamp20(gm[i]);
         // (v + h (F - Gamma)) / (1 + h * 5 sigmoid(gate)) with one division:
-        // 1 + 5h sigmoid = (1 + e + 5h) / (1 + e), e = exp(-gate); an
-        // overflowing e means sigmoid = 0 (no friction)
+        // 1 + 5h sigmoid = (1 + e + 5h) / (1 + e), e = exp(-gate); e beyond
+        // 1e30 means sigmoid = 0 in float32 (no friction; also keeps num * ope finite)
         const float ope = 1.f + expf(-(g[j] * inv_s + bj[i]));
         const float num = V[j] + hh * (F[j] - gam);
-        V[j] = isinf(ope) ? num : (num * ope) / (ope + 5.f * hh);
+        V[j] = ope > 1e30f ? num : (num * ope) / (ope + 5.f * hh);
       }
     }
     if (kick == 0) {

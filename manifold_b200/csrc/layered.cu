@@ -5,6 +5,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <mutex>
+#include <utility>
 
 #include <cublas_v2.h>
 #include <cudaTypedefs.h>
@@ -153,10 +154,39 @@ int make_mix_plan(MixUmmaPlan* p, const __half* catkh, const float* packed, cons
   return encode_f16_map(&p->tb, packed + lo.WH, 3, bdims, bstr, bbox);
 }
 
+// Programmatic dependent launch of the layered path's tensor-core kernels:
+// each may start its prologue (barriers, TMEM, weight copies, the token's
+// force) while the previous kernel of the stream finishes; the kernels wait
+// for it (griddepcontrol.wait) before touching its outputs.  GFN_LAY_PDL=0
+// launches them plainly.
+bool use_pdl() {
+  static const bool on = [] {
+    const char* env = getenv("GFN_LAY_PDL");
+    return !(env && atoi(env) == 0);
+  }();
+  return on;
+}
+
+template <typename... KArgs, typename... Args>
+void launch_maybe_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                      Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = use_pdl() ? 1 : 0;
+  cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
 void launch_mix(const MixUmmaPlan& p, const MixUmmaArgs& ma, cudaStream_t s) {
 #define GFN_MIX_LAUNCH(BN, BK, MH)                                                       \
   if (p.bn == BN && p.bk == BK && p.mh == MH) {                                          \
-    mix_umma_kernel<BN, BK, MH><<<p.grid, p.threads, p.smem, s>>>(p.ta, p.tb, ma);      \
+    launch_maybe_pdl(mix_umma_kernel<BN, BK, MH>, dim3(p.grid), dim3(p.threads), p.smem, s, p.ta, p.tb, ma); \
     return;                                                                              \
   }
   GFN_MIX_SHAPES(GFN_MIX_LAUNCH)
@@ -183,11 +213,12 @@ void launch_head_umma_p(int rank, const CUtensorMap& tmz, const CUtensorMap& tmo
                         dim3 grid, cudaStream_t s) {
   constexpr int T = HeadUmmaCfg<64, P>::THREADS;
   if (rank == 4)
-    layered_head_umma_kernel<4, 64, P><<<grid, T, head_umma_smem<4, 64, P>(), s>>>(tmz, tmo, a);
+    launch_maybe_pdl(layered_head_umma_kernel<4, 64, P>, grid, dim3(T), head_umma_smem<4, 64, P>(), s, tmz, tmo, a);
   else if (rank == 8)
-    layered_head_umma_kernel<8, 64, P><<<grid, T, head_umma_smem<8, 64, P>(), s>>>(tmz, tmo, a);
+    launch_maybe_pdl(layered_head_umma_kernel<8, 64, P>, grid, dim3(T), head_umma_smem<8, 64, P>(), s, tmz, tmo, a);
   else
-    layered_head_umma_kernel<16, 64, P><<<grid, T, head_umma_smem<16, 64, P>(), s>>>(tmz, tmo, a);
+    launch_maybe_pdl(layered_head_umma_kernel<16, 64, P>, grid, dim3(T), head_umma_smem<16, 64, P>(), s, tmz, tmo,
+                     a);
 }
 
 void launch_head_umma(int rank, const CUtensorMap& tmz, const CUtensorMap& tmo, const LayPreArgs& a,

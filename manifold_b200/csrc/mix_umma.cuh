@@ -103,6 +103,10 @@ __global__ void __launch_bounds__(MixCfg<BN, BK, MH>::THREADS, 1)
   __syncthreads();
   umma::tc_fence_after();
   const uint32_t tbase = *tslot;
+  // the previous kernel (the head step) wrote the A operand and still reads
+  // this GEMM's output buffers until it completes
+  umma::gdc_launch_dependents();
+  umma::gdc_wait();
 
   const int ntiles_total = 2 * a.mtiles * a.ntiles;
   const int kblocks = a.d / C::BK;

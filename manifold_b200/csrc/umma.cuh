@@ -100,6 +100,13 @@ GFN_DEV void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
 }
 
 GFN_DEV void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+// Programmatic dependent launch: launch_dependents lets the next kernel of the
+// stream start its prologue on SMs this grid frees; wait blocks until the
+// previous kernel of the stream has completed and its writes are visible.
+// Both are no-ops for a kernel launched without the attribute.
+GFN_DEV void gdc_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+GFN_DEV void gdc_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 GFN_DEV void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
 // ------------------------------------------------------------------ MMA
