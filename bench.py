@@ -436,8 +436,8 @@ def run_ours(args, c):
 def run_scan(args, c):
     """C3 through the parallel-scan path (use_scan=True): one step = the 12
     ParallelMLayers over one [B, L] batch of functional-embedding forces
-    (LayerNorm + the three d x d projections as one GEMM + the fused
-    sigmoid/softplus/two-scan kernel per layer)."""
+    (LayerNorm + the three d x d projections as one split-fp16 tcgen05 GEMM +
+    the fused sigmoid/softplus/two-scan kernel per layer)."""
     import torch
     import torch.distributed as dist
     import manifold_b200 as gfn
@@ -515,8 +515,10 @@ def run_scan(args, c):
             ks.append((k0, k1))
         g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         g0.record(stream)
+        from manifold_b200.readout import SplitLinear
+        fl = f.reshape(-1, d)
         for i in range(steps):
-            torch.nn.functional.linear(layer.norm_x(f), Wcat, bcat)
+            SplitLinear.apply(layer.norm_x(fl), Wcat, bcat)
         g1.record(stream)
     torch.cuda.synchronize(dev)
     scan_us = sum(a.elapsed_time(b) for a, b in ks) * 1e3 / len(ks)
@@ -550,7 +552,9 @@ def run_scan(args, c):
                          "launch_us": round(scan_us, 2),
                          "algorithmic_bytes_per_launch": scan_bytes,
                          "projections": {"launch_us": round(proj_us, 2), "tflops": round(proj_tf, 1),
-                                         "note": "LayerNorm + [B*L, d] x [d, 3d] fp32 GEMM (torch)"}},
+                                         "note": "LayerNorm + [B*L, d] x [d, 3d] product as the split-fp16 "
+                                                 "tcgen05 GEMM (tflops: the fp32 product's FLOPs; the tensor "
+                                                 "pipe runs 3x, plus the operand split)"}},
             "clocks": clocks,
         }
     if world > 1:

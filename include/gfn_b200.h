@@ -391,6 +391,18 @@ int gfn_debug_layered_timing_read(double* head_ms, double* mix_ms, int* layer_st
 int gfn_debug_latency_probe(int rank, int clusters, int steps, long long* cycles,
                             gfn_stream_t stream);
 
+/* The same split-fp16 product, C = A' B'^T (+ bias) for operands split with
+ * K along their columns (k_along_rows = 0: a2 [M][3K] role A, b2 [N][3K] role
+ * B), on the library's own tcgen05 GEMM kernel (the layered path's mixing
+ * kernel, one product per launch) instead of the library GEMM.  Serves the
+ * readout's logits (gfn/model.py:393-397) and the scan path's projections
+ * (gfn/layers/parallel.py:91-108).  K <= 512 and a multiple of 32, N a
+ * multiple of 64, 16-byte aligned operands; bias [N] or NULL; alpha_slot: one
+ * float of device scratch for 1/(s_a s_b).  C [M][N] fp32 is overwritten. */
+int gfn_gemm_split_f16_tc(int M, int N, int K, const void* a2, const void* b2, const float* scale_a,
+                          const float* scale_b, const float* bias, float* c, float* alpha_slot,
+                          gfn_stream_t stream);
+
 /* ------------------------------------------------------------------------
  * Readout GEMMs at fp32-level accuracy on the tensor cores (the readout
  * nn.Linear(d -> vocab) of gfn/model.py:393-397 and its backward, which the

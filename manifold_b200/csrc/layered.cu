@@ -93,12 +93,13 @@ int encode_f16_map(CUtensorMap* m, const void* base, int rank, const cuuint64_t*
 // tile that gives every SM work (K blocks of 64).
 struct MixShape { int bn, bk, mh; };
 
-MixShape pick_mix_shape(int batch, int dim, int sms) {
+MixShape pick_mix_shape(int batch, int dim, int sms, int nmat = 2, int K = 0) {
   MixShape m{64, 64, 1};
   const long long mt1 = (batch + 127) / 128, mt2 = (batch + 255) / 256;
-  if (dim % 256 == 0 && 2 * mt2 * (dim / 256) >= (sms * 3) / 4) m = {256, 32, 2};
-  else if (dim % 256 == 0 && 2 * mt1 * (dim / 256) >= sms) m = {256, 64, 1};
-  else if (dim % 128 == 0 && 2 * mt1 * (dim / 128) >= sms) m = {128, 64, 1};
+  if (dim % 256 == 0 && nmat * mt2 * (dim / 256) >= (sms * 3) / 4) m = {256, 32, 2};
+  else if (dim % 256 == 0 && nmat * mt1 * (dim / 256) >= sms) m = {256, 64, 1};
+  else if (dim % 128 == 0 && nmat * mt1 * (dim / 128) >= sms) m = {128, 64, 1};
+  if (K && K % m.bk) m.bk = 32;  // K blocks must divide the reduction
   if (const char* env = getenv("GFN_MIX_TILE")) {  // tuning override "BN,BK,MH"
     int bn, bk, mh;
     if (sscanf(env, "%d,%d,%d", &bn, &bk, &mh) == 3 && (bn == 64 || bn == 128 || bn == 256) &&
@@ -115,11 +116,11 @@ struct MixUmmaPlan {
 };
 
 template <int BN, int BK, int MH>
-int mix_plan_for(MixUmmaPlan* p, int sms, int batch, int d) {
+int mix_plan_for(MixUmmaPlan* p, int sms, int batch, int d, int nmat = 2) {
   using C = MixCfg<BN, BK, MH>;
   p->smem = C::SMEM;
   p->threads = C::THREADS;
-  const int tiles = 2 * ((batch + C::BM - 1) / C::BM) * (d / BN);
+  const int tiles = nmat * ((batch + C::BM - 1) / C::BM) * (d / BN);
   p->grid = tiles < sms ? tiles : sms;
   cudaError_t e = cudaFuncSetAttribute(mix_umma_kernel<BN, BK, MH>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p->smem);
@@ -332,6 +333,16 @@ bool lay_pre_for(int r, int hd, int tr, int hblock, LayPreInst* out) {
 
 }  // namespace
 
+namespace {
+__global__ void split_alpha_tc_kernel(const float* sa, const float* sb, float* alpha) {
+  // the split scales are powers of two: 1 / (s_a s_b) = 2^-(e_a + e_b) exactly
+  int ea, eb;
+  frexpf(sa[1], &ea);
+  frexpf(sb[1], &eb);
+  alpha[0] = ldexpf(1.f, 2 - ea - eb);
+}
+}  // namespace
+
 extern "C" {
 
 int gfn_debug_head_profile(long long* device_stamps) {
@@ -404,6 +415,48 @@ int gfn_leapfrog_layered_pack(const float* U_stack, const float* W_stack,
                                                                 L.hd, a.LF, lo.HUs);
   layered_pack_kernel<<<148 * 8, 256, 0, s>>>(a);
   return launch_status("layered_pack_kernel");
+}
+
+int gfn_gemm_split_f16_tc(int M, int N, int K, const void* a2, const void* b2, const float* scale_a,
+                          const float* scale_b, const float* bias, float* c, float* alpha_slot,
+                          gfn_stream_t stream) {
+  if (M <= 0 || N <= 0 || K <= 0 || !a2 || !b2 || !scale_a || !scale_b || !c || !alpha_slot)
+    return fail(GFN_ERR_INVALID, "gemm_split_f16_tc: bad arguments");
+  if (K > 512 || K % 32 || N % 64)
+    return fail(GFN_ERR_UNSUPPORTED, "gemm_split_f16_tc: needs K <= 512, K %% 32 == 0, N %% 64 == 0 "
+                "(K=%d, N=%d)", K, N);
+  if ((reinterpret_cast<uintptr_t>(a2) | reinterpret_cast<uintptr_t>(b2)) & 15u || (bias && !aligned16(bias)) ||
+      !aligned16(c))
+    return fail(GFN_ERR_ALIGN, "gemm_split_f16_tc: operands must be 16-byte aligned");
+  int sms = 148, dev = 0;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const MixShape sh = pick_mix_shape(M, N, sms, 1, K);
+  MixUmmaPlan p;
+  p.bn = sh.bn; p.bk = sh.bk; p.mh = sh.mh;
+  int st = GFN_ERR_UNSUPPORTED;
+#define GFN_GEMM_PLAN(BN, BK, MH) \
+  if (sh.bn == BN && sh.bk == BK && sh.mh == MH) st = mix_plan_for<BN, BK, MH>(&p, sms, M, N, 1);
+  GFN_MIX_SHAPES(GFN_GEMM_PLAN)
+#undef GFN_GEMM_PLAN
+  if (st) return st == GFN_ERR_UNSUPPORTED ? fail(st, "gemm_split_f16_tc: no kernel for the tile") : st;
+  const cuuint64_t adims[2] = {(cuuint64_t)3 * K, (cuuint64_t)M};
+  const cuuint64_t astr[1] = {(cuuint64_t)6 * K};
+  const cuuint32_t abox[2] = {(cuuint32_t)sh.bk, (cuuint32_t)(128 * sh.mh)};
+  st = encode_f16_map(&p.ta, a2, 2, adims, astr, abox);
+  if (st) return st;
+  const cuuint64_t bdims[3] = {(cuuint64_t)3 * K, (cuuint64_t)N, 1};
+  const cuuint64_t bstr[2] = {(cuuint64_t)6 * K, (cuuint64_t)6 * K * N};
+  const cuuint32_t bbox[3] = {(cuuint32_t)sh.bk, (cuuint32_t)sh.bn, 1};
+  st = encode_f16_map(&p.tb, b2, 3, bdims, bstr, bbox);
+  if (st) return st;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  split_alpha_tc_kernel<<<1, 1, 0, s>>>(scale_a, scale_b, alpha_slot);
+  MixUmmaArgs ma = {};
+  ma.z = c; ma.spart = nullptr; ma.bias = bias; ma.alpha = alpha_slot; ma.B = M; ma.d = K; ma.layer = 0;
+  ma.mtiles = (M + 128 * sh.mh - 1) / (128 * sh.mh); ma.ntiles = N / sh.bn; ma.K = K; ma.N = N; ma.nmat = 1;
+  ma.out_bias = bias != nullptr;
+  launch_mix(p, ma, s);
+  return launch_status("gemm_split_f16_tc");
 }
 
 int gfn_leapfrog_layered_set_mixing(int mode) {
@@ -553,6 +606,7 @@ int gfn_leapfrog_layered_forward(const float* x_init, const float* v_init,
       if (mode == GFN_MIX_UMMA_F16) {
         MixUmmaArgs ma;
         ma.z = z; ma.alpha = lay + lo.wsc + 2; ma.spart = spart; ma.bias = lay + lo.bx; ma.B = batch; ma.d = dim; ma.layer = l;
+        ma.K = dim; ma.N = dim; ma.nmat = 2; ma.out_bias = 0;
         ma.mtiles = (batch + 128 * mix.mh - 1) / (128 * mix.mh); ma.ntiles = dim / mix.bn;
         launch_mix(mix, ma, s);
         time_mark(s);

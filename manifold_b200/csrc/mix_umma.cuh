@@ -35,12 +35,15 @@
 namespace gfn {
 
 struct MixUmmaArgs {
-  float* z;            // [2][B][d] fp32
-  float* spart;        // [2][ntiles][B] partial sums of (z + bias)^2 over each column tile
-  const float* bias;   // this layer's bx, bv ([2][d], contiguous in the pack)
-  const float* alpha;  // device scalar 1/s of this layer
-  int B, d, layer;
-  int mtiles, ntiles;  // BM-row blocks of B, BN-column blocks of d
+  float* z;            // [nmat][B][N] fp32
+  float* spart;        // [nmat][ntiles][B] partial sums of (z + bias)^2 over each column tile, or null
+  const float* bias;   // [nmat][N] (the layer's bx, bv, contiguous in the pack), or null
+  const float* alpha;  // device scalar: 1 / (product of the operands' split scales)
+  int B, d, layer;     // rows; d = K = N for the mixing GEMM (see K, N)
+  int mtiles, ntiles;  // BM-row blocks of B, BN-column blocks of N
+  int K, N;            // reduction and output widths (the mixing GEMM: both d)
+  int nmat;            // products in one launch (the mixing GEMM: x and v, 2)
+  int out_bias;        // 1: z = alpha (A B^T) + bias; 0: z = alpha (A B^T)
 };
 
 // Tile shape: BM = 128 * MH rows (MH halves of 128, one M=128 MMA each, the
@@ -108,8 +111,8 @@ __global__ void __launch_bounds__(MixCfg<BN, BK, MH>::THREADS, 1)
   umma::gdc_launch_dependents();
   umma::gdc_wait();
 
-  const int ntiles_total = 2 * a.mtiles * a.ntiles;
-  const int kblocks = a.d / C::BK;
+  const int ntiles_total = a.nmat * a.mtiles * a.ntiles;
+  const int kblocks = a.K / C::BK;
   auto decode = [&](int t, int& which, int& mt, int& nt) {
     nt = t % a.ntiles;
     const int rest = t / a.ntiles;
@@ -126,7 +129,7 @@ __global__ void __launch_bounds__(MixCfg<BN, BK, MH>::THREADS, 1)
         int which, mt, nt;
         decode(t, which, mt, nt);
         const int arow = which * a.B + mt * C::BM;
-        const int brow = which * a.d + nt * BN;
+        const int brow = which * a.N + nt * BN;
         for (int kb = 0; kb < kblocks && ok; ++kb) {
           ok = umma::mbar_wait_spin(&empty[s], ph ^ 1u);
           if (!ok) break;
@@ -134,9 +137,9 @@ __global__ void __launch_bounds__(MixCfg<BN, BK, MH>::THREADS, 1)
           uint8_t* st = sm + (size_t)s * C::STAGE;
           const int k = kb * C::BK;
           umma::tma_load_2d(st, &tmA, &full[s], k, arow);                           // c0
-          umma::tma_load_2d(st + C::A_BYTES, &tmA, &full[s], 2 * a.d + k, arow);     // c1
+          umma::tma_load_2d(st + C::A_BYTES, &tmA, &full[s], 2 * a.K + k, arow);     // c1
           umma::tma_load_3d(st + 2 * C::A_BYTES, &tmB, &full[s], k, brow, a.layer);  // w0
-          umma::tma_load_3d(st + 2 * C::A_BYTES + C::B_BYTES, &tmB, &full[s], a.d + k, brow,
+          umma::tma_load_3d(st + 2 * C::A_BYTES + C::B_BYTES, &tmB, &full[s], a.K + k, brow,
                             a.layer);                                                // w1
           if (++s == C::STAGES) {
             s = 0;
@@ -209,8 +212,8 @@ __global__ void __launch_bounds__(MixCfg<BN, BK, MH>::THREADS, 1)
       if (!umma::mbar_wait_sleep(&tfull[buf], use & 1u)) break;
       umma::tc_fence_after();
       const int b = mt * C::BM + r;
-      float* zr = a.z + ((long long)which * a.B + b) * a.d + nt * BN;
-      const float4* bias = reinterpret_cast<const float4*>(a.bias + which * a.d + nt * BN);
+      float* zr = a.z + ((long long)which * a.B + b) * a.N + nt * BN;
+      const float4* bias = a.bias ? reinterpret_cast<const float4*>(a.bias + which * a.N + nt * BN) : nullptr;
       const uint32_t tcol = tbase + ((uint32_t)(32 * q) << 16) + (uint32_t)((buf * MH + h) * BN);
       float ss = 0.f;  // this row's sum of (z + bias)^2 over the tile's columns (RMSNorm)
 #pragma unroll 1
@@ -223,17 +226,17 @@ __global__ void __launch_bounds__(MixCfg<BN, BK, MH>::THREADS, 1)
           for (int j = 0; j < 8; ++j) {
             const float4 o = make_float4(v[4 * j] * alpha, v[4 * j + 1] * alpha, v[4 * j + 2] * alpha,
                                          v[4 * j + 3] * alpha);
-            const float4 bb = __ldg(bias + c * 8 + j);
+            const float4 bb = bias ? __ldg(bias + c * 8 + j) : make_float4(0.f, 0.f, 0.f, 0.f);
             const float e0 = o.x + bb.x, e1 = o.y + bb.y, e2 = o.z + bb.z, e3 = o.w + bb.w;
             ss = fmaf(e0, e0, ss);
             ss = fmaf(e1, e1, ss);
             ss = fmaf(e2, e2, ss);
             ss = fmaf(e3, e3, ss);
-            dst[j] = o;
+            dst[j] = a.out_bias ? make_float4(e0, e1, e2, e3) : o;
           }
         }
       }
-      if (b < a.B) a.spart[((long long)which * a.ntiles + nt) * a.B + b] = ss;
+      if (b < a.B && a.spart) a.spart[((long long)which * a.ntiles + nt) * a.B + b] = ss;
       umma::tc_fence_before();
       __syncwarp();
       if (lane == 0) umma::mbar_arrive(&tempty[buf]);

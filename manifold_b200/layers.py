@@ -256,8 +256,9 @@ class ParallelMLayer(nn.Module):
     force -> LayerNorm -> A = sigmoid(to_A), dt = softplus(to_dt) * 0.1 * 1.5^head,
     B = to_B * dt -> v = scan(A, B), x = scan(1, v dt).
 
-    The three projections run as one cuBLAS GEMM against the concatenated
-    weight; the two scans and all elementwise work run in one fused kernel.
+    The three projections run as one split-fp16 tensor-core GEMM against the
+    concatenated weight (`split_gemm = False`: torch's fp32 matmul); the two
+    scans and all elementwise work run in one fused kernel.
     """
 
     def __init__(self, dim, heads=4, physics_config=None, **kwargs):
@@ -278,6 +279,8 @@ class ParallelMLayer(nn.Module):
         self.base_dt = 0.1
         if heads > 1:
             self.out_proj = nn.Linear(dim * 2, dim * 2)
+        # True: the projections on the tensor cores (split fp16); False: torch's fp32 matmul
+        self.split_gemm = True
 
     def forward(self, x, v, force, collect_christ=False):
         require_cuda(force)
@@ -286,6 +289,13 @@ class ParallelMLayer(nn.Module):
         f = self.norm_x(force)
         Wcat = torch.cat([self.to_A[0].weight, self.to_dt[0].weight, self.to_B.weight], 0)
         bcat = torch.cat([self.to_A[0].bias, self.to_dt[0].bias, self.to_B.bias], 0)
-        z = torch.nn.functional.linear(f, Wcat, bcat)
+        if self.split_gemm and f.is_cuda:
+            # the three projections as one tensor-core GEMM over split-fp16
+            # operands (~1e-6 relative, float32-level; manifold_b200.readout)
+            from .readout import SplitLinear
+            B, L, _ = f.shape
+            z = SplitLinear.apply(f.reshape(B * L, self.dim), Wcat, bcat).reshape(B, L, 3 * self.dim)
+        else:
+            z = torch.nn.functional.linear(f, Wcat, bcat)
         x_seq, v_seq = ops.parallel_layer_scan(z, self.heads, self.base_dt)
         return x_seq, v_seq, None, []

@@ -47,12 +47,19 @@ class SplitLinear(torch.autograd.Function):
         V = W.shape[0]
         out = torch.empty(M, V, device=y.device, dtype=torch.float32)
         w2, sw = _split(W, False, True)  # B' = W^T: K = d along W's columns
+        tc = d <= 512 and d % 32 == 0 and V % 64 == 0
+        bias = b.detach().float().contiguous() if b is not None else None
+        alpha = torch.empty(4, device=y.device, dtype=torch.float32)
         for r0 in range(0, M, CHUNK_ROWS):
             yc = y[r0:r0 + CHUNK_ROWS]
             y2, sy = _split(yc, False, False)
-            _gemm(yc.shape[0], V, d, y2, sy, False, w2, sw, False, out[r0:r0 + CHUNK_ROWS])
-        if b is not None:
-            out += b.detach().float()
+            if tc:  # the library's tcgen05 GEMM, bias added in its epilogue
+                call("gfn_gemm_split_f16_tc", yc.shape[0], V, d, ptr(y2), ptr(w2), ptr(sy), ptr(sw), ptr(bias),
+                     ptr(out[r0:r0 + CHUNK_ROWS]), ptr(alpha), _lib.stream_of(y.device))
+            else:
+                _gemm(yc.shape[0], V, d, y2, sy, False, w2, sw, False, out[r0:r0 + CHUNK_ROWS])
+        if b is not None and not tc:
+            out += bias
         ctx.save_for_backward(y, W)
         ctx.has_bias = b is not None
         return out
