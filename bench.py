@@ -67,6 +67,8 @@ def flops_per_token(c):
 def rank_batch(c, world):
     """Rows per rank: C4's streams are a fixed total sharded over the ranks
     (strong scaling); every other config gives each rank its own batch."""
+    if c.get("batch_override"):
+        return c["batch_override"]
     if c.get("strong"):
         if c["B"] % world:
             raise SystemExit(f"{c['B']} streams do not shard evenly over {world} GPUs")
@@ -746,6 +748,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--config", default="c4", choices=sorted(CONFIGS))
     ap.add_argument("--chunk", type=int, default=0, help="tokens per step (default per config)")
+    ap.add_argument("--batch", type=int, default=0,
+                    help="rows per GPU (default: the config's; C4 shards its 4096 streams)")
     ap.add_argument("--cpu-tokens", type=int, default=0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--path", default="auto", choices=["auto", "fused", "layered"],
@@ -756,6 +760,8 @@ def main():
                     help="print per-phase cycle counts of CTA 0 for one step instead")
     args = ap.parse_args()
     c = dict(CONFIGS[args.config], name=args.config)
+    if args.batch:
+        c["batch_override"] = args.batch
     if args.impl == "reference":
         out = run_reference(args, c)
     else:

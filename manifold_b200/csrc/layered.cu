@@ -98,7 +98,7 @@ MixShape pick_mix_shape(int batch, int dim, int sms, int nmat = 2, int K = 0) {
   const long long mt1 = (batch + 127) / 128, mt2 = (batch + 255) / 256;
   if (dim % 256 == 0 && nmat * mt2 * (dim / 256) >= (sms * 3) / 4) m = {256, 32, 2};
   else if (dim % 256 == 0 && nmat * mt1 * (dim / 256) >= sms) m = {256, 64, 1};
-  else if (dim % 128 == 0 && nmat * mt1 * (dim / 128) >= sms) m = {128, 64, 1};
+  else if (dim % 128 == 0 && nmat * mt1 * (dim / 128) >= (sms * 3) / 4) m = {128, 64, 1};
   if (K && K % m.bk) m.bk = 32;  // K blocks must divide the reduction
   if (const char* env = getenv("GFN_MIX_TILE")) {  // tuning override "BN,BK,MH"
     int bn, bk, mh;
@@ -194,19 +194,23 @@ void launch_mix(const MixUmmaPlan& p, const MixUmmaArgs& ma, cudaStream_t s) {
 #undef GFN_MIX_LAUNCH
 }
 
-// Tensor-core head step (head_dim 64, UMMA mixing): used when it gives every
-// SM at least one 128-row tile; GFN_LAY_HEAD=0/1 forces it off/on.
+// Tensor-core head step (head_dim 64, UMMA mixing); measured faster than the
+// SIMT head step at every C4 batch (512 to 4096 rows).  GFN_LAY_HEAD=0/1
+// forces it off/on.
 bool use_head_umma(int batch, int heads, int hd, int rank, int mode, int sms) {
+  (void)batch; (void)heads; (void)sms;
   if (hd != 64 || mode != GFN_MIX_UMMA_F16 || (rank != 4 && rank != 8 && rank != 16)) return false;
   if (const char* env = getenv("GFN_LAY_HEAD")) return atoi(env) != 0;
-  return (long long)((batch + 127) / 128) * heads >= sms;
+  return true;
 }
 
 // Threads per row of the tensor-core head step: 4 (two 512-thread CTAs per
-// SM, measured faster at C4) or 8 (GFN_LAY_HEAD_PARTS=8).
-int head_parts() {
+// SM) when there are at least as many tiles as SMs (C4 at 2048 and 4096
+// rows), else 8 (half the work per thread, a shorter chain per tile: 512 rows
+// 27.3 -> 24.9 us, 1024 rows 29.3 -> 25.1 us).  GFN_LAY_HEAD_PARTS=4/8 overrides.
+int head_parts(int batch, int heads, int sms) {
   if (const char* env = getenv("GFN_LAY_HEAD_PARTS")) return atoi(env) == 8 ? 8 : 4;
-  return 4;
+  return (long long)((batch + 127) / 128) * heads >= sms ? 4 : 8;
 }
 
 template <int P>
@@ -223,8 +227,8 @@ void launch_head_umma_p(int rank, const CUtensorMap& tmz, const CUtensorMap& tmo
 }
 
 void launch_head_umma(int rank, const CUtensorMap& tmz, const CUtensorMap& tmo, const LayPreArgs& a,
-                      dim3 grid, cudaStream_t s) {
-  if (head_parts() == 4)
+                      dim3 grid, cudaStream_t s, int sms) {
+  if (head_parts(a.B, a.H, sms) == 4)
     launch_head_umma_p<4>(rank, tmz, tmo, a, grid, s);
   else
     launch_head_umma_p<8>(rank, tmz, tmo, a, grid, s);
@@ -599,7 +603,7 @@ int gfn_leapfrog_layered_forward(const float* x_init, const float* v_init,
       a.prof = g_head_prof;
       time_mark(s);
       if (head_tc)
-        launch_head_umma(rank, zmap, omap, a, head_grid, s);
+        launch_head_umma(rank, zmap, omap, a, head_grid, s, sms);
       else
         pre<<<pre_grid, LAY_THREADS, pre_smem, s>>>(a);
       time_mark(s);
