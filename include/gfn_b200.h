@@ -177,8 +177,9 @@ int gfn_christoffel_backward(const float* grad_gamma, const float* v, const floa
  *   grad_f [batch, dim] (optional), grad_U / grad_W [dim, rank] (topology 0),
  *   grad_W_forget [dim, fin] + grad_b_forget [dim] when W_forget is given,
  *   grad_W_input [dim, dim] when W_input is given.
- * Parameter gradients are batch sums in a fixed order (overwritten).  dt
- * scales are constants (no gradient).  Workspace:
+ * Parameter gradients are batch sums in a fixed order (overwritten).
+ * grad_dt_scale (optional, [batch]): dL/d dt_scale of each row (sum the rows
+ * for a shared scale).  Workspace:
  * gfn_leapfrog_step_backward_workspace_floats(batch, dim, rank, steps, topology).
  */
 long long gfn_leapfrog_step_backward_workspace_floats(int batch, int dim, int rank, int steps,
@@ -188,7 +189,8 @@ int gfn_leapfrog_backward(const float* grad_x_new, const float* grad_v_new, cons
                           const float* W_forget, const float* b_forget, const float* W_input,
                           float* grad_x, float* grad_v, float* grad_f, float* grad_U,
                           float* grad_W, float* grad_W_forget, float* grad_b_forget,
-                          float* grad_W_input, int batch, int dim, int rank, float dt,
+                          float* grad_W_input, float* grad_dt_scale, int batch, int dim, int rank,
+                          float dt,
                           const float* dt_scales, int dt_scales_count, int steps, int topology,
                           float R_val, float r_val, float* workspace, long long workspace_floats,
                           gfn_stream_t stream);

@@ -70,7 +70,7 @@ _SIGS = {
                                  _i, _f, _f, _p, _ll, _p],
     "gfn_leapfrog_step_backward_workspace_floats": [_i, _i, _i, _i, _i],
     "gfn_leapfrog_backward": [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p,
-                              _i, _i, _i, _f, _p, _i, _i, _i, _f, _f, _p, _ll, _p],
+                              _p, _i, _i, _i, _f, _p, _i, _i, _i, _f, _f, _p, _ll, _p],
 }
 _RESTYPES = {
     "gfn_status_string": ctypes.c_char_p,

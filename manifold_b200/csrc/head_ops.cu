@@ -148,7 +148,8 @@ int gfn_leapfrog_backward(const float* grad_x_new, const float* grad_v_new, cons
                           const float* f, const float* U, const float* W, const float* W_forget,
                           const float* b_forget, const float* W_input, float* grad_x, float* grad_v,
                           float* grad_f, float* grad_U, float* grad_W, float* grad_W_forget,
-                          float* grad_b_forget, float* grad_W_input, int batch, int dim, int rank, float dt,
+                          float* grad_b_forget, float* grad_W_input, float* grad_dt_scale, int batch, int dim,
+                          int rank, float dt,
                           const float* dt_scales, int dt_scales_count, int steps, int topology, float R_val,
                           float r_val, float* workspace, long long workspace_floats, gfn_stream_t stream) {
   int st = check_common("leapfrog backward", batch, dim, rank, topology, 0.f, R_val, r_val);
@@ -186,6 +187,7 @@ int gfn_leapfrog_backward(const float* grad_x_new, const float* grad_v_new, cons
     if (e == cudaSuccess && W_forget) e = cudaMemsetAsync(grad_W_forget, 0, (size_t)dim * fin * 4, s);
     if (e == cudaSuccess && W_forget) e = cudaMemsetAsync(grad_b_forget, 0, (size_t)dim * 4, s);
     if (e == cudaSuccess && W_input) e = cudaMemsetAsync(grad_W_input, 0, (size_t)dim * dim * 4, s);
+    if (e == cudaSuccess && grad_dt_scale && batch) e = cudaMemsetAsync(grad_dt_scale, 0, (size_t)batch * 4, s);
     return cuda_status(e, "leapfrog backward: empty problem");
   }
   hops::Params p = {};
@@ -194,6 +196,7 @@ int gfn_leapfrog_backward(const float* grad_x_new, const float* grad_v_new, cons
   p.dt_scale = dt_scales; p.dt_scale_n = dt_scales_count; p.dt = dt; p.steps = steps;
   p.topo = topology; p.R = R_val; p.r = r_val; p.B = batch; p.hd = dim; p.fin = fin;
   p.gx_in = grad_x_new; p.gv_in = grad_v_new; p.gx = grad_x; p.gv = grad_v; p.gf = grad_f; p.ws = workspace;
+  p.gdt = grad_dt_scale;
   st = dispatch<BwdLaunch>(rank, dim, p, smem, s);
   if (st) return st;
   const float* sig = workspace + (long long)steps * batch * 2 * dim;

@@ -62,6 +62,7 @@ struct Params {
   float* gx;
   float* gv;
   float* gf;
+  float* gdt;            // backward: dL / d dt_scale per row (null: not wanted)
   float* ws;             // states [steps][B][2 hd] then signals [steps][2][B][SR]
 };
 
@@ -581,19 +582,20 @@ __global__ void __launch_bounds__(WARPS * 32) head_bwd_kernel(const Params a) {
     }
   }
   float gx[EPL], gv[EPL], gF[EPL];
+  float geff = 0.f;  // this lane's part of dL / d eff
   row_load<EPL>(gx, a.gx_in ? a.gx_in + off : nullptr, hd, lane);
   row_load<EPL>(gv, a.gv_in ? a.gv_in + off : nullptr, hd, lane);
 #pragma unroll
   for (int e = 0; e < EPL; ++e) gF[e] = 0.f;
   for (int st = a.steps - 1; st >= 0; --st) {
     const float* sp = states + ((long long)st * B + row) * 2 * hd;
-    float xs[2][EPL], vs[3][EPL], sgs[2][EPL], ts[2][EPL], ps[2][RK], ss[2];
+    float xs[2][EPL], vs[3][EPL], sgs[2][EPL], ts[2][EPL], gs[2][EPL], ps[2][RK], ss[2];
     row_load<EPL>(xs[0], sp, hd, lane);
     row_load<EPL>(vs[0], sp + hd, hd, lane);
     // recompute both kicks
 #pragma unroll
     for (int half = 0; half < 2; ++half) {
-      float g[EPL];
+      float (&g)[EPL] = gs[half];
       if (fric) friction<EPL>(xs[half], zin, sm, L, rb, hd, fin, a.topo, lane, sgs[half]);
       else {
 #pragma unroll
@@ -621,6 +623,8 @@ __global__ void __launch_bounds__(WARPS * 32) head_bwd_kernel(const Params a) {
         const float sgv = sgs[half][e];
         const float den = 1.f + h * (sgv * 5.f);
         ga[e] = gv[e] / den;
+        // d v' / d h = ((F - Gamma) - v' mu) / den, and h = eff / 2
+        geff = fmaf(0.5f * ga[e], (F[e] - gs[half][e]) - vs[half + 1][e] * (sgv * 5.f), geff);
         gz[e] = fric ? (-(gv[e] * vs[half + 1][e]) / den) * h * 5.f * sgv * (1.f - sgv) : 0.f;
         gF[e] += h * ga[e];
         gg[e] = -h * ga[e];
@@ -639,7 +643,10 @@ __global__ void __launch_bounds__(WARPS * 32) head_bwd_kernel(const Params a) {
       if (half == 1) {
         // drift x1 = x0 + eff v1 (the wrap passes the gradient through)
 #pragma unroll
-        for (int e = 0; e < EPL; ++e) gv[e] = gvn[e] + eff * gx[e];
+        for (int e = 0; e < EPL; ++e) {
+          geff = fmaf(gx[e], vs[1][e], geff);
+          gv[e] = gvn[e] + eff * gx[e];
+        }
       } else {
 #pragma unroll
         for (int e = 0; e < EPL; ++e) gv[e] = gvn[e];
@@ -649,6 +656,8 @@ __global__ void __launch_bounds__(WARPS * 32) head_bwd_kernel(const Params a) {
   row_store<EPL>(gx, a.gx + off, hd, lane);
   row_store<EPL>(gv, a.gv + off, hd, lane);
   if (a.gf) row_store<EPL>(gF, a.gf + off, hd, lane);
+  geff = warp_sum(geff);  // eff = dt * dt_scale: d/d dt_scale = dt d/d eff
+  if (a.gdt && lane == 0) a.gdt[row] = geff * a.dt;
 }
 
 // ---------------------------------------------------------------- other integrators

@@ -33,8 +33,8 @@ def christoffel_fused_autograd(v, U, W, x=None, V_w=None, plasticity=0.0, sing_t
 
 
 class LeapfrogFusedFn(Function):
-    """gfn/cuda/autograd.py:74-101, with the friction gate (Wf, bf) and input
-    gate (Wi) differentiated too."""
+    """gfn/cuda/autograd.py:74-101, with the friction gate (Wf, bf), the input
+    gate (Wi) and a tensor dt_scale differentiated too."""
 
     @staticmethod
     def forward(ctx, x, v, f, U, W, dt, dt_scale, steps, topology, Wf, bf, plasticity, R, r, Wi):
@@ -47,10 +47,13 @@ class LeapfrogFusedFn(Function):
     def backward(ctx, grad_xn, grad_vn):
         x, v, f, U, W, Wf, bf, Wi = ctx.saved_tensors
         dt, dt_scale, steps, topology, R, r = ctx.args
-        if isinstance(dt_scale, torch.Tensor):
-            dt_scale = dt_scale.detach()
-        out = ops.leapfrog_backward(grad_xn, grad_vn, x, v, f, U, W, dt, dt_scale, steps, topology, R,
-                                    r, Wf=Wf, bf=bf, Wi=Wi)
+        want_dt = isinstance(dt_scale, torch.Tensor) and ctx.needs_input_grad[6]
+        dts = dt_scale.detach() if isinstance(dt_scale, torch.Tensor) else dt_scale
+        out = ops.leapfrog_backward(grad_xn, grad_vn, x, v, f, U, W, dt, dts, steps, topology, R,
+                                    r, Wf=Wf, bf=bf, Wi=Wi, want_dt=want_dt)
+        gdt = None
+        if want_dt:
+            gdt = out.pop().reshape(dt_scale.shape).to(dt_scale.dtype)
         gx, gv, gf, gU, gW = out[:5]
         rest = out[5:]
         gWf = gbf = gWi = None
@@ -61,7 +64,7 @@ class LeapfrogFusedFn(Function):
                 gbf = None
         if Wi is not None:
             gWi = rest[0]
-        return (gx, gv, gf, gU, gW, None, None, None, None, gWf, gbf, None, None, None, gWi)
+        return (gx, gv, gf, gU, gW, None, gdt, None, None, gWf, gbf, None, None, None, gWi)
 
 
 def leapfrog_fused_autograd(x, v, f, U, W, dt, dt_scale, steps, topology=0, Wf=None, bf=None,

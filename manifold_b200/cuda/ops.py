@@ -150,11 +150,12 @@ def _leapfrog_forward(x, v, f, U, W, dt, dt_scale, steps, topology, Wf, bf, plas
 
 
 def leapfrog_backward(grad_x_new, grad_v_new, x, v, f, U, W, dt, dt_scale, steps, topology=0,
-                      R=2.0, r=1.0, Wf=None, bf=None, Wi=None):
+                      R=2.0, r=1.0, Wf=None, bf=None, Wi=None, want_dt=False):
     """Backward of leapfrog_fused (the gfn_cuda.leapfrog_backward binding,
     gfn/cuda/cuda_kernels.cpp:190-196), by reverse replay.  Returns
     [grad_x, grad_v, grad_f, grad_U, grad_W], followed by grad_Wf, grad_bf
-    when Wf is given and grad_Wi when Wi is given.  dt_scale is a constant."""
+    when Wf is given, grad_Wi when Wi is given, and (want_dt) the gradient of
+    dt_scale in its own shape (one value or one per row)."""
     require_cuda(x, v, f, U, W, Wf, bf, Wi, grad_x_new, grad_v_new)
     x, v = _f32c(x, "x"), _f32c(v, "v")
     f, Wf, bf, Wi = _f32c(f, "f"), _f32c(Wf, "Wf"), _f32c(bf, "bf"), _f32c(Wi, "Wi")
@@ -180,15 +181,18 @@ def leapfrog_backward(grad_x_new, grad_v_new, x, v, f, U, W, dt, dt_scale, steps
     gWi = torch.empty(d, d, device=dev, dtype=torch.float32) if Wi is not None else None
     n = _lib.load().gfn_leapfrog_step_backward_workspace_floats(B, d, rank, int(steps), int(topology))
     ws = torch.empty(max(int(n), 1), device=dev, dtype=torch.float32)
+    gdt = torch.empty(B, device=dev, dtype=torch.float32) if want_dt else None
     call("gfn_leapfrog_backward", ptr(gxn), ptr(gvn), ptr(x), ptr(v), ptr(f), ptr(U), ptr(W), ptr(Wf),
          ptr(bf), ptr(Wi), ptr(gx), ptr(gv), ptr(gf), ptr(gU), ptr(gW), ptr(gWf), ptr(gbf), ptr(gWi),
-         B, d, rank, float(dt), ptr(dts), dts.numel(), int(steps), int(topology), float(R), float(r),
+         ptr(gdt), B, d, rank, float(dt), ptr(dts), dts.numel(), int(steps), int(topology), float(R), float(r),
          ptr(ws), ws.numel(), _stream(x))
     out = [gx, gv, gf, gU, gW]
     if Wf is not None:
         out += [gWf, gbf]
     if Wi is not None:
         out.append(gWi)
+    if want_dt:
+        out.append(gdt.sum().reshape(1) if dts.numel() == 1 else gdt)
     return out
 
 

@@ -180,10 +180,54 @@ class MLayer(nn.Module):
         [sin x, cos x, tanh(v / 100)] and x wraps into [0, 2 pi) instead of
         the RMSNorm)."""
         if self.training and torch.is_grad_enabled() and any(p.requires_grad for p in self.parameters()):
-            raise GfnError("training is implemented for the Euclidean leapfrog path only (call eval() "
-                           "or run under torch.no_grad() for inference)")
+            ai = self.physics_config.get("active_inference", {})
+            if self.integrator_type != "leapfrog" or self.use_dynamic_time or ai.get("enabled", False):
+                raise GfnError("training is implemented for the leapfrog integrator without active "
+                               "curvature or dynamic time (call eval() or run under torch.no_grad() "
+                               "for inference)")
+            return self._generic_step_train(x, v, force, context)
         with torch.no_grad():
             return self._generic_step_nograd(x, v, force, context)
+
+    def _generic_step_train(self, x, v, force, context):
+        """Differentiable leapfrog layer step for the torus (and the Euclidean
+        leapfrog with recursive geodesics): per head the leapfrog autograd
+        operator (forward kernel, reverse-replay backward with the gradients of
+        the state, force, U, W, the forget gate and the dt scale), then the
+        head mixing of gfn/layers/base.py:304-335 with torch's autograd."""
+        B = x.shape[0]
+        H, hd = self.heads, self.head_dim
+        if self.use_recursive and context is not None:
+            force = force + self.context_proj(context)
+        dts = torch.nn.functional.softplus(self.dt_params)
+        xo, vo = [], []
+        for h, ch in enumerate(self.christoffels):
+            sl = slice(h * hd, (h + 1) * hd)
+            if self.topology_id == 1:
+                U = W = None
+                R, r = ch.R, ch.r
+            else:
+                U, W, R, r = ch.U, ch.W, 2.0, 1.0
+            xh, vh = ops.leapfrog_fused(x[:, sl].contiguous(), v[:, sl].contiguous(), force[:, sl].contiguous(),
+                                        U, W, self.base_dt, dts[h:h + 1], 1, topology=self.topology_id,
+                                        Wf=ch.forget_gate.weight, bf=ch.forget_gate.bias, R=R, r=r)
+            xo.append(xh)
+            vo.append(vh)
+        xc, vc = torch.cat(xo, -1), torch.cat(vo, -1)
+        return self._mix(xc, vc, B, H)
+
+    def _mix(self, xc, vc, B, H):
+        if H > 1:
+            if self.topology_id == 1:
+                mix_in = torch.cat([torch.sin(xc), torch.cos(xc), torch.tanh(vc / 100.0)], dim=-1)
+                xn = torch.remainder(self.out_proj_x(mix_in), 2.0 * 3.14159265359)
+            else:
+                xn = self.mixed_norm_x(self.out_proj_x(xc))
+            vn = self.mixed_norm_v(self.out_proj_v(vc))
+        else:
+            xn, vn = xc, vc
+        vn = 100.0 * torch.tanh(vn / 100.0)
+        return xn, vn, torch.ones(B, H, device=xc.device, dtype=xc.dtype), []
 
     def _active_terms(self):
         """Active-inference operands (gfn/geometry/reactive.py:53-81,

@@ -61,6 +61,11 @@ GRAD_CASES = {
     "gmask":  dict(V=7, d=64, NL=3, H=4, rank=16, B=4, L=6, dt=0.05, seed=33, mask=True),
     "gc5":    dict(V=300, d=512, NL=2, H=8, rank=32, B=2, L=3, dt=0.1, seed=34),
 }
+# gradient cases of the generic (layer-by-layer) path
+GENERIC_GRAD_CASES = {
+    "gtorus": dict(V=7, d=32, NL=2, H=2, rank=8, B=3, L=4, dt=0.1, seed=36, torus=True),
+    "gtorus_h1": dict(V=5, d=16, NL=2, H=1, rank=4, B=2, L=3, dt=0.1, seed=37, torus=True),
+}
 
 
 def head_rank(cfg):

@@ -265,8 +265,9 @@ def gen_grad_case(name, cfg):
     big = name == "gc5"
     for l, layer in enumerate(m.layers):
         out[f"l{l}_dt_params"] = layer.dt_params.grad.numpy()
-        out[f"l{l}_U"] = np.stack([c.U.grad.numpy() for c in layer.christoffels])
-        out[f"l{l}_W"] = np.stack([c.W.grad.numpy() for c in layer.christoffels])
+        if not cfg.get("torus"):
+            out[f"l{l}_U"] = np.stack([c.U.grad.numpy() for c in layer.christoffels])
+            out[f"l{l}_W"] = np.stack([c.W.grad.numpy() for c in layer.christoffels])
         out[f"l{l}_Wf"] = np.stack([c.forget_gate.weight.grad.numpy() for c in layer.christoffels])
         out[f"l{l}_bf"] = np.stack([c.forget_gate.bias.grad.numpy() for c in layer.christoffels])
         if cfg["H"] > 1:
@@ -279,7 +280,9 @@ def gen_grad_case(name, cfg):
                 else:
                     out[f"l{l}_W{nm}"] = gW
                 out[f"l{l}_b{nm}"] = getattr(layer, mod).bias.grad.numpy()
-                out[f"l{l}_g{nm}"] = getattr(layer, "mixed_norm_" + nm).weight.grad.numpy()
+                gn = getattr(layer, "mixed_norm_" + nm).weight.grad
+                if gn is not None:  # the torus mixes x without the RMSNorm
+                    out[f"l{l}_g{nm}"] = gn.numpy()
     np.savez_compressed(os.path.join(HERE, f"{name}.npz"), **out)
     print(name, len(out))
 
@@ -328,6 +331,8 @@ if __name__ == "__main__":
             gen_init()
         elif n in C.GRAD_CASES:
             gen_grad_case(n, C.GRAD_CASES[n])
+        elif n in C.GENERIC_GRAD_CASES:
+            gen_grad_case(n, C.GENERIC_GRAD_CASES[n])
         else:
             gen_model_case(n, C.CASES[n])
     if not sys.argv[1:]:

@@ -152,3 +152,29 @@ def test_mlayer_step_gradients_flow():
     (xn.sum() + 2 * vn.sum()).backward()
     assert x.grad is not None and torch.isfinite(x.grad).all()
     assert layer.out_proj_x.weight.grad is not None
+
+
+@pytest.mark.parametrize("name", list(C.GENERIC_GRAD_CASES))
+def test_generic_torus_backward_matches_reference_autograd(name):
+    """Training on the torus (the generic layer step with the leapfrog
+    autograd operator): gradients of forces, initial state, dt_params, the
+    forget gates and the mixing against the reference's autograd."""
+    cfg = C.GENERIC_GRAD_CASES[name]
+    g = dict(np.load(os.path.join(GOLD, f"{name}.npz")))
+    P = C.make_params(cfg)
+    m, F = run_grad(cfg, P, g["ids"], g["Gx"], g["Gv"], g["gxf"], g["gvf"])
+    assert m.layers[0].generic
+    gclose(F.grad.cpu(), g["g_forces"], "forces")
+    gclose(m.x0.grad.cpu()[0], g["g_x0"], "x0")
+    gclose(m.v0.grad.cpu()[0], g["g_v0"], "v0")
+    for l, layer in enumerate(m.layers):
+        gclose(layer.dt_params.grad.cpu(), g[f"l{l}_dt_params"], f"l{l} dt_params")
+        gclose(torch.stack([c.forget_gate.weight.grad for c in layer.christoffels]).cpu(), g[f"l{l}_Wf"],
+               f"l{l} Wf")
+        gclose(torch.stack([c.forget_gate.bias.grad for c in layer.christoffels]).cpu(), g[f"l{l}_bf"],
+               f"l{l} bf")
+        if cfg["H"] > 1:
+            for nm in ("x", "v"):
+                gclose(getattr(layer, "out_proj_" + nm).weight.grad.cpu(), g[f"l{l}_W{nm}"], f"l{l} W{nm}")
+                gclose(getattr(layer, "out_proj_" + nm).bias.grad.cpu(), g[f"l{l}_b{nm}"], f"l{l} b{nm}")
+            gclose(layer.mixed_norm_v.weight.grad.cpu(), g[f"l{l}_gv"], f"l{l} gv")
