@@ -229,6 +229,20 @@ def run_train(args, c):
     torch.cuda.synchronize(dev)
     clocks = sampler.stop() if sampler else None
     ms = sum(a.elapsed_time(b) for a, b in ev)
+    # per-kernel device time of the two recurrence kernels (a second timed
+    # pass with CUDA events around each launch), for the latency roofline
+    from manifold_b200 import training as TR
+    TR.KERNEL_EVENTS = []
+    for i in range(min(2, steps)):
+        flush.zero_()
+        step(warm + i)
+    torch.cuda.synchronize(dev)
+    kev, TR.KERNEL_EVENTS = TR.KERNEL_EVENTS, None
+    kt = {"fwd": [], "bwd": []}
+    for tag, a0, a1 in kev:
+        kt[tag].append(a0.elapsed_time(a1))
+    fwd_ms = float(np.mean(kt["fwd"])) if kt["fwd"] else None
+    bwd_ms = float(np.mean(kt["bwd"])) if kt["bwd"] else None
     if os.environ.get("GFN_BENCH_DEBUG"):
         print(f"rank {rank} step ms {[round(a.elapsed_time(b), 1) for a, b in ev]}", file=sys.stderr)
     if world > 1:
@@ -254,9 +268,7 @@ def run_train(args, c):
                     "h2d_bytes_per_step": int(B * (T + 1) * 8), "d2h_bytes_per_step": 4,
                     "note": "each timed step already copies its ids from pinned host memory and reads the loss back"},
             "gpu_launches": steps * 4,
-            "roofline": {"bound": "hbm", "achieved": None, "peak": hbm, "unit": "GB/s", "frac": None,
-                         "traffic": None, "peak_source": kind,
-                         "note": "training step: recurrence forward + backward kernels, cuBLAS readout/CE and weight-gradient GEMMs"},
+            "roofline": c5_roofline(c, B, T, ms / steps, fwd_ms, bwd_ms, dev),
             "loss": [round(x, 4) for x in losses],
             "clocks": clocks,
         }
@@ -264,6 +276,33 @@ def run_train(args, c):
         dist.barrier()
         dist.destroy_process_group()
     return result
+
+
+def c5_roofline(c, B, T, step_ms, fwd_ms, bwd_ms, dev):
+    """Training step roofline: the two recurrence kernels (84% of the step,
+    profiles/launches_c5.md) are dependent chains over T tokens x NL layers.
+    Floor of one layer step = the latency probe's dependent chain on this
+    plan; the backward replays the forward chain and runs the reverse chain,
+    so its floor is taken as twice that (a lower bound)."""
+    from manifold_b200.cuda import ops
+    r = max(4, c["rank"] // c["H"])
+    plan = ops.leapfrog_plan(B, c["d"], c["H"], r, c["NL"])
+    n = T * c["NL"]
+    fwd_ns = fwd_ms * 1e6 / n if fwd_ms else None
+    lat = latency_floor(dev, r, plan["clusters"], fwd_ns or 1.0)
+    floor = lat["floor_ns_per_layer_step"]
+    bwd_ns = bwd_ms * 1e6 / n if bwd_ms else None
+    out = {"bound": "latency", "kernel": "leapfrog_bwd_kernel", "unit": "ns per layer step",
+           "achieved": round(bwd_ns, 1) if bwd_ns else None, "peak": round(2 * floor, 1),
+           "frac": round(2 * floor / bwd_ns, 4) if bwd_ns else None, "traffic": None,
+           "forward": {"kernel": "leapfrog_seq_kernel (training)", "ms_per_launch": fwd_ms,
+                       "ns_per_layer_step": round(fwd_ns, 1) if fwd_ns else None,
+                       "floor_ns": floor, "frac": round(floor / fwd_ns, 4) if fwd_ns else None},
+           "backward": {"ms_per_launch": bwd_ms, "floor_ns": round(2 * floor, 1),
+                        "floor_note": "forward replay + reverse chain, each at least the probe floor"},
+           "share_of_step": round(((fwd_ms or 0) + (bwd_ms or 0)) / step_ms, 3),
+           "latency_probe": lat["source"]}
+    return out
 
 
 def run_ours(args, c):

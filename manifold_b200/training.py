@@ -26,6 +26,21 @@ def _stacks(layers):
     return out
 
 
+# Measurement hook: when a list, each forward / backward recurrence launch
+# appends ("fwd" | "bwd", start event, end event), CUDA events recorded on the
+# launch stream around the kernel (bench.py's C5 roofline reads them).
+KERNEL_EVENTS = None
+
+
+def _mark(tag, stream):
+    """An event on the current stream (the stream the library launches on)."""
+    if KERNEL_EVENTS is None:
+        return None
+    e = torch.cuda.Event(enable_timing=True)
+    e.record()
+    return e
+
+
 class LeapfrogSequenceTrain(torch.autograd.Function):
     """(x0, v0, forces, *param stacks) -> (x_seq, v_seq, x_final, v_final)."""
 
@@ -59,9 +74,12 @@ class LeapfrogSequenceTrain(torch.autograd.Function):
         xf = torch.empty(B, d, device=dev)
         vf = torch.empty_like(xf)
         traj = torch.empty(2, NL, L, B, d, device=dev)
+        e0 = _mark("fwd", stream)
         call("gfn_leapfrog_sequence_forward_train", ptr(x0c), ptr(v0c), d, ptr(fl32), ptr(fbf), None,
              None, 0, ptr(m), ptr(packed), packed.numel(), B, L, d, H, r, NL, float(base_dt),
              ptr(x_seq), ptr(v_seq), ptr(xf), ptr(vf), ptr(traj), stream)
+        if e0 is not None:
+            KERNEL_EVENTS.append(("fwd", e0, _mark("fwd", stream)))
         ctx.save_for_backward(packed, traj, fc, *[t for t in st])
         ctx.mask = m
         ctx.meta = meta
@@ -87,10 +105,13 @@ class LeapfrogSequenceTrain(torch.autograd.Function):
         dF = torch.empty(B, L, d, device=dev)
         fl32 = fc if fc.dtype == torch.float32 else None
         fbf = fc if fc.dtype == torch.bfloat16 else None
+        bstream = _lib.stream_of(dev)
+        e0 = _mark("bwd", bstream)
         call("gfn_leapfrog_sequence_backward", ptr(traj), ptr(fl32), ptr(fbf), None, None, 0,
              ptr(ctx.mask), ptr(packed), packed.numel(), ptr(gxs), ptr(gvs), ptr(gxf), ptr(gvf), B, L,
-             d, H, r, NL, float(base_dt), ptr(dx0), ptr(dv0), ptr(dF), ptr(ws), ws.numel(),
-             _lib.stream_of(dev))
+             d, H, r, NL, float(base_dt), ptr(dx0), ptr(dv0), ptr(dF), ptr(ws), ws.numel(), bstream)
+        if e0 is not None:
+            KERNEL_EVENTS.append(("bwd", e0, _mark("bwd", bstream)))
         grads = param_grads(ws, traj, st, B, L, d, H, r, NL, base_dt)
         if ctx.broadcast:
             dx0 = dx0.sum(0, keepdim=True)
