@@ -31,39 +31,48 @@
 
 namespace gfn {
 
-template <int HD, int P>
+template <int HD, int P, bool HALF = false>
 struct HeadUmmaCfg {
   // PARTS threads per row (one warp per TMEM lane quarter and column part).
   // PARTS 8: 1024 threads, the force staged in shared memory, one CTA per SM;
   // PARTS 4: 512 threads, the force in registers, two CTAs per SM.
-  static constexpr int ROWS = 128, PARTS = P, THREADS = 128 * PARTS, CPT = HD / PARTS;
-  static constexpr bool F_SMEM = P == 8;
-  static constexpr int MIN_BLOCKS = P == 8 ? 1 : 2;
-  static constexpr int TL = CPT < 16 ? CPT : 16;  // TMEM columns per load
+  // HALF: 64-row tiles, 512 threads, 8 columns per thread.  The gate's A
+  // operand holds the 64 rows twice (MMA rows r and r + 64, M = 128 keeps the
+  // one-row-per-TMEM-lane accumulator layout), so the warps of TMEM lane
+  // quarters 0-1 read columns 0-31 and those of quarters 2-3 columns 32-63 of
+  // the same rows: twice the tiles of 128-row tiles at the same work per
+  // thread as PARTS 8, without register spills.
+  static constexpr int ROWS = 128;                      // MMA rows
+  static constexpr int RROWS = HALF ? 64 : 128;         // batch rows per tile
+  static constexpr int PARTS = HALF ? 8 : P;            // threads (column parts) per row
+  static constexpr int THREADS = HALF ? 512 : 128 * P;
+  static constexpr int CPT = HD / PARTS;
+  static constexpr bool F_SMEM = !HALF && P == 8;
+  static constexpr int MIN_BLOCKS = (HALF || P != 8) ? 2 : 1;
   static constexpr int ROWB = HD * 2;             // bytes per fp16 operand row
   static constexpr int A_BYTES = ROWS * ROWB;     // one fp16 piece of x (or v)
+  static constexpr int VO_BYTES = RROWS * ROWB;   // one fp16 piece of the v' output
   static constexpr int W_BYTES = HD * ROWB;       // one fp16 piece of W_f
-  static constexpr int ZBOX = ROWS * 128;         // one [128][32] fp32 box
+  static constexpr int ZBOX = RROWS * 128;        // one [RROWS][32] fp32 box
   // shared memory (bytes):
-  //   [0, 64K)    z boxes [x lo | x hi | v lo | v hi]; then x pieces c0 | c1
-  //               (the gate's A operand; x' is also the output) and v' pieces
-  //   [64K, 96K)  the token's force, [128][HD] fp32 as two swizzled boxes
+  //   staging: z boxes [x lo | x hi | v lo | v hi]; then x pieces c0 | c1
+  //            (the gate's A operand; x' is also the output) and v' pieces
+  //   the token's force, [128][HD] fp32 as two swizzled boxes (PARTS 8 only)
   //   W_f pieces w0 | w1; bias / gain of the previous layer [4][HD];
-  //   U [HD][RK]; W^T [RK][HD]; b_f [HD]; p parts [PARTS][128][RK]; barriers
-  static constexpr int STAGE = 4 * ZBOX;
+  //   U [HD][RK]; W^T [RK][HD]; b_f [HD]; p parts [PARTS][RROWS][RK]; barriers
+  static constexpr int STAGE = (4 * ZBOX > 2 * A_BYTES + 2 * VO_BYTES) ? 4 * ZBOX : 2 * A_BYTES + 2 * VO_BYTES;
   static constexpr int OFF_F = STAGE;
   static constexpr int OFF_W = OFF_F + (F_SMEM ? 2 * ZBOX : 0);
   static constexpr int OFF_F32 = OFF_W + 2 * W_BYTES;
   static_assert(HD == 64, "head dim (one 128-byte swizzle row per operand row)");
-  static_assert(4 * A_BYTES <= STAGE, "x and v pieces reuse the staging area");
   static_assert(CPT % 8 == 0, "whole 16-byte units of fp16 pieces per thread");
 };
 
-template <int RK, int HD, int P>
+template <int RK, int HD, int P, bool HALF = false>
 constexpr size_t head_umma_smem() {
-  using C = HeadUmmaCfg<HD, P>;
+  using C = HeadUmmaCfg<HD, P, HALF>;
   return 1024 /* alignment */ + C::OFF_F32 +
-         (size_t)(4 * HD + HD * RK + RK * HD + HD + C::PARTS * C::ROWS * RK) * 4 + 64;
+         (size_t)(4 * HD + HD * RK + RK * HD + HD + C::PARTS * C::RROWS * RK) * 4 + 64;
 }
 
 // fp16 pieces of 8 consecutive values as two 16-byte units (c0, c1); flags
@@ -122,11 +131,11 @@ GFN_DEV void tma_store_3d(const void* tmap, const void* src, int x, int y, int z
 // (128-byte swizzle; unused for a layer that starts from the carried state).
 // tmo: the split output rows catkh viewed as [2][B][3d] fp16 in [1][128][64]
 // boxes (128-byte swizzle); rows past B are clipped by the map.
-template <int RK, int HD, int P>
-__global__ void __launch_bounds__(HeadUmmaCfg<HD, P>::THREADS, HeadUmmaCfg<HD, P>::MIN_BLOCKS)
+template <int RK, int HD, int P, bool HALF = false>
+__global__ void __launch_bounds__(HeadUmmaCfg<HD, P, HALF>::THREADS, HeadUmmaCfg<HD, P, HALF>::MIN_BLOCKS)
     layered_head_umma_kernel(const __grid_constant__ CUtensorMap tmz, const __grid_constant__ CUtensorMap tmo,
                              const LayPreArgs a) {
-  using C = HeadUmmaCfg<HD, P>;
+  using C = HeadUmmaCfg<HD, P, HALF>;
   static_assert(RK % 4 == 0, "rank");
   constexpr int CPT = C::CPT;
   extern __shared__ __align__(1024) uint8_t hu_smem_raw[];
@@ -141,15 +150,18 @@ __global__ void __launch_bounds__(HeadUmmaCfg<HD, P>::THREADS, HeadUmmaCfg<HD, P
   float* sU = sBG + 4 * HD;                                // [HD][RK]
   float* sWg = sU + HD * RK;                               // [RK][HD]
   float* sbf = sWg + RK * HD;                              // [HD]
-  float* sP = sbf + HD;                                    // [PARTS][128][RK]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + C::PARTS * C::ROWS * RK);  // w, z, mma
+  float* sP = sbf + HD;                                    // [PARTS][RROWS][RK]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + C::PARTS * C::RROWS * RK);  // w, z, mma
   uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 3);
 
   const int d = a.d, B = a.B, h = blockIdx.y;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int q = warp & 3, part = warp >> 2;  // TMEM lane quarter, column part
-  const int r = 32 * q + lane;                 // row within the tile (= TMEM lane)
-  const int b0 = blockIdx.x * C::ROWS;
+  const int q = warp & 3;                      // TMEM lane quarter this warp reads
+  // row within the tile (TMEM lane 32 q + lane holds it, or its duplicate) and
+  // the column part; HALF: quarters 2-3 take the second 32 columns
+  const int r = HALF ? 32 * (q & 1) + lane : 32 * q + lane;
+  const int part = HALF ? (((q >> 1) << 2) | (warp >> 2)) : (warp >> 2);
+  const int b0 = blockIdx.x * C::RROWS;
   const int b = b0 + r;                        // batch row
   const bool live = b < B;
   const int c0 = part * CPT;                   // first head column of this thread
@@ -351,6 +363,11 @@ __global__ void __launch_bounds__(HeadUmmaCfg<HD, P>::THREADS, HeadUmmaCfg<HD, P
       const int aoff = umma_kmajor_off(r, c0 + 8 * u8, C::ROWB);
       *reinterpret_cast<uint4*>(sA + aoff) = p0;
       *reinterpret_cast<uint4*>(sA + C::A_BYTES + aoff) = p1;
+      if constexpr (HALF) {  // the duplicate MMA row r + 64
+        const int doff = umma_kmajor_off(r + 64, c0 + 8 * u8, C::ROWB);
+        *reinterpret_cast<uint4*>(sA + doff) = p0;
+        *reinterpret_cast<uint4*>(sA + C::A_BYTES + doff) = p1;
+      }
     }
     // generic-proxy writes -> visible to the tensor core's async proxy
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -368,7 +385,7 @@ __global__ void __launch_bounds__(HeadUmmaCfg<HD, P>::THREADS, HeadUmmaCfg<HD, P
           pp[k + 2] = fmaf(V[j], u.z, pp[k + 2]);
           pp[k + 3] = fmaf(V[j], u.w, pp[k + 3]);
         }
-      float* dst = sP + (part * C::ROWS + r) * RK;
+      float* dst = sP + (part * C::RROWS + r) * RK;
 #pragma unroll
       for (int k = 0; k < RK; k += 4)
         *reinterpret_cast<float4*>(dst + k) = make_float4(pp[k], pp[k + 1], pp[k + 2], pp[k + 3]);
@@ -399,7 +416,7 @@ __global__ void __launch_bounds__(HeadUmmaCfg<HD, P>::THREADS, HeadUmmaCfg<HD, P
     for (int pt = 0; pt < C::PARTS; ++pt)
 #pragma unroll
       for (int k = 0; k < RK; k += 4) {
-        const float4 pk = *reinterpret_cast<const float4*>(sP + (pt * C::ROWS + r) * RK + k);
+        const float4 pk = *reinterpret_cast<const float4*>(sP + (pt * C::RROWS + r) * RK + k);
         p[k] += pk.x; p[k + 1] += pk.y; p[k + 2] += pk.z; p[k + 3] += pk.w;
       }
     float ss = 0.f;
@@ -454,7 +471,7 @@ __global__ void __launch_bounds__(HeadUmmaCfg<HD, P>::THREADS, HeadUmmaCfg<HD, P
     split8(V + 8 * u8, p0, p1);
     const int aoff = umma_kmajor_off(r, c0 + 8 * u8, C::ROWB);
     *reinterpret_cast<uint4*>(sVo + aoff) = p0;
-    *reinterpret_cast<uint4*>(sVo + C::A_BYTES + aoff) = p1;
+    *reinterpret_cast<uint4*>(sVo + C::VO_BYTES + aoff) = p1;
   }
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
   __syncthreads();
@@ -463,9 +480,10 @@ __global__ void __launch_bounds__(HeadUmmaCfg<HD, P>::THREADS, HeadUmmaCfg<HD, P
 #pragma unroll
     for (int w = 0; w < 2; ++w) {
       const uint8_t* pc = w == 0 ? sA : sVo;
+      const int c1off = w == 0 ? C::A_BYTES : C::VO_BYTES;
       tma_store_3d(&tmo, pc, col, b0, w);                        // c0
       tma_store_3d(&tmo, pc, d + col, b0, w);                    // c0
-      tma_store_3d(&tmo, pc + C::A_BYTES, 2 * d + col, b0, w);   // c1
+      tma_store_3d(&tmo, pc + c1off, 2 * d + col, b0, w);        // c1
     }
     asm volatile("cp.async.bulk.commit_group;" ::: "memory");
     asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");  // smem read before exit
