@@ -31,24 +31,26 @@
 
 namespace gfn {
 
-template <int HD, int P, bool HALF = false>
+template <int HD, int P, int NDUP = 1>
 struct HeadUmmaCfg {
   // PARTS threads per row (one warp per TMEM lane quarter and column part).
-  // PARTS 8: 1024 threads, the force staged in shared memory, one CTA per SM;
-  // PARTS 4: 512 threads, the force in registers, two CTAs per SM.
-  // HALF: 64-row tiles, 512 threads, 8 columns per thread.  The gate's A
-  // operand holds the 64 rows twice (MMA rows r and r + 64, M = 128 keeps the
-  // one-row-per-TMEM-lane accumulator layout), so the warps of TMEM lane
-  // quarters 0-1 read columns 0-31 and those of quarters 2-3 columns 32-63 of
-  // the same rows: twice the tiles of 128-row tiles at the same work per
-  // thread as PARTS 8, without register spills.
-  static constexpr int ROWS = 128;                      // MMA rows
-  static constexpr int RROWS = HALF ? 64 : 128;         // batch rows per tile
-  static constexpr int PARTS = HALF ? 8 : P;            // threads (column parts) per row
-  static constexpr int THREADS = HALF ? 512 : 128 * P;
+  // NDUP 1, PARTS 8: 128-row tiles, 1024 threads, the force staged in shared
+  //   memory, one CTA per SM; PARTS 4: 512 threads, the force in registers,
+  //   two CTAs per SM.
+  // NDUP 2 / 4: 64- / 32-row tiles, 8 columns per thread (512 / 256 threads).
+  //   The gate's A operand holds the tile's rows NDUP times (MMA rows r,
+  //   r + RROWS, ...; M = 128 keeps the one-row-per-TMEM-lane accumulator
+  //   layout), and the warps of each group of 4 / NDUP lane quarters read the
+  //   next HD / NDUP columns of the same rows: more, shorter tiles at the same
+  //   work per thread, no register spills.
+  static constexpr int ROWS = 128;                          // MMA rows
+  static constexpr int RROWS = 128 / NDUP;                  // batch rows per tile
+  static constexpr int WPQ = NDUP == 1 ? P : HD / (8 * NDUP);  // warps per lane quarter
+  static constexpr int PARTS = NDUP == 1 ? P : NDUP * WPQ;  // threads (column parts) per row
+  static constexpr int THREADS = 128 * WPQ;
   static constexpr int CPT = HD / PARTS;
-  static constexpr bool F_SMEM = !HALF && P == 8;
-  static constexpr int MIN_BLOCKS = (HALF || P != 8) ? 2 : 1;
+  static constexpr bool F_SMEM = NDUP == 1 && P == 8;
+  static constexpr int MIN_BLOCKS = NDUP == 4 ? 3 : (NDUP == 2 || P != 8) ? 2 : 1;
   static constexpr int ROWB = HD * 2;             // bytes per fp16 operand row
   static constexpr int A_BYTES = ROWS * ROWB;     // one fp16 piece of x (or v)
   static constexpr int VO_BYTES = RROWS * ROWB;   // one fp16 piece of the v' output
@@ -57,7 +59,7 @@ struct HeadUmmaCfg {
   // shared memory (bytes):
   //   staging: z boxes [x lo | x hi | v lo | v hi]; then x pieces c0 | c1
   //            (the gate's A operand; x' is also the output) and v' pieces
-  //   the token's force, [128][HD] fp32 as two swizzled boxes (PARTS 8 only)
+  //   the token's force, [128][HD] fp32 as two swizzled boxes (F_SMEM only)
   //   W_f pieces w0 | w1; bias / gain of the previous layer [4][HD];
   //   U [HD][RK]; W^T [RK][HD]; b_f [HD]; p parts [PARTS][RROWS][RK]; barriers
   static constexpr int STAGE = (4 * ZBOX > 2 * A_BYTES + 2 * VO_BYTES) ? 4 * ZBOX : 2 * A_BYTES + 2 * VO_BYTES;
@@ -66,11 +68,12 @@ struct HeadUmmaCfg {
   static constexpr int OFF_F32 = OFF_W + 2 * W_BYTES;
   static_assert(HD == 64, "head dim (one 128-byte swizzle row per operand row)");
   static_assert(CPT % 8 == 0, "whole 16-byte units of fp16 pieces per thread");
+  static_assert(NDUP == 1 || NDUP == 2 || NDUP == 4, "row duplication");
 };
 
-template <int RK, int HD, int P, bool HALF = false>
+template <int RK, int HD, int P, int NDUP = 1>
 constexpr size_t head_umma_smem() {
-  using C = HeadUmmaCfg<HD, P, HALF>;
+  using C = HeadUmmaCfg<HD, P, NDUP>;
   return 1024 /* alignment */ + C::OFF_F32 +
          (size_t)(4 * HD + HD * RK + RK * HD + HD + C::PARTS * C::RROWS * RK) * 4 + 64;
 }
@@ -131,11 +134,11 @@ GFN_DEV void tma_store_3d(const void* tmap, const void* src, int x, int y, int z
 // (128-byte swizzle; unused for a layer that starts from the carried state).
 // tmo: the split output rows catkh viewed as [2][B][3d] fp16 in [1][128][64]
 // boxes (128-byte swizzle); rows past B are clipped by the map.
-template <int RK, int HD, int P, bool HALF = false>
-__global__ void __launch_bounds__(HeadUmmaCfg<HD, P, HALF>::THREADS, HeadUmmaCfg<HD, P, HALF>::MIN_BLOCKS)
+template <int RK, int HD, int P, int NDUP = 1>
+__global__ void __launch_bounds__(HeadUmmaCfg<HD, P, NDUP>::THREADS, HeadUmmaCfg<HD, P, NDUP>::MIN_BLOCKS)
     layered_head_umma_kernel(const __grid_constant__ CUtensorMap tmz, const __grid_constant__ CUtensorMap tmo,
                              const LayPreArgs a) {
-  using C = HeadUmmaCfg<HD, P, HALF>;
+  using C = HeadUmmaCfg<HD, P, NDUP>;
   static_assert(RK % 4 == 0, "rank");
   constexpr int CPT = C::CPT;
   extern __shared__ __align__(1024) uint8_t hu_smem_raw[];
@@ -157,10 +160,12 @@ __global__ void __launch_bounds__(HeadUmmaCfg<HD, P, HALF>::THREADS, HeadUmmaCfg
   const int d = a.d, B = a.B, h = blockIdx.y;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int q = warp & 3;                      // TMEM lane quarter this warp reads
-  // row within the tile (TMEM lane 32 q + lane holds it, or its duplicate) and
-  // the column part; HALF: quarters 2-3 take the second 32 columns
-  const int r = HALF ? 32 * (q & 1) + lane : 32 * q + lane;
-  const int part = HALF ? (((q >> 1) << 2) | (warp >> 2)) : (warp >> 2);
+  // row within the tile (TMEM lane 32 q + lane holds it, or a duplicate) and
+  // the column part: each group of 4 / NDUP quarters (one copy of the rows)
+  // takes the next HD / NDUP columns
+  constexpr int QPD = 4 / NDUP;  // lane quarters per copy of the rows
+  const int r = 32 * (q % QPD) + lane;
+  const int part = NDUP == 1 ? (warp >> 2) : (q / QPD) * C::WPQ + (warp >> 2);
   const int b0 = blockIdx.x * C::RROWS;
   const int b = b0 + r;                        // batch row
   const bool live = b < B;
@@ -363,8 +368,9 @@ __global__ void __launch_bounds__(HeadUmmaCfg<HD, P, HALF>::THREADS, HeadUmmaCfg
       const int aoff = umma_kmajor_off(r, c0 + 8 * u8, C::ROWB);
       *reinterpret_cast<uint4*>(sA + aoff) = p0;
       *reinterpret_cast<uint4*>(sA + C::A_BYTES + aoff) = p1;
-      if constexpr (HALF) {  // the duplicate MMA row r + 64
-        const int doff = umma_kmajor_off(r + 64, c0 + 8 * u8, C::ROWB);
+#pragma unroll
+      for (int k = 1; k < NDUP; ++k) {  // the duplicate MMA rows r + k RROWS
+        const int doff = umma_kmajor_off(r + k * C::RROWS, c0 + 8 * u8, C::ROWB);
         *reinterpret_cast<uint4*>(sA + doff) = p0;
         *reinterpret_cast<uint4*>(sA + C::A_BYTES + doff) = p1;
       }

@@ -213,39 +213,43 @@ int head_parts(int batch, int heads, int sms) {
   return (long long)((batch + 127) / 128) * heads >= sms ? 4 : 8;
 }
 
-// Rows per head-step tile: 64 (HeadUmmaCfg HALF: twice the tiles of 128-row
-// tiles, 8 columns per thread, no spills; measured faster at every C4 batch:
-// 4096 rows 76.3 -> 60.0 us, 512 rows 24.9 -> 17.1 us per launch) or 128.
-// GFN_LAY_HEAD_ROWS=64/128 overrides.
+// Rows per head-step tile: 64 (HeadUmmaCfg NDUP 2: twice the tiles of 128-row
+// tiles, 8 columns per thread, no spills; C4 at 4096 rows 76.3 -> 60.0 us per
+// launch), or 32 (NDUP 4) when 64-row tiles would leave SMs idle (512 rows:
+// step 0.76 -> 0.69 ms).  GFN_LAY_HEAD_ROWS=32/64/128 overrides.
 int head_rows(int batch, int heads, int sms) {
-  (void)batch; (void)heads; (void)sms;
-  if (const char* env = getenv("GFN_LAY_HEAD_ROWS")) return atoi(env) == 128 ? 128 : 64;
-  return 64;
+  if (const char* env = getenv("GFN_LAY_HEAD_ROWS")) {
+    const int v = atoi(env);
+    return v == 128 ? 128 : v == 32 ? 32 : 64;
+  }
+  return (long long)((batch + 63) / 64) * heads < sms ? 32 : 64;
 }
 
-template <int P, bool HALF>
+template <int P, int NDUP>
 void launch_head_umma_p(int rank, const CUtensorMap& tmz, const CUtensorMap& tmo, const LayPreArgs& a,
                         dim3 grid, cudaStream_t s) {
-  constexpr int T = HeadUmmaCfg<64, P, HALF>::THREADS;
+  constexpr int T = HeadUmmaCfg<64, P, NDUP>::THREADS;
   if (rank == 4)
-    launch_maybe_pdl(layered_head_umma_kernel<4, 64, P, HALF>, grid, dim3(T), head_umma_smem<4, 64, P, HALF>(), s,
+    launch_maybe_pdl(layered_head_umma_kernel<4, 64, P, NDUP>, grid, dim3(T), head_umma_smem<4, 64, P, NDUP>(), s,
                      tmz, tmo, a);
   else if (rank == 8)
-    launch_maybe_pdl(layered_head_umma_kernel<8, 64, P, HALF>, grid, dim3(T), head_umma_smem<8, 64, P, HALF>(), s,
+    launch_maybe_pdl(layered_head_umma_kernel<8, 64, P, NDUP>, grid, dim3(T), head_umma_smem<8, 64, P, NDUP>(), s,
                      tmz, tmo, a);
   else
-    launch_maybe_pdl(layered_head_umma_kernel<16, 64, P, HALF>, grid, dim3(T), head_umma_smem<16, 64, P, HALF>(),
+    launch_maybe_pdl(layered_head_umma_kernel<16, 64, P, NDUP>, grid, dim3(T), head_umma_smem<16, 64, P, NDUP>(),
                      s, tmz, tmo, a);
 }
 
 void launch_head_umma(int rank, const CUtensorMap& tmz, const CUtensorMap& tmo, const LayPreArgs& a,
                       dim3 grid, cudaStream_t s, int sms, int rows) {
-  if (rows == 64)
-    launch_head_umma_p<8, true>(rank, tmz, tmo, a, grid, s);
+  if (rows == 32)
+    launch_head_umma_p<8, 4>(rank, tmz, tmo, a, grid, s);
+  else if (rows == 64)
+    launch_head_umma_p<8, 2>(rank, tmz, tmo, a, grid, s);
   else if (head_parts(a.B, a.H, sms) == 4)
-    launch_head_umma_p<4, false>(rank, tmz, tmo, a, grid, s);
+    launch_head_umma_p<4, 1>(rank, tmz, tmo, a, grid, s);
   else
-    launch_head_umma_p<8, false>(rank, tmz, tmo, a, grid, s);
+    launch_head_umma_p<8, 1>(rank, tmz, tmo, a, grid, s);
 }
 
 // The split head-step output catkh as [2][B][3d] fp16 in [1][rows][64] boxes.
@@ -264,24 +268,25 @@ int make_z_map(CUtensorMap* m, const float* z, int batch, int dim, int rows) {
   return encode_map(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, z, 2, dims, str, box);
 }
 
-template <int P, bool HALF>
+template <int P, int NDUP>
 cudaError_t set_head_umma_smem_p() {
-  cudaError_t e = cudaFuncSetAttribute(layered_head_umma_kernel<4, 64, P, HALF>,
+  cudaError_t e = cudaFuncSetAttribute(layered_head_umma_kernel<4, 64, P, NDUP>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)head_umma_smem<4, 64, P, HALF>());
+                                       (int)head_umma_smem<4, 64, P, NDUP>());
   if (e == cudaSuccess)
-    e = cudaFuncSetAttribute(layered_head_umma_kernel<8, 64, P, HALF>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)head_umma_smem<8, 64, P, HALF>());
+    e = cudaFuncSetAttribute(layered_head_umma_kernel<8, 64, P, NDUP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)head_umma_smem<8, 64, P, NDUP>());
   if (e == cudaSuccess)
-    e = cudaFuncSetAttribute(layered_head_umma_kernel<16, 64, P, HALF>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)head_umma_smem<16, 64, P, HALF>());
+    e = cudaFuncSetAttribute(layered_head_umma_kernel<16, 64, P, NDUP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)head_umma_smem<16, 64, P, NDUP>());
   return e;
 }
 
 int set_head_umma_smem() {
-  cudaError_t e = set_head_umma_smem_p<8, false>();
-  if (e == cudaSuccess) e = set_head_umma_smem_p<4, false>();
-  if (e == cudaSuccess) e = set_head_umma_smem_p<8, true>();
+  cudaError_t e = set_head_umma_smem_p<8, 1>();
+  if (e == cudaSuccess) e = set_head_umma_smem_p<4, 1>();
+  if (e == cudaSuccess) e = set_head_umma_smem_p<8, 2>();
+  if (e == cudaSuccess) e = set_head_umma_smem_p<8, 4>();
   return e == cudaSuccess ? GFN_OK : cuda_status(e, "head step: shared memory attribute");
 }
 
