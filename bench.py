@@ -656,8 +656,8 @@ def layered_kernel_times(step, i0, state, steps, flush, dev):
 # capture each (dram__bytes_read.sum + dram__bytes_write.sum; the commands and
 # figures are in profiles/*.md).  Keyed by (config, kernel).
 TRAFFIC = {
-    ("c4", "head"): 49.90e6 + 12.88e6,  # profiles/head_umma_c4.md
-    ("c4", "mix"): 42.90e6 + 2.02e6,    # profiles/mix_umma_c4.md
+    ("c4", "head"): 49.87e6 + 6.98e6,  # profiles/head_umma_c4.md
+    ("c4", "mix"): 42.64e6 + 1.38e6,   # profiles/mix_umma_c4.md
 }
 
 
@@ -686,7 +686,7 @@ def roofline_entry(c, layered, achieved_gbs, hbm, bf16, peak_kind, fp32_tflops, 
                             "frac_of_bf16_peak": round(mix_tf / bf16, 4),
                             "tensor_pipe_tflops": round(3 * mix_tf, 1),
                             "traffic": TRAFFIC.get((c.get("name"), "mix"))},
-            "head_step": {"kernel": "layered_head_umma_kernel / layered_pre_kernel",
+            "head_step": {"kernel": "layered_head_umma_kernel (tcgen05 gate, 64-row tiles)",
                           "launch_us": round(ktime["head_us"], 2),
                           "algorithmic_bytes_per_launch": head_bytes, "achieved_gbs": round(head_gbs, 1),
                           "frac_of_hbm": round(head_gbs / hbm, 4),
