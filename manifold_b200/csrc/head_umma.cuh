@@ -97,6 +97,17 @@ GFN_DEV void split8(const float* c, uint4& u0, uint4& u1) {
   u1 = make_uint4(h1[0], h1[1], h1[2], h1[3]);
 }
 
+// 20 tanh(g / 20) from one fast exponential: tanh(y) = (e - 1) / (e + 1),
+// e = exp(2 y), saturated for |y| > 9 (where tanh rounds to +-1 in float32).
+// Absolute error ~1e-7 on the tanh (the subtraction near y = 0), i.e. ~2e-6
+// on Gamma and ~1e-7 on v after the kick's h scaling.
+GFN_DEV float soft_clamp20_fast(float g) {
+  const float y = g * 0.05f;
+  if (fabsf(y) > 9.f) return y > 0.f ? 20.f : -20.f;
+  const float e = __expf(2.f * y);
+  return 20.f * __fdividef(e - 1.f, e + 1.f);
+}
+
 // 16-byte shared-memory load the compiler may not hoist out of a loop or keep
 // across iterations (head weights are re-read where used instead of pinning
 // registers for them).
@@ -452,13 +463,13 @@ __global__ void __launch_bounds__(HeadUmmaCfg<HD, P, NDUP>::THREADS, HeadUmmaCfg
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         const int j = j4 + i;
-        const float gam = soft_clamp20(gm[i]);
+        const float gam = soft_clamp20_fast(gm[i]);
         // (v + h (F - Gamma)) / (1 + h * 5 sigmoid(gate)) with one division:
         // 1 + 5h sigmoid = (1 + e + 5h) / (1 + e), e = exp(-gate); e beyond
         // 1e30 means sigmoid = 0 in float32 (no friction; also keeps num * ope finite)
-        const float ope = 1.f + expf(-(g[j] * inv_s + bj[i]));
+        const float ope = 1.f + __expf(-(g[j] * inv_s + bj[i]));
         const float num = V[j] + hh * (F[j] - gam);
-        V[j] = ope > 1e30f ? num : (num * ope) / (ope + 5.f * hh);
+        V[j] = ope > 1e30f ? num : __fdividef(num * ope, ope + 5.f * hh);
       }
     }
     if (kick == 0) {
