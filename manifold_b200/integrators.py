@@ -1,5 +1,6 @@
 """Leapfrog (kick-drift-kick) integrator, mirror of
 gfn/integrators/symplectic/leapfrog.py on the B200 kernels."""
+import torch
 import torch.nn as nn
 
 from ._lib import GfnError, require_cuda
@@ -159,3 +160,101 @@ INTEGRATOR_CLASSES = {
     "rk4": RK4Integrator, "rk45": DormandPrinceIntegrator, "yoshida": YoshidaIntegrator,
     "forest_ruth": ForestRuthIntegrator, "omelyan": OmelyanIntegrator,
 }
+
+
+# ---------------------------------------------------------------- training form
+# The scheme arithmetic of the multi-scheme kernel on [B, H, hd] tensors with
+# torch's autograd: used by MLayer in training for the non-leapfrog
+# integrators (inference runs the kernel).
+
+def _accel_torch(x, v, F, U, W, Wf, bf, Wi, topology, R, r):
+    """a = F - C(v, x), C the Christoffel term in its combined form
+    (gfn/geometry/lowrank.py:100-131, gfn/geometry/toroidal.py:70-148)."""
+    feat = torch.cat([torch.sin(x), torch.cos(x)], -1) if topology == 1 else x
+    gate = torch.einsum("bhk,hjk->bhj", feat, Wf) + bf
+    if Wi is not None:
+        gate = gate + torch.einsum("bhk,hjk->bhj", F, Wi)
+    mu = torch.sigmoid(gate) * 5.0
+    if topology == 1:
+        th, ph = x[..., 0::2], x[..., 1::2]
+        vth, vph = v[..., 0::2], v[..., 1::2]
+        denom = R + r * torch.cos(th)
+        g0 = denom * torch.sin(th) / r * vph ** 2
+        g1 = 2.0 * (-(r * torch.sin(th)) / torch.clamp(denom, min=1e-6)) * vph * vth
+        g = torch.stack([g0, g1], -1).reshape(x.shape) * 0.05
+        return F - (g + mu * v)
+    p = torch.einsum("bhk,hkr->bhr", v, U)
+    s = 1.0 / (1.0 + torch.norm(p, dim=-1, keepdim=True) + 1e-6)
+    pre = torch.einsum("bhr,hkr->bhk", (p * p) * s, W)
+    return F - 20.0 * torch.tanh((pre + mu * v) / 20.0)
+
+
+def _wrap(x, topology):
+    return torch.remainder(x, 2.0 * 3.14159265359) if topology == 1 else x
+
+
+_CBRT2 = 2.0 ** (1.0 / 3.0)
+_FR_TH = 1.0 / (2.0 - _CBRT2)
+_SYMPLECTIC = {
+    "yoshida": ([_FR_TH / 2, (1 - _FR_TH) / 2, (1 - _FR_TH) / 2, _FR_TH / 2],
+                [_FR_TH, 1 - 2 * _FR_TH, _FR_TH, _FR_TH]),
+    "omelyan": ([0.1786178958448091, -0.06626458266981849,
+                 1.0 - 2.0 * (-0.06626458266981849 + 0.1786178958448091), -0.06626458266981849,
+                 0.1786178958448091],
+                [(1.0 + 2.0 * 0.2123418310626054) / 2.0, -0.2123418310626054, -0.2123418310626054,
+                 (1.0 + 2.0 * 0.2123418310626054) / 2.0, (1.0 + 2.0 * 0.2123418310626054) / 2.0]),
+}
+_SYMPLECTIC["forest_ruth"] = _SYMPLECTIC["yoshida"]
+_DP_A = [[1 / 5], [3 / 40, 9 / 40], [44 / 45, -56 / 15, 32 / 9],
+         [19372 / 6561, -25360 / 2187, 64448 / 6561, -212 / 729],
+         [9017 / 3168, -355 / 33, 46732 / 5247, 49 / 176, -5103 / 18656]]
+_DP_B = [35 / 384, 0, 500 / 1113, 125 / 192, -2187 / 6784, 11 / 84]
+
+
+def scheme_step_torch(scheme, x, v, F, U, W, Wf, bf, Wi, dt, topology=0, R=2.0, r=1.0):
+    """One step of `scheme` (gfn/integrators/**) with a differentiable dt [1, H, 1]."""
+    def acc(xx, vv):
+        return _accel_torch(xx, vv, F, U, W, Wf, bf, Wi, topology, R, r)
+
+    if scheme == "euler":
+        a = acc(x, v)
+        return _wrap(x + dt * v, topology), v + dt * a
+    if scheme == "heun":
+        dv1 = acc(x, v)
+        vp = v + dt * dv1
+        xp = _wrap(x + dt * v, topology)
+        dv2 = acc(xp, vp)
+        return _wrap(x + (dt / 2.0) * (v + vp), topology), v + (dt / 2.0) * (dv1 + dv2)
+    if scheme == "rk4":
+        hh = 0.5 * dt
+        dv1 = acc(x, v)
+        v2, x2 = v + hh * dv1, _wrap(x + hh * v, topology)
+        dv2 = acc(x2, v2)
+        v3, x3 = v + hh * dv2, _wrap(x + hh * v2, topology)
+        dv3 = acc(x3, v3)
+        v4, x4 = v + dt * dv3, _wrap(x + dt * v3, topology)
+        dv4 = acc(x4, v4)
+        return (_wrap(x + (dt / 6.0) * (v + 2 * v2 + 2 * v3 + v4), topology),
+                v + (dt / 6.0) * (dv1 + 2 * dv2 + 2 * dv3 + dv4))
+    if scheme == "verlet":
+        vh = v + 0.5 * dt * acc(x, v)
+        x = _wrap(x + dt * vh, topology)
+        return x, vh + 0.5 * dt * acc(x, vh)
+    if scheme in _SYMPLECTIC:
+        cs, ds = _SYMPLECTIC[scheme]
+        for c, dd in zip(cs, ds):
+            x = _wrap(x + c * dt * v, topology)
+            v = v + dd * dt * acc(x, v)
+        return x, v
+    if scheme in ("rk45", "dormand_prince"):
+        kx, kv = [v], [acc(x, v)]
+        for row in _DP_A:
+            sx = sum(a * kx[j] for j, a in enumerate(row))
+            sv = sum(a * kv[j] for j, a in enumerate(row))
+            xs, vs = _wrap(x + dt * sx, topology), v + dt * sv
+            kx.append(vs)
+            kv.append(acc(xs, vs))
+        sx = sum(b * kx[j] for j, b in enumerate(_DP_B) if b)
+        sv = sum(b * kv[j] for j, b in enumerate(_DP_B) if b)
+        return _wrap(x + dt * sx, topology), v + dt * sv
+    raise GfnError(f"scheme {scheme!r}")

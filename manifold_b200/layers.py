@@ -181,10 +181,11 @@ class MLayer(nn.Module):
         the RMSNorm)."""
         if self.training and torch.is_grad_enabled() and any(p.requires_grad for p in self.parameters()):
             ai = self.physics_config.get("active_inference", {})
-            if self.integrator_type != "leapfrog" or self.use_dynamic_time or ai.get("enabled", False):
-                raise GfnError("training is implemented for the leapfrog integrator without active "
-                               "curvature or dynamic time (call eval() or run under torch.no_grad() "
-                               "for inference)")
+            if self.use_dynamic_time or ai.get("enabled", False):
+                raise GfnError("training with active curvature or dynamic time is not implemented on "
+                               "this build (call eval() or run under torch.no_grad() for inference)")
+            if self.integrator_type != "leapfrog":
+                return self._generic_step_train_scheme(x, v, force, context)
             return self._generic_step_train(x, v, force, context)
         with torch.no_grad():
             return self._generic_step_nograd(x, v, force, context)
@@ -215,6 +216,33 @@ class MLayer(nn.Module):
             vo.append(vh)
         xc, vc = torch.cat(xo, -1), torch.cat(vo, -1)
         return self._mix(xc, vc, B, H)
+
+    def _generic_step_train_scheme(self, x, v, force, context):
+        """Differentiable layer step for the non-leapfrog integrators: the same
+        scheme arithmetic as the multi-scheme kernel (gfn/integrators/**), on
+        [B, H, hd] tensors for all heads at once through torch's autograd (the
+        inference path uses the kernel)."""
+        from .integrators import scheme_step_torch
+        B = x.shape[0]
+        H, hd = self.heads, self.head_dim
+        if self.use_recursive and context is not None:
+            force = force + self.context_proj(context)
+        ch = self.christoffels
+        Wf = torch.stack([c.forget_gate.weight for c in ch])
+        bf = torch.stack([c.forget_gate.bias for c in ch])
+        Wi = torch.stack([c.input_gate.weight for c in ch])
+        if self.topology_id == 0:
+            U = torch.stack([c.U for c in ch])
+            W = torch.stack([c.W for c in ch])
+            R = r = 1.0
+        else:
+            U = W = None
+            R, r = ch[0].R, ch[0].r
+        dts = torch.nn.functional.softplus(self.dt_params).view(1, H, 1)
+        scheme = self.integrator_type if self.integrator_type in ops.SCHEMES else "verlet"
+        xh, vh = scheme_step_torch(scheme, x.reshape(B, H, hd), v.reshape(B, H, hd), force.reshape(B, H, hd),
+                                   U, W, Wf, bf, Wi, self.base_dt * dts, self.topology_id, R, r)
+        return self._mix(xh.reshape(B, H * hd), vh.reshape(B, H * hd), B, H)
 
     def _mix(self, xc, vc, B, H):
         if H > 1:

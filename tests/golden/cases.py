@@ -65,6 +65,9 @@ GRAD_CASES = {
 GENERIC_GRAD_CASES = {
     "gtorus": dict(V=7, d=32, NL=2, H=2, rank=8, B=3, L=4, dt=0.1, seed=36, torus=True),
     "gtorus_h1": dict(V=5, d=16, NL=2, H=1, rank=4, B=2, L=3, dt=0.1, seed=37, torus=True),
+    "gheun": dict(V=7, d=32, NL=2, H=2, rank=8, B=3, L=4, dt=0.1, seed=38, integrator="heun"),
+    "grk4_torus": dict(V=7, d=32, NL=2, H=2, rank=8, B=2, L=3, dt=0.1, seed=39, integrator="rk4", torus=True),
+    "gomelyan": dict(V=7, d=32, NL=2, H=2, rank=8, B=2, L=3, dt=0.1, seed=40, integrator="omelyan"),
 }
 
 

@@ -155,9 +155,10 @@ def test_mlayer_step_gradients_flow():
 
 
 @pytest.mark.parametrize("name", list(C.GENERIC_GRAD_CASES))
-def test_generic_torus_backward_matches_reference_autograd(name):
-    """Training on the torus (the generic layer step with the leapfrog
-    autograd operator): gradients of forces, initial state, dt_params, the
+def test_generic_backward_matches_reference_autograd(name):
+    """Training on the generic layer step (the torus with the leapfrog
+    autograd operator; Heun, RK4, Omelyan through the scheme arithmetic with
+    autograd): gradients of forces, initial state, dt_params, U / W, the
     forget gates and the mixing against the reference's autograd."""
     cfg = C.GENERIC_GRAD_CASES[name]
     g = dict(np.load(os.path.join(GOLD, f"{name}.npz")))
@@ -173,8 +174,13 @@ def test_generic_torus_backward_matches_reference_autograd(name):
                f"l{l} Wf")
         gclose(torch.stack([c.forget_gate.bias.grad for c in layer.christoffels]).cpu(), g[f"l{l}_bf"],
                f"l{l} bf")
+        if f"l{l}_U" in g:
+            gclose(torch.stack([c.U.grad for c in layer.christoffels]).cpu(), g[f"l{l}_U"], f"l{l} U")
+            gclose(torch.stack([c.W.grad for c in layer.christoffels]).cpu(), g[f"l{l}_W"], f"l{l} W")
         if cfg["H"] > 1:
             for nm in ("x", "v"):
                 gclose(getattr(layer, "out_proj_" + nm).weight.grad.cpu(), g[f"l{l}_W{nm}"], f"l{l} W{nm}")
                 gclose(getattr(layer, "out_proj_" + nm).bias.grad.cpu(), g[f"l{l}_b{nm}"], f"l{l} b{nm}")
             gclose(layer.mixed_norm_v.weight.grad.cpu(), g[f"l{l}_gv"], f"l{l} gv")
+            if f"l{l}_gx" in g:
+                gclose(layer.mixed_norm_x.weight.grad.cpu(), g[f"l{l}_gx"], f"l{l} gx")

@@ -130,3 +130,32 @@ def test_oracle_generic_variants_match_reference(name):
                                               cfg.get("active"))
     close(xs, g["x_seq"], 1e-4, 1e-5)
     close(vs, g["v_seq"], 1e-4, 1e-5)
+
+
+@pytest.mark.parametrize("scheme", ["euler", "heun", "rk4", "verlet", "yoshida", "forest_ruth", "omelyan", "rk45"])
+@pytest.mark.parametrize("topology", [0, 1])
+def test_training_scheme_arithmetic_matches_oracle(scheme, topology):
+    """The differentiable [B, H, hd] scheme arithmetic the generic layer step
+    trains with equals the oracle's per-head integrator (float64, CPU)."""
+    import torch
+    from manifold_b200.integrators import scheme_step_torch
+    rng = np.random.default_rng(11)
+    B, H, hd, r = 3, 2, 8, 4
+    x = rng.uniform(0, 6, (B, H, hd)) if topology else rng.standard_normal((B, H, hd))
+    v = rng.standard_normal((B, H, hd))
+    F = rng.standard_normal((B, H, hd))
+    U = rng.standard_normal((H, hd, r)) * 0.3
+    W = rng.standard_normal((H, hd, r)) * 0.3
+    fin = 2 * hd if topology else hd
+    Wf = rng.standard_normal((H, hd, fin)) * 0.1
+    bf = rng.standard_normal((H, hd)) * 0.3
+    Wi = rng.standard_normal((H, hd, hd)) * 0.1
+    sc = np.array([0.9, 1.1])
+    T = torch.as_tensor
+    xt, vt = scheme_step_torch(scheme, T(x), T(v), T(F), None if topology else T(U), None if topology else T(W),
+                               T(Wf), T(bf), T(Wi), T(0.1 * sc).view(1, H, 1), topology)
+    for h in range(H):
+        xo, vo = O.integrator_step(scheme, x[:, h], v[:, h], F[:, h], None if topology else U[h],
+                                   None if topology else W[h], Wf[h], bf[h], Wi[h], 0.1, sc[h], 1, topology)
+        np.testing.assert_allclose(xt[:, h].numpy(), xo, rtol=1e-12, atol=1e-12)
+        np.testing.assert_allclose(vt[:, h].numpy(), vo, rtol=1e-12, atol=1e-12)
