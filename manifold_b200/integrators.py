@@ -167,26 +167,54 @@ INTEGRATOR_CLASSES = {
 # torch's autograd: used by MLayer in training for the non-leapfrog
 # integrators (inference runs the kernel).
 
-def _accel_torch(x, v, F, U, W, Wf, bf, Wi, topology, R, r):
-    """a = F - C(v, x), C the Christoffel term in its combined form
-    (gfn/geometry/lowrank.py:100-131, gfn/geometry/toroidal.py:70-148)."""
+def _active_factor_torch(x, v, act, topology):
+    """The active-inference multiplier of the Christoffel term
+    (gfn/geometry/reactive.py:62-81, gfn/geometry/toroidal.py:126-141)."""
+    m = 1.0
+    if act.get("plasticity", 0.0):
+        m = m * (1.0 + act["plasticity"] * torch.tanh((v * v).mean(-1, keepdim=True)))
+    if act.get("V") is not None:
+        feat = torch.cat([torch.sin(x), torch.cos(x)], -1) if topology == 1 else x
+        z = torch.einsum("bhk,hk->bh", feat, act["V"]).unsqueeze(-1)
+        if act.get("Vb") is not None:
+            z = z + act["Vb"].view(1, -1, 1)
+        pot = torch.sigmoid(z)
+        sg = (pot > act["thr"]).to(x.dtype) if topology == 1 else torch.sigmoid(10.0 * (pot - act["thr"]))
+        m = m * (1.0 + sg * (act["strength"] - 1.0))
+    return m
+
+
+def _torus_gamma_torch(x, v, R, r):
+    th, vth, vph = x[..., 0::2], v[..., 0::2], v[..., 1::2]
+    denom = R + r * torch.cos(th)
+    g0 = denom * torch.sin(th) / r * vph ** 2
+    g1 = 2.0 * (-(r * torch.sin(th)) / torch.clamp(denom, min=1e-6)) * vph * vth
+    return torch.stack([g0, g1], -1).reshape(x.shape) * 0.05
+
+
+def _lowrank_pre_torch(v, U, W):
+    p = torch.einsum("bhk,hkr->bhr", v, U)
+    s = 1.0 / (1.0 + torch.norm(p, dim=-1, keepdim=True) + 1e-6)
+    return torch.einsum("bhr,hkr->bhk", (p * p) * s, W)
+
+
+def _mu_torch(x, F, Wf, bf, Wi, topology):
     feat = torch.cat([torch.sin(x), torch.cos(x)], -1) if topology == 1 else x
     gate = torch.einsum("bhk,hjk->bhj", feat, Wf) + bf
     if Wi is not None:
         gate = gate + torch.einsum("bhk,hjk->bhj", F, Wi)
-    mu = torch.sigmoid(gate) * 5.0
+    return torch.sigmoid(gate) * 5.0
+
+
+def _accel_torch(x, v, F, U, W, Wf, bf, Wi, topology, R, r, act=None):
+    """a = F - C(v, x), C the Christoffel term in its combined form
+    (gfn/geometry/lowrank.py:100-131, gfn/geometry/toroidal.py:70-148)."""
+    mu = _mu_torch(x, F, Wf, bf, Wi, topology)
+    M = _active_factor_torch(x, v, act, topology) if act else 1.0
     if topology == 1:
-        th, ph = x[..., 0::2], x[..., 1::2]
-        vth, vph = v[..., 0::2], v[..., 1::2]
-        denom = R + r * torch.cos(th)
-        g0 = denom * torch.sin(th) / r * vph ** 2
-        g1 = 2.0 * (-(r * torch.sin(th)) / torch.clamp(denom, min=1e-6)) * vph * vth
-        g = torch.stack([g0, g1], -1).reshape(x.shape) * 0.05
-        return F - (g + mu * v)
-    p = torch.einsum("bhk,hkr->bhr", v, U)
-    s = 1.0 / (1.0 + torch.norm(p, dim=-1, keepdim=True) + 1e-6)
-    pre = torch.einsum("bhr,hkr->bhk", (p * p) * s, W)
-    return F - 20.0 * torch.tanh((pre + mu * v) / 20.0)
+        return F - (_torus_gamma_torch(x, v, R, r) * M + mu * v)
+    pre = _lowrank_pre_torch(v, U, W)
+    return F - 20.0 * torch.tanh((pre + mu * v) / 20.0) * M
 
 
 def _wrap(x, topology):
@@ -211,10 +239,25 @@ _DP_A = [[1 / 5], [3 / 40, 9 / 40], [44 / 45, -56 / 15, 32 / 9],
 _DP_B = [35 / 384, 0, 500 / 1113, 125 / 192, -2187 / 6784, 11 / 84]
 
 
-def scheme_step_torch(scheme, x, v, F, U, W, Wf, bf, Wi, dt, topology=0, R=2.0, r=1.0):
-    """One step of `scheme` (gfn/integrators/**) with a differentiable dt [1, H, 1]."""
+def scheme_step_torch(scheme, x, v, F, U, W, Wf, bf, Wi, dt, topology=0, R=2.0, r=1.0, act=None):
+    """One step of `scheme` (gfn/integrators/**) with a differentiable dt
+    ([1, H, 1] or per row [B, H, 1]); act: the active-inference terms."""
     def acc(xx, vv):
-        return _accel_torch(xx, vv, F, U, W, Wf, bf, Wi, topology, R, r)
+        return _accel_torch(xx, vv, F, U, W, Wf, bf, Wi, topology, R, r, act)
+
+    if scheme == "leapfrog":
+        # implicit friction, forget gate only (gfn/integrators/symplectic/leapfrog.py:50-114)
+        h = 0.5 * dt
+        for half in range(2):
+            mu = _mu_torch(x, F, Wf, bf, None, topology)
+            g = (_torus_gamma_torch(x, v, R, r) if topology == 1
+                 else 20.0 * torch.tanh(_lowrank_pre_torch(v, U, W) / 20.0))
+            if act:
+                g = g * _active_factor_torch(x, v, act, topology)
+            v = (v + h * (F - g)) / (1.0 + h * mu)
+            if half == 0:
+                x = _wrap(x + dt * v, topology)
+        return x, v
 
     if scheme == "euler":
         a = acc(x, v)

@@ -181,10 +181,9 @@ class MLayer(nn.Module):
         the RMSNorm)."""
         if self.training and torch.is_grad_enabled() and any(p.requires_grad for p in self.parameters()):
             ai = self.physics_config.get("active_inference", {})
-            if self.use_dynamic_time or ai.get("enabled", False):
-                raise GfnError("training with active curvature or dynamic time is not implemented on "
-                               "this build (call eval() or run under torch.no_grad() for inference)")
-            if self.integrator_type != "leapfrog":
+            if (self.integrator_type != "leapfrog" or self.use_dynamic_time
+                    or (ai.get("enabled", False) and (ai.get("reactive_curvature", {}).get("enabled", False)
+                                                      or ai.get("singularities", {}).get("enabled", False)))):
                 return self._generic_step_train_scheme(x, v, force, context)
             return self._generic_step_train(x, v, force, context)
         with torch.no_grad():
@@ -218,10 +217,10 @@ class MLayer(nn.Module):
         return self._mix(xc, vc, B, H)
 
     def _generic_step_train_scheme(self, x, v, force, context):
-        """Differentiable layer step for the non-leapfrog integrators: the same
-        scheme arithmetic as the multi-scheme kernel (gfn/integrators/**), on
-        [B, H, hd] tensors for all heads at once through torch's autograd (the
-        inference path uses the kernel)."""
+        """Differentiable layer step for the non-leapfrog integrators, dynamic
+        time and the active curvature terms: the same scheme arithmetic as the
+        multi-scheme kernel (gfn/integrators/**), on [B, H, hd] tensors for all
+        heads at once through torch's autograd (inference uses the kernel)."""
         from .integrators import scheme_step_torch
         B = x.shape[0]
         H, hd = self.heads, self.head_dim
@@ -239,10 +238,26 @@ class MLayer(nn.Module):
             U = W = None
             R, r = ch[0].R, ch[0].r
         dts = torch.nn.functional.softplus(self.dt_params).view(1, H, 1)
+        gates = None
+        if self.use_dynamic_time:
+            # dt scale per head and row (gfn/layers/base.py:219-229)
+            hv = x.view(B, H, hd)
+            gates = torch.stack([self.gatings[i](hv[:, i]) for i in range(H)], dim=0)  # [H, B, 1]
+            dts = dts.view(H, 1, 1) * gates                                           # [H, B, 1]
+            dts = dts.permute(1, 0, 2)                                                # [B, H, 1]
         scheme = self.integrator_type if self.integrator_type in ops.SCHEMES else "verlet"
+        plast, mode, V, Vb, thr, strength = self._active_terms()
+        act = None
+        if plast or mode:
+            act = dict(plasticity=plast, V=V, Vb=Vb, thr=thr, strength=strength)
+        leap = scheme == "leapfrog"
         xh, vh = scheme_step_torch(scheme, x.reshape(B, H, hd), v.reshape(B, H, hd), force.reshape(B, H, hd),
-                                   U, W, Wf, bf, Wi, self.base_dt * dts, self.topology_id, R, r)
-        return self._mix(xh.reshape(B, H * hd), vh.reshape(B, H * hd), B, H)
+                                   U, W, Wf, bf, None if leap else Wi, self.base_dt * dts, self.topology_id, R, r,
+                                   act)
+        xn, vn, ctx, _ = self._mix(xh.reshape(B, H * hd), vh.reshape(B, H * hd), B, H)
+        if gates is not None:
+            ctx = gates.squeeze(-1).t()
+        return xn, vn, ctx, []
 
     def _mix(self, xc, vc, B, H):
         if H > 1:

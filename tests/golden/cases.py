@@ -68,6 +68,13 @@ GENERIC_GRAD_CASES = {
     "gheun": dict(V=7, d=32, NL=2, H=2, rank=8, B=3, L=4, dt=0.1, seed=38, integrator="heun"),
     "grk4_torus": dict(V=7, d=32, NL=2, H=2, rank=8, B=2, L=3, dt=0.1, seed=39, integrator="rk4", torus=True),
     "gomelyan": dict(V=7, d=32, NL=2, H=2, rank=8, B=2, L=3, dt=0.1, seed=40, integrator="omelyan"),
+    "gai_heun": dict(V=7, d=32, NL=2, H=2, rank=8, B=3, L=3, dt=0.1, seed=56, integrator="heun",
+                     active={"enabled": True, "reactive_curvature": {"enabled": True, "plasticity": 0.5},
+                             "singularities": {"enabled": True, "threshold": 0.5, "strength": 3.0}}),
+    "gai_torus": dict(V=7, d=32, NL=2, H=2, rank=8, B=3, L=3, dt=0.1, seed=57, torus=True,
+                      active={"enabled": True, "reactive_curvature": {"enabled": True, "plasticity": 0.2}}),
+    "gdyn": dict(V=7, d=64, NL=2, H=4, rank=16, B=3, L=3, dt=0.1, seed=58,
+                 active={"dynamic_time": {"enabled": True}, "recursive_geodesics": {"enabled": True}}),
 }
 
 

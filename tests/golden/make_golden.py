@@ -283,6 +283,16 @@ def gen_grad_case(name, cfg):
                 gn = getattr(layer, "mixed_norm_" + nm).weight.grad
                 if gn is not None:  # the torus mixes x without the RMSNorm
                     out[f"l{l}_g{nm}"] = gn.numpy()
+        if cfg.get("active"):
+            gv = [c.V.weight.grad for c in layer.christoffels if getattr(c, "V", None) is not None]
+            if gv and gv[0] is not None:
+                out[f"l{l}_V"] = np.stack([t.numpy() for t in gv])
+            g0 = layer.gatings[0].curvature_net[0].weight.grad
+            if g0 is not None:
+                out[f"l{l}_gate_W1"] = np.stack([g.curvature_net[0].weight.grad.numpy() for g in layer.gatings])
+                out[f"l{l}_gate_b2"] = np.stack([g.curvature_net[2].bias.grad.numpy() for g in layer.gatings])
+            if getattr(layer, "context_proj", None) is not None and layer.context_proj.weight.grad is not None:
+                out[f"l{l}_ctx_W"] = layer.context_proj.weight.grad.numpy()
     np.savez_compressed(os.path.join(HERE, f"{name}.npz"), **out)
     print(name, len(out))
 

@@ -184,3 +184,12 @@ def test_generic_backward_matches_reference_autograd(name):
             gclose(layer.mixed_norm_v.weight.grad.cpu(), g[f"l{l}_gv"], f"l{l} gv")
             if f"l{l}_gx" in g:
                 gclose(layer.mixed_norm_x.weight.grad.cpu(), g[f"l{l}_gx"], f"l{l} gx")
+        if f"l{l}_V" in g:
+            gclose(torch.stack([c.V.weight.grad for c in layer.christoffels]).cpu(), g[f"l{l}_V"], f"l{l} V")
+        if f"l{l}_gate_W1" in g:
+            gclose(torch.stack([q.curvature_net[0].weight.grad for q in layer.gatings]).cpu(),
+                   g[f"l{l}_gate_W1"], f"l{l} gate W1")
+            gclose(torch.stack([q.curvature_net[2].bias.grad for q in layer.gatings]).cpu(),
+                   g[f"l{l}_gate_b2"], f"l{l} gate b2")
+        if f"l{l}_ctx_W" in g:
+            gclose(layer.context_proj.weight.grad.cpu(), g[f"l{l}_ctx_W"], f"l{l} context_proj")
