@@ -273,9 +273,12 @@ int gfn_leapfrog_pack_train(const float* U_stack, const float* W_stack,
                             const float* norm_v_w, int dim, int heads, int rank, int num_layers,
                             float* packed, long long packed_floats, gfn_stream_t stream);
 
-/* gfn_leapfrog_sequence_forward on the training pack that also stores every
- * layer step's input state: traj [2][num_layers][seq_len][batch][dim]
- * (x then v), the checkpoints the backward replays from. */
+/* gfn_leapfrog_sequence_forward on the training pack that also stores, for
+ * every layer step, what the backward replays from: traj holds
+ * [2][num_layers][seq_len][batch][dim] the step's input state (x then v),
+ * then [2][num_layers][seq_len][batch][dim] its head-mixing outputs z_x, z_v
+ * (bias included, before the RMSNorm), then [2][num_layers][seq_len][batch]
+ * its RMSNorm factors r_x, r_v: 4 L B d NL + 2 L B NL floats. */
 int gfn_leapfrog_sequence_forward_train(const float* x_init, const float* v_init,
                                         long long state_row_stride, const float* forces_f32,
                                         const void* forces_bf16, const long long* token_ids,

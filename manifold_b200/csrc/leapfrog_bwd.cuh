@@ -371,7 +371,9 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) leapfrog_bwd_kernel(const BwdA
       int slot = 0, l = NL - 1;
       uint32_t empty_phase = 0;
       bool first_lap = true;
-      const int nck = a.mix ? 2 * a.nchunk : 0;
+      // only the transposed mixing chunks: the forward's mixing outputs are
+      // stored, not recomputed
+      const int nck = a.mix ? a.nchunk : 0;
       for (long long g = 0; g < total_steps; ++g) {
         const int hslot = (int)(g & 1);
         if (g >= 2) mbar_wait(&head_empty[hslot], (uint32_t)(((g >> 1) - 1) & 1), kProducerSleepNs);
@@ -382,7 +384,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) leapfrog_bwd_kernel(const BwdA
           if (!first_lap) mbar_wait(&chunk_empty[slot], empty_phase, kProducerSleepNs);
           mbar_arrive_expect_tx(&chunk_full[slot], (uint32_t)a.CF * 4u);
           bulk_g2s(chunk_ring + (long long)slot * a.CF,
-                   my_pack + l * layer_stride + a.HST + (long long)i * a.CF, (uint32_t)a.CF * 4u,
+                   my_pack + l * layer_stride + a.HST + (long long)(a.nchunk + i) * a.CF, (uint32_t)a.CF * 4u,
                    &chunk_full[slot]);
           if (++slot == a.NST) {
             slot = 0;
@@ -523,37 +525,27 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) leapfrog_bwd_kernel(const BwdA
       }
 
       if (a.mix) {
-        // ---- E1: all-gather (x', v') blocks
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        named_sync<BWD_CT>();
-        if (tid < K && tid != (int)crank) {
-          const uint32_t off = (uint32_t)((int)crank * R * C);
-          const uint32_t rb = dsmem_addr(xch_bar, tid);
-          bulk_s2peer(dsmem_addr(catx + off, tid), catx + off, blk_bytes, rb);
-          bulk_s2peer(dsmem_addr(catv + off, tid), catv + off, blk_bytes, rb);
-        }
-        if (K > 1) mbar_wait(xch_bar, (uint32_t)(g & 1));
-        if (tid == 0 && K > 1) mbar_arrive_expect_tx(xch_bar, xch_bytes);
-        // ---- mixing recompute: pre-activations zx, zv of this CTA's columns
-        bwd_mix<BWD_CT>(a, catx, catv, ox, ov, hs + ho.bx, hs + ho.bv, chunk_ring, chunk_full,
-                        chunk_empty, cslot, cphase, tid, lane);
-        named_sync<BWD_CT>();
-        // ---- E2: sums of squares per row
-        for (int row = warp; row < R; row += BWD_NW) {
-          float sx = 0.f, sv = 0.f;
-          for (int j = lane; j < C; j += 32) {
-            const float u = ox[row * C + j], w = ov[row * C + j];
-            sx = fmaf(u, u, sx);
-            sv = fmaf(w, w, sv);
+        // ---- the forward's mixing outputs of this CTA's columns (stored by
+        // the training forward; no concat exchange, mixing recompute or
+        // sums-of-squares exchange)
+        const long long nlbd = (long long)NL * L * BD;
+#pragma unroll
+        for (int i = 0; i < BWD_MAXU; ++i) {
+          if (!uok[i]) continue;
+#pragma unroll
+          for (int e = 0; e < EPL; ++e) {
+            if (!eok[e]) continue;
+            const int col = uhl[i] * hd + jj[e];
+            float zx = 0.f, zv = 0.f;
+            if (valid(i, e)) {
+              const long long off = step_off + (long long)(row0 + urow[i]) * d + col0 + col;
+              zx = a.traj[2 * nlbd + off];
+              zv = a.traj[3 * nlbd + off];
+            }
+            ox[urow[i] * C + col] = zx;
+            ov[urow[i] * C + col] = zv;
           }
-          sx = warp_sum(sx);
-          sv = warp_sum(sv);
-          if (lane < K)
-            st_async2(dsmem_addr(part + ((int)crank * R + row) * 2, lane), sx, sv,
-                      dsmem_addr(part_bar, lane));
         }
-        mbar_wait(part_bar, (uint32_t)(g & 1));
-        if (tid == 0) mbar_arrive_expect_tx(part_bar, part_bytes);
         // ---- RMSNorm / saturation backward, first half
         float rxs[BWD_MAXU], rvs[BWD_MAXU], dyx[BWD_MAXU][EPL], dyv[BWD_MAXU][EPL];
 #pragma unroll
@@ -561,13 +553,12 @@ __global__ void __launch_bounds__(BWD_THREADS, 1) leapfrog_bwd_kernel(const BwdA
           rxs[i] = rvs[i] = 0.f;
           if (!uok[i]) continue;
           const int row = urow[i];
-          float ssx = 0.f, ssv = 0.f;
-          for (int c2 = 0; c2 < K; ++c2) {
-            ssx += part[(c2 * R + row) * 2];
-            ssv += part[(c2 * R + row) * 2 + 1];
+          float rx = 1.f, rv = 1.f;
+          if (row0 + row < B) {  // [2][NL][L][B] after the inputs and mixing outputs
+            const long long ro = 4 * nlbd + ((long long)l * L + t) * B + row0 + row;
+            rx = a.traj[ro];
+            rv = a.traj[ro + (long long)NL * L * B];
           }
-          const float rx = 1.f / sqrtf(ssx * inv_d + rms_eps);
-          const float rv = 1.f / sqrtf(ssv * inv_d + rms_eps);
           rxs[i] = rx;
           rvs[i] = rv;
 #pragma unroll

@@ -116,7 +116,9 @@ struct SeqArgs {
   float base_dt;
   int o_head, o_chunk, o_ox, o_ov, o_catx, o_catv, o_part;
   int chunk_base;   // offset of the first weight chunk in a (layer, CTA) pack run
-  float* traj;      // optional [2][NL][L][B][d]: every layer step's input (x, v), for BPTT
+  float* traj;      // optional, for BPTT: [2][NL][L][B][d] every layer step's input (x, v),
+                    // then [2][NL][L][B][d] its mixing outputs (z_x, z_v, bias included),
+                    // then [2][NL][L][B] its RMSNorm factors (r_x, r_v)
 };
 
 // ---------------------------------------------------------------- PTX bits
@@ -690,6 +692,27 @@ __global__ void __launch_bounds__(SeqShape<NW>::THREADS, SeqShape<NW>::MINB) lea
           }
           const float rx = 1.f / sqrtf(ssx * inv_d + rms_eps);
           const float rv = 1.f / sqrtf(ssv * inv_d + rms_eps);
+          if (a.traj) {  // the mixing outputs and RMSNorm factors, for the backward
+            const long long BD = (long long)a.B * d;
+            const long long nlb = (long long)a.NL * a.L;
+            const long long so = ((long long)l * a.L + t) * BD;
+            const int b = row0 + row;
+            if (b < a.B) {
+#pragma unroll
+              for (int e = 0; e < EPL; ++e) {
+                if (!eok[e]) continue;
+                const int col = uhl[i] * hd + jj[e];
+                const long long off = so + (long long)b * d + col0 + col;
+                a.traj[2 * nlb * BD + off] = ox[row * C + col];
+                a.traj[3 * nlb * BD + off] = ov[row * C + col];
+              }
+              if (crank == 0 && uhl[i] == 0 && lane == 0) {
+                const long long ro = 4 * nlb * BD + ((long long)l * a.L + t) * a.B + b;
+                a.traj[ro] = rx;
+                a.traj[ro + nlb * a.B] = rv;
+              }
+            }
+          }
 #pragma unroll
           for (int e = 0; e < EPL; ++e) {
             const int col = uhl[i] * hd + jj[e];

@@ -73,7 +73,10 @@ class LeapfrogSequenceTrain(torch.autograd.Function):
         v_seq = torch.empty_like(x_seq)
         xf = torch.empty(B, d, device=dev)
         vf = torch.empty_like(xf)
-        traj = torch.empty(2, NL, L, B, d, device=dev)
+        # layer-step inputs (x, v), the mixing outputs (z_x, z_v) and the RMSNorm
+        # factors (r_x, r_v) of every layer step, for the backward
+        S = NL * L * B * d
+        traj = torch.empty(4 * S + 2 * NL * L * B, device=dev)
         e0 = _mark("fwd", stream)
         call("gfn_leapfrog_sequence_forward_train", ptr(x0c), ptr(v0c), d, ptr(fl32), ptr(fbf), None,
              None, 0, ptr(m), ptr(packed), packed.numel(), B, L, d, H, r, NL, float(base_dt),
@@ -131,8 +134,8 @@ def param_grads(ws, traj, stacks, B, L, d, H, r, NL, base_dt):
     small = ws[NSIG * S: NSIG * S + NSMALL * M].view(NSMALL, NL, N, H, r)
     q1, q2, dp1, dp2 = small.unbind(0)
     deff = ws[NSIG * S + NSMALL * M: NSIG * S + NSMALL * M + NL * N * H].view(NL, N, H)
-    xin = traj[0].reshape(NL, N, d)
-    vin = traj[1].reshape(NL, N, d)
+    xin = traj[:S].view(NL, N, d)
+    vin = traj[S:2 * S].view(NL, N, d)
     hv = lambda t: t.view(NL, N, H, hd)
     dWf = torch.einsum("lnhj,lnhk->lhjk", hv(dz1), hv(xin)) + torch.einsum("lnhj,lnhk->lhjk", hv(dz2), hv(x2))
     dbf = (hv(dz1) + hv(dz2)).sum(1)
