@@ -157,7 +157,7 @@ class MLayer(nn.Module):
         B = x.shape[0]
         if force is None:
             force = torch.zeros_like(x)
-        if self.generic:
+        if self.generic or (self.training_generic() and self.training and torch.is_grad_enabled()):
             return self._generic_step(x, v, force, context)
         if torch.is_grad_enabled() and any(t.requires_grad for t in
                                            [x, v, force, *self.parameters()]):
@@ -172,6 +172,11 @@ class MLayer(nn.Module):
         context_next = torch.ones(B, self.heads, device=x.device, dtype=x.dtype)
         return xn, vn, context_next, []
 
+    def training_generic(self):
+        """True when training takes the generic layer step: the generic
+        configurations, and head dims above the fused BPTT kernels' 64 (the
+        per-head leapfrog autograd operator takes up to 256)."""
+        return self.generic or self.head_dim > 64
 
     def _generic_step(self, x, v, force, context=None):
         """One layer step for the torus and the non-leapfrog integrators:

@@ -215,11 +215,17 @@ class Manifold(nn.Module):
             x_final = cur if self.holographic else self.readout_norm(cur)
             logits = self.readout(x_final)
             return logits, (x_final[:, -1], None), []
-        if torch.is_grad_enabled() and any(p.requires_grad for p in self.parameters()) \
-                and not self.layers[0].generic:
+        train = torch.is_grad_enabled() and any(p.requires_grad for p in self.parameters())
+        if train and not self.layers[0].training_generic():
             from .training import manifold_train_forward
             return manifold_train_forward(self, input_ids, attention_mask, state, force_manual)
-        x_seq, v_seq, (x, v), forces = self.recurrence(input_ids, attention_mask, state, force_manual)
+        if train and self.training and not self.layers[0].generic:
+            # head dims beyond the fused BPTT kernels: the generic (layer by
+            # layer, per-head autograd) path
+            x_seq, v_seq, (x, v), forces = self._generic_recurrence(input_ids, attention_mask, state,
+                                                                    force_manual, True)
+        else:
+            x_seq, v_seq, (x, v), forces = self.recurrence(input_ids, attention_mask, state, force_manual)
         if forces is None and self.return_forces:
             forces = self.embedding(input_ids)
         out = x_seq if self.holographic else self.readout_norm(x_seq)

@@ -73,6 +73,7 @@ GENERIC_GRAD_CASES = {
                              "singularities": {"enabled": True, "threshold": 0.5, "strength": 3.0}}),
     "gai_torus": dict(V=7, d=32, NL=2, H=2, rank=8, B=3, L=3, dt=0.1, seed=57, torus=True,
                       active={"enabled": True, "reactive_curvature": {"enabled": True, "plasticity": 0.2}}),
+    "ghd128": dict(V=7, d=256, NL=2, H=2, rank=8, B=2, L=3, dt=0.1, seed=59),
     "gdyn": dict(V=7, d=64, NL=2, H=4, rank=16, B=3, L=3, dt=0.1, seed=58,
                  active={"dynamic_time": {"enabled": True}, "recursive_geodesics": {"enabled": True}}),
 }

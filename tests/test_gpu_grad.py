@@ -164,7 +164,7 @@ def test_generic_backward_matches_reference_autograd(name):
     g = dict(np.load(os.path.join(GOLD, f"{name}.npz")))
     P = C.make_params(cfg)
     m, F = run_grad(cfg, P, g["ids"], g["Gx"], g["Gv"], g["gxf"], g["gvf"])
-    assert m.layers[0].generic
+    assert m.layers[0].training_generic()
     gclose(F.grad.cpu(), g["g_forces"], "forces")
     gclose(m.x0.grad.cpu()[0], g["g_x0"], "x0")
     gclose(m.v0.grad.cpu()[0], g["g_v0"], "v0")
