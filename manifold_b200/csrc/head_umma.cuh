@@ -87,25 +87,18 @@ GFN_DEV void split8(const float* c, uint4& u0, uint4& u1) {
   for (int i = 0; i < 4; ++i) {
     const float a = c[2 * i], b = c[2 * i + 1];
     bad |= !(fabsf(a) < 32768.f) || !(fabsf(b) < 32768.f);
-    const __half a0 = __float2half_rn(a), b0 = __float2half_rn(b);
-    const __half a1 = __float2half_rn(a - __half2float(a0)), b1 = __float2half_rn(b - __half2float(b0));
-    h0[i] = (unsigned)__half_as_ushort(a0) | ((unsigned)__half_as_ushort(b0) << 16);
-    h1[i] = (unsigned)__half_as_ushort(a1) | ((unsigned)__half_as_ushort(b1) << 16);
+    // packed pair conversions (one f32x2 -> f16x2 round, one f16x2 -> f32x2
+    // widen): the same round-to-nearest pieces as per-value conversions, off
+    // the special-function pipe the transcendentals use
+    const __half2 p0 = __floats2half2_rn(a, b);
+    const float2 r0 = __half22float2(p0);
+    const __half2 p1 = __floats2half2_rn(a - r0.x, b - r0.y);
+    h0[i] = *reinterpret_cast<const unsigned*>(&p0);
+    h1[i] = *reinterpret_cast<const unsigned*>(&p1);
   }
   if (bad) gfn_flag_error(kDevErrF16Range);
   u0 = make_uint4(h0[0], h0[1], h0[2], h0[3]);
   u1 = make_uint4(h1[0], h1[1], h1[2], h1[3]);
-}
-
-// 20 tanh(g / 20) from one fast exponential: tanh(y) = (e - 1) / (e + 1),
-// e = exp(2 y), saturated for |y| > 9 (where tanh rounds to +-1 in float32).
-// Absolute error ~1e-7 on the tanh (the subtraction near y = 0), i.e. ~2e-6
-// on Gamma and ~1e-7 on v after the kick's h scaling.
-GFN_DEV float soft_clamp20_fast(float g) {
-  const float y = g * 0.05f;
-  if (fabsf(y) > 9.f) return y > 0.f ? 20.f : -20.f;
-  const float e = __expf(2.f * y);
-  return 20.f * __fdividef(e - 1.f, e + 1.f);
 }
 
 // 16-byte shared-memory load the compiler may not hoist out of a loop or keep
@@ -463,13 +456,19 @@ __global__ void __launch_bounds__(HeadUmmaCfg<HD, P, NDUP>::THREADS, HeadUmmaCfg
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         const int j = j4 + i;
-        const float gam = soft_clamp20_fast(gm[i]);
-        // (v + h (F - Gamma)) / (1 + h * 5 sigmoid(gate)) with one division:
-        // 1 + 5h sigmoid = (1 + e + 5h) / (1 + e), e = exp(-gate); e beyond
-        // 1e30 means sigmoid = 0 in float32 (no friction; also keeps num * ope finite)
-        const float ope = 1.f + __expf(-(g[j] * inv_s + bj[i]));
+        // Gamma = 20 tanh(y) = 20 (et - 1) / (et + 1), et = exp(2y), y = gm / 20
+        // clamped to +-9 (tanh(9) rounds to 1 in float32);
+        // v' = (v + h (F - Gamma)) / (1 + h * 5 sigmoid(gate))
+        //    = num * ope / (ope + 5h), ope = 1 + exp(-gate), the exponent
+        // clamped to 60 (sigmoid < 1e-26: no friction in float32).  Both
+        // quotients share one reciprocal of dt * df (both >= 1, product < 1e35).
+        const float et = __expf(fminf(fmaxf(gm[i] * 0.1f, -18.f), 18.f));
+        const float ope = 1.f + __expf(fminf(-(g[j] * inv_s + bj[i]), 60.f));
+        const float dt = et + 1.f, df = ope + 5.f * hh;
+        const float rr = __fdividef(1.f, dt * df);
+        const float gam = 20.f * (et - 1.f) * (df * rr);
         const float num = V[j] + hh * (F[j] - gam);
-        V[j] = ope > 1e30f ? num : __fdividef(num * ope, ope + 5.f * hh);
+        V[j] = num * ope * (dt * rr);
       }
     }
     if (kick == 0) {
