@@ -655,8 +655,8 @@ def layered_kernel_times(step, i0, state, steps, flush, dev):
 # capture each (dram__bytes_read.sum + dram__bytes_write.sum; the commands and
 # figures are in profiles/*.md).  Keyed by (config, kernel).
 TRAFFIC = {
-    ("c4", "head"): 49.87e6 + 6.98e6,  # profiles/head_umma_c4.md
-    ("c4", "mix"): 42.64e6 + 1.38e6,   # profiles/mix_umma_c4.md
+    ("c4", "head"): 49.88e6 + 8.12e6,  # profiles/head_umma_c4.md
+    ("c4", "mix"): 42.57e6 + 0.64e6,   # profiles/mix_umma_c4.md
 }
 
 
