@@ -191,7 +191,9 @@ def run_train(args, c):
     B, T, V = c["B"], args.chunk or c["chunk"], c["V"]
     steps, warm = args.steps, args.warmup
     host = [torch.from_numpy(make_ids(c, B, T + 1, 100 * rank + i)).pin_memory() for i in range(steps + warm)]
-    ce = torch.nn.CrossEntropyLoss()
+    # the library's loss kernels (one read of the logits forward, one read and
+    # one write backward) for the reference loop's nn.CrossEntropyLoss()
+    ce = gfn.CrossEntropyLoss()
     stream = torch.cuda.current_stream(dev)
     flush = torch.empty(256 * 1024 * 1024 // 4, device=dev, dtype=torch.float32)
 

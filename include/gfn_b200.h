@@ -480,6 +480,30 @@ int gfn_functional_embedding(const long long* ids, long long n, const float* W0,
                              const float* Wo, const float* bo, const float* impulse, float omega0,
                              int dim, float* out_f32, void* out_bf16, gfn_stream_t stream);
 
+/* ------------------------------------------------------------------------
+ * Next-token cross-entropy over the readout's logits: the loss of the
+ * reference's training loops, nn.CrossEntropyLoss() on logits.view(-1, V)
+ * (demos/wikitext/train_wikitext.py:162,185; ignore_index as in
+ * demos/copy_task/train_copy_task.py:175), computed on fp32 logits [rows][V]
+ * with int64 targets [rows].
+ *
+ * Forward: row_loss[r] = logsumexp(logits[r]) - logits[r][t_r] (0 where
+ * t_r == ignore_index) and row_stats[r] = (m_r, log sum_j exp(logits[r][j] -
+ * m_r)), m_r the row maximum: two floats per row, 8-byte aligned, kept apart
+ * so large logits lose no precision to their sum.  The mean loss
+ * is sum(row_loss) / (number of rows not ignored), summed by the caller.  A
+ * target outside [0, V) that is not ignore_index sets GFN_DEVERR_BAD_TOKEN
+ * and a NaN row loss.
+ * Backward: grad_logits[r][j] = (softmax(logits[r])[j] - [j == t_r])
+ * * grad_scale[0] (zero rows where t_r is ignored or out of range);
+ * grad_scale is ONE float in device memory (dL/dloss / rows not ignored), so
+ * no host sync is needed.  grad_logits may alias logits.  rows < 2^31. */
+int gfn_cross_entropy_forward(const float* logits, const long long* targets, long long rows, int V,
+                              long long ignore_index, float* row_loss, float* row_stats, gfn_stream_t stream);
+int gfn_cross_entropy_backward(const float* logits, const long long* targets, const float* row_stats,
+                               long long rows, int V, long long ignore_index, const float* grad_scale,
+                               float* grad_logits, gfn_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -18,9 +18,10 @@ from .integrators import (DormandPrinceIntegrator, EulerIntegrator, ForestRuthIn
 from .integrators import INTEGRATOR_CLASSES as INTEGRATORS
 from .embeddings import FunctionalEmbedding, ImplicitEmbedding, SineLayer
 from .scan import parallel_scan
+from .losses import CrossEntropyLoss, cross_entropy
 from . import cuda
 
-__all__ = ["GFN", "Manifold", "GLayer", "MLayer", "ParallelMLayer", "RiemannianGating",
+__all__ = ["CrossEntropyLoss", "cross_entropy", "GFN", "Manifold", "GLayer", "MLayer", "ParallelMLayer", "RiemannianGating",
            "LowRankChristoffel", "ReactiveChristoffel", "ToroidalChristoffel", "LeapfrogIntegrator",
            "EulerIntegrator", "HeunIntegrator", "RK4Integrator", "DormandPrinceIntegrator",
            "SymplecticIntegrator", "VerletIntegrator", "YoshidaIntegrator", "ForestRuthIntegrator",

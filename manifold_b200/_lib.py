@@ -55,6 +55,8 @@ _SIGS = {
                                      _i, _i, _f, _p, _p, _p, _p, _p, _ll, _p],
     "gfn_split_f16": [_p, _ll, _ll, _i, _i, _p, _p, _p],
     "gfn_gemm_split_f16_tc": [_i, _i, _i, _p, _p, _p, _p, _p, _p, _p, _p],
+    "gfn_cross_entropy_forward": [_p, _p, _ll, _i, _ll, _p, _p, _p],
+    "gfn_cross_entropy_backward": [_p, _p, _p, _ll, _i, _ll, _p, _p, _p],
     "gfn_gemm_split_f16": [_i, _i, _i, _p, _i, _p, _i, _p, _p, _f, _p, _p, _p],
     "gfn_parallel_scan": [_p, _p, _p, _p, _ll, _i, _i, _i, _p],
     "gfn_parallel_scan_noalloc": [_p, _p, _p, _i, _i, _i, _p],

@@ -178,3 +178,177 @@ int gfn_gemm_split_f16(int M, int N, int K, const void* a2, int a_k_rows, const 
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Next-token cross-entropy over the readout's logits, the loss of the
+// reference's training loops (nn.CrossEntropyLoss() on logits.view(-1, V),
+// demos/wikitext/train_wikitext.py:162,185; ignore_index as in
+// demos/copy_task/train_copy_task.py:175).  One CTA per row, both passes
+// HBM-bound streams of float4:
+//   forward   one read of the row: online (max m, sum exp(x - m)) per thread,
+//             merged across the CTA; the row keeps (m, ls = log(sum)) apart
+//             (their sum rounds at the ulp of m, too coarse for large logits);
+//             loss = (m - x[t]) + ls;
+//   backward  one read, one write: g = (exp((x - m) - ls) - [j == t]) * scale,
+//             scale = dL/dloss / (number of rows not ignored), read from
+//             device memory so the upstream gradient needs no host sync.
+namespace {
+
+constexpr int XENT_THREADS = 256;
+
+// (max, sum of exp(x - max)) pairs merged; an empty side has max = -inf.
+GFN_DEV void lse_merge(float& m, float& s, float m2, float s2) {
+  const float mn = fmaxf(m, m2);
+  if (mn == -INFINITY) return;
+  s = s * expf(m - mn) + s2 * expf(m2 - mn);
+  m = mn;
+}
+
+GFN_DEV void lse_add4(float& m, float& s, float4 v) {
+  const float c = fmaxf(fmaxf(v.x, v.y), fmaxf(v.z, v.w));
+  if (c > m) {
+    s = (m == -INFINITY) ? 0.f : s * expf(m - c);
+    m = c;
+  }
+  if (m == -INFINITY) return;  // all -inf so far: nothing to add
+  s += expf(v.x - m) + expf(v.y - m) + expf(v.z - m) + expf(v.w - m);
+}
+
+template <bool VEC>
+__global__ void __launch_bounds__(XENT_THREADS) xent_forward_kernel(const float* __restrict__ logits,
+                                                                   const long long* __restrict__ tgt,
+                                                                   int V, long long ignore,
+                                                                   float* __restrict__ row_loss,
+                                                                   float2* __restrict__ row_stats) {
+  const long long row = blockIdx.x;
+  const float* x = logits + row * (long long)V;
+  float m = -INFINITY, s = 0.f;
+  if (VEC) {
+    const float4* x4 = reinterpret_cast<const float4*>(x);
+    for (int i = threadIdx.x; i < V / 4; i += XENT_THREADS) lse_add4(m, s, __ldcs(x4 + i));
+  } else {
+    for (int i = threadIdx.x; i < V; i += XENT_THREADS) {
+      const float v = x[i];
+      if (v > m) {
+        s = (m == -INFINITY) ? 0.f : s * expf(m - v);
+        m = v;
+      }
+      if (m != -INFINITY) s += expf(v - m);
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float m2 = __shfl_xor_sync(0xffffffffu, m, o), s2 = __shfl_xor_sync(0xffffffffu, s, o);
+    lse_merge(m, s, m2, s2);
+  }
+  __shared__ float sm[XENT_THREADS / 32], ss[XENT_THREADS / 32];
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) { sm[w] = m; ss[w] = s; }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int k = 1; k < XENT_THREADS / 32; ++k) lse_merge(m, s, sm[k], ss[k]);
+    const float ls = logf(s);
+    const long long t = tgt[row];
+    float loss = 0.f;
+    if (t != ignore) {
+      if (t < 0 || t >= V) {
+        gfn_flag_error(kDevErrBadToken);
+        loss = __int_as_float(0x7fc00000);  // NaN: the row has no valid target
+      } else {
+        loss = (m - x[t]) + ls;
+      }
+    }
+    row_loss[row] = loss;
+    row_stats[row] = make_float2(m, ls);
+  }
+}
+
+template <bool VEC>
+__global__ void __launch_bounds__(XENT_THREADS) xent_backward_kernel(const float* logits,
+                                                                    const long long* __restrict__ tgt,
+                                                                    const float2* __restrict__ row_stats,
+                                                                    int V, long long ignore,
+                                                                    const float* __restrict__ scale_p,
+                                                                    float* grad) {
+  // logits and grad may be the same buffer: every element is read, then
+  // written, by one thread
+  const long long row = blockIdx.x;
+  const float* x = logits + row * (long long)V;
+  float* g = grad + row * (long long)V;
+  const long long t = tgt[row];
+  const bool skip = (t == ignore) || t < 0 || t >= V;
+  const float scale = skip ? 0.f : *scale_p;
+  const float2 st = row_stats[row];
+  const float m = st.x, ls = st.y;
+  if (VEC) {
+    const float4* x4 = reinterpret_cast<const float4*>(x);
+    float4* g4 = reinterpret_cast<float4*>(g);
+    for (int i = threadIdx.x; i < V / 4; i += XENT_THREADS) {
+      const float4 v = __ldcs(x4 + i);
+      float4 o;
+      o.x = skip ? 0.f : expf((v.x - m) - ls) * scale;
+      o.y = skip ? 0.f : expf((v.y - m) - ls) * scale;
+      o.z = skip ? 0.f : expf((v.z - m) - ls) * scale;
+      o.w = skip ? 0.f : expf((v.w - m) - ls) * scale;
+      if (!skip && t >= 4LL * i && t < 4LL * i + 4) {
+        const int k = (int)(t - 4LL * i);
+        if (k == 0) o.x -= scale; else if (k == 1) o.y -= scale; else if (k == 2) o.z -= scale; else o.w -= scale;
+      }
+      __stcs(g4 + i, o);
+    }
+  } else {
+    for (int i = threadIdx.x; i < V; i += XENT_THREADS) {
+      float o = skip ? 0.f : expf((x[i] - m) - ls) * scale;
+      if (!skip && i == t) o -= scale;
+      g[i] = o;
+    }
+  }
+}
+
+bool xent_vec(const void* a, const void* b, int V) {
+  return V % 4 == 0 && ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(b)) & 15u) == 0;
+}
+
+}  // namespace
+
+extern "C" {
+
+int gfn_cross_entropy_forward(const float* logits, const long long* targets, long long rows, int V,
+                              long long ignore_index, float* row_loss, float* row_stats, gfn_stream_t stream) {
+  if (rows < 0 || V <= 0 || (rows > 0 && (!logits || !targets || !row_loss || !row_stats)))
+    return fail(GFN_ERR_INVALID, "cross_entropy_forward: bad arguments");
+  if (rows > 0x7fffffffLL) return fail(GFN_ERR_INVALID, "cross_entropy_forward: rows > 2^31 - 1");
+  if (rows == 0) return GFN_OK;
+  if (reinterpret_cast<uintptr_t>(row_stats) & 7u)
+    return fail(GFN_ERR_ALIGN, "cross_entropy_forward: row_stats must be 8-byte aligned");
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  float2* st = reinterpret_cast<float2*>(row_stats);
+  if (xent_vec(logits, logits, V))
+    xent_forward_kernel<true><<<(unsigned)rows, XENT_THREADS, 0, s>>>(logits, targets, V, ignore_index, row_loss, st);
+  else
+    xent_forward_kernel<false><<<(unsigned)rows, XENT_THREADS, 0, s>>>(logits, targets, V, ignore_index, row_loss, st);
+  return launch_status("cross_entropy_forward");
+}
+
+int gfn_cross_entropy_backward(const float* logits, const long long* targets, const float* row_stats,
+                               long long rows, int V, long long ignore_index, const float* grad_scale,
+                               float* grad_logits, gfn_stream_t stream) {
+  if (rows < 0 || V <= 0 ||
+      (rows > 0 && (!logits || !targets || !row_stats || !grad_scale || !grad_logits)))
+    return fail(GFN_ERR_INVALID, "cross_entropy_backward: bad arguments");
+  if (rows > 0x7fffffffLL) return fail(GFN_ERR_INVALID, "cross_entropy_backward: rows > 2^31 - 1");
+  if (rows == 0) return GFN_OK;
+  if (reinterpret_cast<uintptr_t>(row_stats) & 7u)
+    return fail(GFN_ERR_ALIGN, "cross_entropy_backward: row_stats must be 8-byte aligned");
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const float2* st = reinterpret_cast<const float2*>(row_stats);
+  if (xent_vec(logits, grad_logits, V))
+    xent_backward_kernel<true><<<(unsigned)rows, XENT_THREADS, 0, s>>>(logits, targets, st, V, ignore_index,
+                                                                       grad_scale, grad_logits);
+  else
+    xent_backward_kernel<false><<<(unsigned)rows, XENT_THREADS, 0, s>>>(logits, targets, st, V, ignore_index,
+                                                                        grad_scale, grad_logits);
+  return launch_status("cross_entropy_backward");
+}
+
+}  // extern "C"

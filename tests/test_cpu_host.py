@@ -99,3 +99,13 @@ def test_no_cpu_fallback():
         gfn.parallel_scan(torch.ones(1, 4, 4), torch.ones(1, 4, 4))
     with pytest.raises(gfn.GfnError):
         m.layers[0](torch.zeros(1, 32), torch.zeros(1, 32), torch.zeros(1, 32))
+
+
+def test_cross_entropy_loss_host_checks():
+    import manifold_b200 as gfn
+    with pytest.raises(gfn.GfnError):
+        gfn.CrossEntropyLoss(label_smoothing=0.1)
+    with pytest.raises(gfn.GfnError):
+        gfn.CrossEntropyLoss(weight=torch.ones(3))
+    with pytest.raises(gfn.GfnError):  # no CPU path
+        gfn.cross_entropy(torch.zeros(2, 3), torch.zeros(2, dtype=torch.int64))
