@@ -772,7 +772,7 @@ def run_reference(args, c):
     return {"metric": "recurrent tokens/sec (prefill+decode)", "value": round(v, 1),
             "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(B * T / v * 1e3, 3), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "scaling": "strong" if c.get("strong") else "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic", "impl": "reference",
             "config": {"workload": c["workload"], "batch_per_gpu": c["B"]},
             "cpu_baseline": cb,
