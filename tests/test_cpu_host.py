@@ -109,3 +109,15 @@ def test_cross_entropy_loss_host_checks():
         gfn.CrossEntropyLoss(weight=torch.ones(3))
     with pytest.raises(gfn.GfnError):  # no CPU path
         gfn.cross_entropy(torch.zeros(2, 3), torch.zeros(2, dtype=torch.int64))
+
+
+def test_training_routing_by_head_dim():
+    # the fused BPTT kernels take head_dim <= 64; larger heads (and the generic
+    # configurations) train through the generic layer step
+    import manifold_b200 as gfn
+    small = gfn.Manifold(vocab_size=7, dim=64, depth=1, rank=8, heads=1, integrator_type="leapfrog")
+    big = gfn.Manifold(vocab_size=7, dim=256, depth=1, rank=8, heads=2, integrator_type="leapfrog")
+    heun = gfn.Manifold(vocab_size=7, dim=64, depth=1, rank=8, heads=2, integrator_type="heun")
+    assert not small.layers[0].training_generic()
+    assert big.layers[0].training_generic() and not big.layers[0].generic
+    assert heun.layers[0].training_generic() and heun.layers[0].generic
